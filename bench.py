@@ -1,0 +1,491 @@
+#!/usr/bin/env python
+"""Benchmark of the 4-bit quantized matmul hot path on B200 (driver contract: one JSON line from rank 0).
+
+Workload ("skinny-M decode / speculative-verify GEMV sweep"): K = 2048, M in {1, 2, 4, 8},
+N in {2048, 16384, 262144}; W ~ N(0, 0.02) packed to q4g32a.t64 on the device (the reference's packQ4); x ~ N(0, 1)
+fp16 values. N = 262144 is the vocabulary head and runs as the engine runs it (rms prologue, softcap epilogue with
+per-tile max/argmax, gemma4.js:503-509); the others run raw/store. M = 1 calls gemv (lops.js), M > 1 gemvM
+(lops_spec.js). One step = the 12 calls once. With N GPUs every call is column-split (each rank owns N/ranks rows,
+whole 64-row tiles) and the step ends with ONE all-gather of every rank's outputs (NCCL over NVLink).
+value = algorithmic bytes of the step (N*K*0.625 + M*K*4 + M*N*4 (+MX) per call) / device time (max over ranks).
+Inputs larger than L2: each small-N call cycles through a ring of weight copies totalling >= 2x the 126 MB L2.
+Secondary (same line, key "gemm"): config 3 / config 4 W4A16 GEMM TFLOP/s (rows split across ranks, no comm).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 2 ** 20
+K = 2048
+MS = (1, 2, 4, 8)
+NS = (2048, 16384, 262144)
+HEAD_N = 262144
+
+
+def gemv_bytes(M, N, K, head):
+    b = N * K * 0.625 + M * K * 4 + M * N * 4
+    if head:
+        b += M * (N // 64) * 8
+    return b
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ------------------------------------------------------------------------------------------ clocks sampler
+class Clocks:
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, index):
+        self.index, self.proc, self.lines = index, None, []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(2)
+            except Exception:
+                self.proc.kill()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------ distributed plumbing
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def init_dist(ws, local):
+    import torch
+    import torch.distributed as dist
+    if ws > 1 and not dist.is_initialized():
+        import datetime
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=datetime.timedelta(seconds=120))
+    return dist if ws > 1 else None
+
+
+# ------------------------------------------------------------------------------------------ our arm
+class Sweep:
+    """the config-2 sweep on this rank: weight rings, inputs, outputs, one step = 12 calls"""
+
+    def __init__(self, g, torch, ws, rank, seed=0):
+        import p0pc0rn_b200 as p0
+        self.p0, self.g, self.torch, self.ws, self.rank = p0, g, torch, ws, rank
+        dev = torch.device("cuda", torch.cuda.current_device())
+        gen = torch.Generator(device=dev)
+        self.calls = []
+        self.keep = []
+        out_floats = 0
+        for N in NS:
+            Nr = N // ws                                     # this rank's rows (whole tiles)
+            head = N == HEAD_N
+            wbytes = Nr * K * 5 // 8
+            copies = 1 if wbytes * 1 >= 2 * L2_BYTES else max(2, -(-2 * L2_BYTES // wbytes))
+            ring = []
+            for c in range(copies):
+                gen.manual_seed(seed * 1000003 + N * 31 + c * 7 + rank)
+                wf = torch.randn(Nr, K, generator=gen, device=dev, dtype=torch.float32) * 0.02
+                wb = g.wrap(wf.data_ptr(), wf.numel() * 4, "wf32")
+                q = p0.pack_q4(g, wb, Nr, K)
+                g.done()
+                g.free(wb)
+                del wf
+                ring.append(q)
+            for M in MS:
+                rng = np.random.default_rng(seed + 17 * M + N)
+                x = rng.standard_normal(M * K).astype(np.float16).astype(np.float32)
+                xb = g.upload(x, "x")
+                NT = Nr // 64
+                c = {"M": M, "N": Nr, "Nfull": N, "head": head, "ring": ring, "i": 0, "x": x, "xb": xb,
+                     "bytes": gemv_bytes(M, Nr, K, head), "out_off": out_floats}
+                c["y"] = g.buffer(M * Nr * 4, "y")
+                if head:
+                    nw = (1.0 + 0.1 * rng.standard_normal(K)).astype(np.float32)
+                    c["nw"] = g.upload(nw, "nw")
+                    mx = np.zeros(M * NT * 2 + 8, np.float32)
+                    c["mxb"] = g.upload(mx, "mx")
+                    c["st"] = g.upload(np.full(8, 0.9, np.float32), "st")
+                    c["stat_off"] = M * NT * 2              # the rstd slot past the tile slots (gemma4.js:504)
+                    g.write(c["mxb"], np.full(1, 0.9, np.float32), dst_off=c["stat_off"] * 4)
+                    out_floats += M * NT * 2
+                else:
+                    out_floats += M * Nr
+                self.calls.append(c)
+        self.out_floats = out_floats
+        self.step_bytes = sum(c["bytes"] for c in self.calls)
+
+    def args(self, c):
+        q = c["ring"][c["i"] % len(c["ring"])]
+        w = {"buf": q, "off": 0, "enc": "q4g32a.t64", "rows": c["N"], "cols": K}
+        a = {"w": w, "x": {"buf": c["xb"]}, "N": c["N"], "K": K, "y": {"buf": c["y"]}}
+        if c["head"]:
+            a.update(pro="rms", epi="softcap", cap=30.0, norm={"buf": c["nw"], "off": 0}, mx={"buf": c["mxb"]})
+            if c["M"] == 1:
+                a["stat"] = {"buf": c["mxb"], "off": c["stat_off"]}
+            else:
+                a["stat"] = {"buf": c["st"], "off": 0, "ld": 1}
+        if c["M"] > 1:
+            a["M"] = c["M"]
+        return a
+
+    def launch(self, c, ev=None):
+        a = self.args(c)
+        if ev is not None:
+            ev[0].record()
+        if c["M"] == 1:
+            self.p0.gemv(self.g, a)
+        else:
+            self.p0.gemvM(self.g, a)
+        if ev is not None:
+            ev[1].record()
+        c["i"] += 1
+
+    def step(self, head_events=None):
+        n = 0
+        for c in self.calls:
+            ev = None
+            if head_events is not None and c["head"]:
+                ev = (self.torch.cuda.Event(enable_timing=True), self.torch.cuda.Event(enable_timing=True))
+                head_events.append((c, ev))
+            self.launch(c, ev)
+            n += 1
+        return n
+
+
+def run_ours(args, ws, rank, local):
+    import torch
+    torch.cuda.set_device(local)
+    dist = init_dist(ws, local)
+    import p0pc0rn_b200 as p0
+    g = p0.Gpu(local)
+    stream = torch.cuda.current_stream()
+    g.set_stream(stream.cuda_stream)          # the library launches on torch's stream: events and NCCL order with it
+    sw = Sweep(g, torch, ws, rank)
+    torch.cuda.synchronize()
+    # one gather buffer: every call's outputs of this rank, concatenated; one all-gather per step
+    gather_src = torch.empty(sw.out_floats, dtype=torch.float32, device="cuda")
+    gather_dst = torch.empty(sw.out_floats * ws, dtype=torch.float32, device="cuda")
+    # device views of each call's output for the gather copy
+    outs = []
+    for c in sw.calls:
+        buf = c["mxb"] if c["head"] else c["y"]
+        n = c["M"] * (c["N"] // 64) * 2 if c["head"] else c["M"] * c["N"]
+        outs.append((c["out_off"], n, buf.ptr))
+
+    def gather():
+        """every call's outputs of this rank -> one buffer -> one NCCL all-gather (stream-ordered)"""
+        if dist is None:
+            return
+        for off, n, ptr in outs:
+            _memcpy_d2d(gather_src.data_ptr() + off * 4, ptr, n * 4, stream.cuda_stream)
+        dist.all_gather_into_tensor(gather_dst, gather_src)
+
+    launches_per_step = len(sw.calls)
+    for _ in range(args.warmup):
+        sw.step()
+        gather()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = Clocks(local)
+    clk.start()
+    head_events = []
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        sw.step(head_events)
+        gather()
+    t1.record()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    ms = t0.elapsed_time(t1)
+    if dist:
+        tt = torch.tensor([ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    head_ms = {}
+    for c, (a, b) in head_events:
+        head_ms.setdefault(c["M"], []).append(a.elapsed_time(b))
+    # ---- e2e: host inputs (pinned) -> device, the public API calls, results -> host, every step
+    e2e = run_e2e(args, sw, g, torch, dist, gather)
+    # ---- secondary: GEMM configs 3 and 4
+    gemm = run_gemm_secondary(args, g, torch, ws, rank, dist)
+    res = None
+    if rank == 0:
+        hbm, tfl, src = peaks()
+        total_bytes = sw.step_bytes * ws * args.steps
+        value = total_bytes / (ms / 1e3) / 1e9
+        # roofline of the dominant kernel: the vocabulary head GEMV, averaged over its launches in the timed region
+        per_m = {M: float(np.mean(v)) for M, v in head_ms.items()}
+        head_bytes = sum(c["bytes"] for c in sw.calls if c["head"])
+        head_time = sum(per_m.values()) / 1e3
+        achieved = head_bytes / head_time / 1e9
+        res = {
+            "metric": "W4 GEMV GB/s (config 2 sweep: M 1/2/4/8 x N 2048/16384/262144, K 2048)",
+            "value": round(value, 1), "unit": "GB/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "q4 weights, f32 x/accumulate", "data": "synthetic (seeded N(0,0.02) weights packed to q4g32a.t64 on device; N(0,1) fp16 x)",
+            "config": {"workload": "config2_gemv_sweep", "M": list(MS), "N": list(NS), "K": K, "parallelism": "column-split x%d + all-gather" % ws,
+                       "l2": "weight rings >= 2x L2 per small-N call; head 335 MB > L2", "bytes_per_step": sw.step_bytes * ws},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                         "traffic": None, "kernel": "gemv head (rms+softcap) N=%d/rank K=%d, M=1/2/4/8" % (HEAD_N // ws, K),
+                         "per_M_us": {str(k): round(v * 1e3, 2) for k, v in sorted(per_m.items())}, "peak_source": src},
+            "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clocks, "gemm": gemm,
+        }
+        res["cpu_baseline"] = cpu_baseline(args) if ws == 1 else None
+    if dist:
+        dist.barrier()
+    g.close()
+    return res
+
+
+_cudart = None
+
+
+def _memcpy_d2d(dst, src, nbytes, stream):
+    global _cudart
+    import ctypes
+    if _cudart is None:
+        import torch  # noqa: F401  (loads the CUDA runtime into the process)
+        for name in ("libcudart.so.12", "libcudart.so"):
+            try:
+                _cudart = ctypes.CDLL(name)
+                break
+            except OSError:
+                continue
+        _cudart.cudaMemcpyAsync.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
+    r = _cudart.cudaMemcpyAsync(ctypes.c_void_p(dst), ctypes.c_void_p(src), nbytes, 3, ctypes.c_void_p(stream))
+    if r != 0:
+        raise RuntimeError("cudaMemcpyAsync failed: %d" % r)
+
+
+def run_e2e(args, sw, g, torch, dist, gather):
+    """the same sweep through the public API with host buffers: x from pinned host memory -> device, the call,
+    results device -> pinned host, every step; wall-clock over the steps (max over ranks)"""
+    pin_in, pin_out = [], []
+    h2d = d2h = 0
+    for c in sw.calls:
+        t = torch.from_numpy(c["x"]).pin_memory()
+        pin_in.append(t)
+        h2d += t.numel() * 4
+        n = c["M"] * (c["N"] // 64) * 2 if c["head"] else c["M"] * c["N"]
+        o = torch.empty(n, dtype=torch.float32).pin_memory()
+        pin_out.append(o)
+        d2h += n * 4
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def step():
+        for c, t in zip(sw.calls, pin_in):
+            _memcpy_h2d(c["xb"].ptr, t.data_ptr(), t.numel() * 4, stream)
+            sw.launch(c)
+        gather()
+        for c, o in zip(sw.calls, pin_out):
+            src = c["mxb"].ptr if c["head"] else c["y"].ptr
+            _memcpy_d2h(o.data_ptr(), src, o.numel() * 4, stream)
+        torch.cuda.current_stream().synchronize()
+
+    steps = max(3, args.steps // 2)
+    for _ in range(3):
+        step()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = time.perf_counter() - t0
+    if dist:
+        tt = torch.tensor([dt], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        dt = float(tt.item())
+    ws = dist.get_world_size() if dist else 1
+    val = sw.step_bytes * ws * steps / dt / 1e9
+    return {"value": round(val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": round(dt / steps * 1e3, 4), "path": "p0pc0rn_b200.gemv/gemvM (ctypes -> libp0mm.so C ABI), pinned host x in, outputs out"}
+
+
+def _memcpy_h2d(dst, src, nbytes, stream):
+    _memcpy_kind(dst, src, nbytes, stream, 1)
+
+
+def _memcpy_d2h(dst, src, nbytes, stream):
+    _memcpy_kind(dst, src, nbytes, stream, 2)
+
+
+def _memcpy_kind(dst, src, nbytes, stream, kind):
+    global _cudart
+    import ctypes
+    if _cudart is None:
+        _memcpy_d2d(0, 0, 0, stream)
+    r = _cudart.cudaMemcpyAsync(ctypes.c_void_p(dst), ctypes.c_void_p(src), nbytes, kind, ctypes.c_void_p(stream))
+    if r != 0:
+        raise RuntimeError("cudaMemcpyAsync failed: %d" % r)
+
+
+# ------------------------------------------------------------------------------------------ GEMM (secondary)
+def run_gemm_secondary(args, g, torch, ws, rank, dist):
+    """configs 3 and 4 (bias epilogue; GELU-tanh fused on the MLP-up): TFLOP/s per shape, rows split across ranks"""
+    import p0pc0rn_b200 as p0
+    shapes = [("c3_qkv", 4096, 9216, 3072, False), ("c3_mlp_up", 4096, 12288, 3072, True), ("c3_down", 4096, 3072, 12288, False),
+              ("c4_qkv", 32760, 6720, 2240, False), ("c4_mlp_up", 32760, 8960, 2240, True), ("c4_down", 32760, 2240, 8960, False)]
+    out = {}
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev)
+    reps = 5
+    for name, M, N, Kk, gelu in shapes:
+        Mr = -(-M // ws)
+        m0 = min(M, rank * Mr)
+        Mr = max(0, min(M, m0 + Mr) - m0)
+        gen.manual_seed(hash(name) & 0xFFFF)
+        wf = torch.randn(N, Kk, generator=gen, device=dev) * 0.02
+        wb = g.wrap(wf.data_ptr(), wf.numel() * 4, "wf")
+        q = p0.pack_q4(g, wb, N, Kk)
+        g.done()
+        g.free(wb)
+        del wf
+        # two activation copies (each > L2 at config 4; config 3's X is 25 MB: L2-resident, as in a real DiT block)
+        xs = [torch.randn(max(Mr, 1), Kk, generator=gen, device=dev).half() for _ in range(2)]
+        bias = torch.randn(N, generator=gen, device=dev) * 0.01
+        y = torch.empty(max(Mr, 1), N, device=dev, dtype=torch.float16)
+        xbs = [g.wrap(x.data_ptr(), x.numel() * 2, "x") for x in xs]
+        bb = g.wrap(bias.data_ptr(), bias.numel() * 4, "bias")
+        yb = g.wrap(y.data_ptr(), y.numel() * 2, "y")
+        w = {"buf": q, "off": 0, "enc": "q4g32a.t64", "rows": N, "cols": Kk}
+
+        def call(i):
+            if Mr:
+                p0.gemm(g, {"w": w, "x": {"buf": xbs[i % 2]}, "M": Mr, "N": N, "K": Kk, "epi": "bias", "ev": {"buf": bb, "off": 0},
+                            "y": {"buf": yb}, "post_gelu": gelu})
+        for i in range(2):
+            call(i)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            call(i)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        if dist:
+            tt = torch.tensor([ms], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        out[name] = {"M": M, "N": N, "K": Kk, "ms": round(ms, 4), "tflops": round(2.0 * M * N * Kk / (ms / 1e3) / 1e12, 1)}
+        for b in xbs + [bb, yb, q]:
+            g.free(b)
+        del xs, bias, y
+    hbm, tfl, src = peaks()
+    tot_fl = sum(2.0 * v["M"] * v["N"] * v["K"] for v in out.values())
+    tot_ms = sum(v["ms"] for v in out.values())
+    agg = tot_fl / (tot_ms / 1e3) / 1e12
+    return {"metric": "W4A16 GEMM TFLOP/s (configs 3+4, bias epilogue, GELU-tanh on MLP-up)", "value": round(agg, 1), "unit": "TFLOP/s",
+            "frac_of_bf16_peak": round(agg / tfl, 4), "peak": tfl, "peak_source": src, "shapes": out,
+            "parallelism": "row-split x%d, no comm" % ws}
+
+
+# ------------------------------------------------------------------------------------------ CPU baseline / reference arm
+def cpu_baseline(args, budget_s=12.0):
+    """The reference's GEMV arithmetic on this host's cores: the oracle's C restatement of lgemv/lgemvM (OpenMP over
+    64-row tiles, all threads), on a bounded sample of the workload: the config-2 calls with N cut to a slice."""
+    from oracle import ref
+    thr = ref.max_threads()
+    rng = np.random.default_rng(1)
+    Ns = 8192
+    W = (rng.standard_normal(Ns * K) * 0.02).astype(np.float32)
+    b, _ = ref.pack_q4(W, Ns, K)
+    t_total, bytes_total, calls = 0.0, 0.0, 0
+    t_start = time.perf_counter()
+    while time.perf_counter() - t_start < budget_s:
+        for M in MS:
+            X = rng.standard_normal(M * K).astype(np.float32)
+            t0 = time.perf_counter()
+            ref.gemv_cpu_mt(b, X, M, Ns, K, thr)
+            t_total += time.perf_counter() - t0
+            bytes_total += gemv_bytes(M, Ns, K, False)
+            calls += 1
+    return {"value": round(bytes_total / t_total / 1e9, 3), "unit": "GB/s", "cores": thr, "kind": "port",
+            "sample": "config-2 GEMV calls M=1/2/4/8 at N=8192 rows, K=2048, repeated for ~%.0f s (%d calls)" % (budget_s, calls)}
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return None
+    cb = cpu_baseline(args, budget_s=max(5.0, min(60.0, 3.0 * args.steps)))
+    return {"impl": "reference", "metric": "W4 GEMV GB/s (config 2 sweep: M 1/2/4/8 x N 2048/16384/262144, K 2048)", "value": cb["value"],
+            "unit": "GB/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "q4 weights, f32 x/accumulate", "data": "synthetic",
+            "config": {"workload": "config2_gemv_sweep", "M": list(MS), "N": list(NS), "K": K},
+            "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference is JS + WebGPU (no CPU WebGPU adapter or JS engine on this box): its lgemv/lgemvM arithmetic "
+                    "restated in C (oracle/oracle.c) on the host cores"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        res = run_reference(args, ws, rank)
+    else:
+        res = run_ours(args, ws, rank, local)
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

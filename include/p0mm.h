@@ -1,0 +1,164 @@
+/*
+ * p0mm.h -- C ABI of the B200 (sm_100a) 4-bit quantized matmul library for p0pc0rn.
+ *
+ * This is the drop-in boundary for p0pc0rn's three matmul operators and the buffer calls they ride on.
+ * The reference binds these as JavaScript functions over WebGPU buffers; each entry point below names the
+ * reference interface it replaces (paths are inside the reference repository ArtistJoshHughes/p0pc0rn).
+ * Plain pointers and sizes only; every call returns a p0_status and never traps. A non-zero status is
+ * returned where the reference throws; p0_last_error() gives the message in the reference's wording.
+ *
+ * Units follow the reference: weight / x / y byte offsets where the reference uses bytes (ops/gemm.js:300-302),
+ * f32-element offsets where it uses elements (llm/lops.js:127-128: x.rowB, norm.off, stat.off, ev.off).
+ * All work is enqueued on the context's stream and is asynchronous; p0_read() and p0_done() synchronise.
+ */
+#ifndef P0MM_H
+#define P0MM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct p0_ctx p0_ctx;
+/* an opaque device allocation; id 0 means "no buffer" (an absent optional binding) */
+typedef struct { uint64_t id; } p0_buf;
+
+typedef enum {
+  P0_OK = 0,
+  P0_EINVAL = 1,    /* argument error: the reference throws `new Error(...)` */
+  P0_EALIGN = 2,    /* offset / stride alignment the kernels need */
+  P0_ENOMEM = 3,
+  P0_EDEVICE = 4,   /* CUDA error; the device may be lost (reference: GpuError / GPU_LOST, core/gpu.js:141-147) */
+  P0_ETIMEOUT = 5,  /* a bounded wait ran out (host poll or an in-kernel wait) */
+  P0_ECOMM = 6
+} p0_status;
+
+/* weight encodings: engine/kcheck.js:22-53 (q4g32a.t64: 1280 B per 64-row x 32-k record; q8g64s.t64: 4224 B per
+ * 64-row x 64-k record); 'f16' = row-major fp16 with a row stride */
+enum { P0_ENC_Q4G32A_T64 = 1, P0_ENC_Q8G64S_T64 = 2, P0_ENC_F16 = 3 };
+
+/* ---------------------------------------------------------------------------------------------- device context */
+/* createGpu (engine/core/gpu.js:18-23): one context per device; owns a CUDA stream and every buffer */
+p0_status p0_init(int device, p0_ctx **out);
+/* Gpu.freeAll + device.destroy (gpu.js) */
+p0_status p0_destroy(p0_ctx *ctx);
+/* run subsequent work on an external cudaStream_t (NULL = the context's own stream) */
+p0_status p0_set_stream(p0_ctx *ctx, void *cuda_stream);
+/* the message of the last failed call, in the reference's wording (e.g. "gemv: N % 64") */
+p0_status p0_last_error(p0_ctx *ctx, char *msg, size_t cap);
+/* byte accounting (gpu.js:28, 81-96) and dispatch counter (Runner, gpu.js:177-179) */
+p0_status p0_stats(p0_ctx *ctx, uint64_t *alive_bytes, uint64_t *peak_bytes, uint64_t *dispatches);
+
+/* ---------------------------------------------------------------------------------------------- buffers */
+/* Gpu.buffer(bytes, label) (gpu.js:81-96): device allocation rounded up to 16 B, zero-filled, accounted */
+p0_status p0_buffer(p0_ctx *ctx, size_t bytes, const char *label, p0_buf *out);
+/* register caller-owned device memory (e.g. a torch tensor) as a buffer; p0_free() only unregisters it */
+p0_status p0_wrap(p0_ctx *ctx, void *device_ptr, size_t bytes, const char *label, p0_buf *out);
+/* Gpu.upload / queue.writeBuffer (gpu.js:98-117): host -> device, ordered on the stream */
+p0_status p0_upload(p0_ctx *ctx, p0_buf buf, size_t dst_off, const void *src, size_t n);
+/* Gpu.read(buf, off, n) -> Gpu._readback (gpu.js:118-140): flushes the stream, then device -> host */
+p0_status p0_read(p0_ctx *ctx, p0_buf buf, size_t off, size_t n, void *dst);
+/* Gpu.free (gpu.js:89-94) */
+p0_status p0_free(p0_ctx *ctx, p0_buf buf);
+/* Gpu.done (gpu.js:141-147): wait for the stream with a bound; reports in-kernel wait timeouts */
+p0_status p0_done(p0_ctx *ctx, uint32_t timeout_ms);
+/* the device address of a buffer (for NCCL / interop); the address is valid until p0_free */
+p0_status p0_device_ptr(p0_ctx *ctx, p0_buf buf, uint64_t *out);
+
+/* a weight tensor view: WeightStore h.t(name) -> {buf, off (bytes), bytes, enc, rows, cols} (core/store.js:249-253) */
+typedef struct {
+  p0_buf buf;
+  uint64_t off;    /* bytes */
+  uint64_t bytes;  /* 0 = to the end of the buffer */
+  uint32_t enc;    /* P0_ENC_* */
+  uint32_t rows;   /* Nw */
+  uint32_t cols;   /* Ktot (for f16: also the row stride in halves unless ld is set) */
+  uint32_t ld;     /* f16 only: row stride in halves (0 = cols) */
+} p0_wview;
+
+/* ---------------------------------------------------------------------------------------------- GEMV */
+enum { P0_PRO_RAW = 0, P0_PRO_RMS = 1, P0_PRO_SUM = 2, P0_PRO_PLEG = 3 };
+enum { P0_EPI_STORE = 0, P0_EPI_GEGLU = 1, P0_EPI_SOFTCAP = 2 };
+
+/* gemv(g, a) -> nsplit (engine/llm/lops.js:108-141): y = x W^T for one token.
+ * Fields mirror `a`: w; x {buf, rowB}; N; K; kPer (0 = none); pro; epi; y {buf}; ldy (0 = N); stat {buf, off}
+ * (rms rstd slot; bound as in lops.js:125: the mx buffer when epi is softcap); norm {buf, off}; ev {buf, off};
+ * src {n, ld} (sum / pleg partials); mx {buf}; cap (0 = 30). Output contract: store -> Y[split*ldy + n];
+ * geglu -> Y[n] = gelu(gate n) * up n (W rows [gate 0..N) | up N..2N)); softcap -> Y[n] and MX[tile*2] =
+ * {max, bitcast idx} per 64-row tile, ties to the lowest index. */
+typedef struct {
+  p0_wview w;
+  p0_buf x;    uint32_t x_rowB;
+  uint32_t N, K, kPer;
+  uint32_t pro, epi;
+  p0_buf y;    uint32_t ldy;
+  p0_buf stat; uint32_t stat_off;
+  p0_buf norm; uint32_t norm_off;
+  p0_buf ev;   uint32_t ev_off;
+  uint32_t src_n, src_ld;
+  p0_buf mx;
+  float cap;
+} p0_gemv_args;
+p0_status p0_gemv(p0_ctx *ctx, const p0_gemv_args *a, uint32_t *nsplit);
+
+/* gemvM(g, a) -> nsplit (engine/llm/lops_spec.js:159-191): M <= 8 rows at once, each weight record read once.
+ * Adds x.ldx (0 = K), y.ldm (0 = N) and y.ldy (0 = M*ldm), stat.ld (0 = 2), ev.ld. Prologues raw | rms | pleg.
+ * store -> Y[split*ldy + m*ldm + n]; softcap -> MX[(m*ntile + tile)*2], ntile = N/64. */
+typedef struct {
+  p0_wview w;
+  p0_buf x;    uint32_t x_rowB, x_ldx;
+  uint32_t M, N, K, kPer;
+  uint32_t pro, epi;
+  p0_buf y;    uint32_t ldy, ldm;
+  p0_buf stat; uint32_t stat_off, stat_ld;
+  p0_buf norm; uint32_t norm_off;
+  p0_buf ev;   uint32_t ev_off, ev_ld;
+  uint32_t src_n, src_ld;
+  p0_buf mx;
+  float cap;
+} p0_gemvM_args;
+p0_status p0_gemvM(p0_ctx *ctx, const p0_gemvM_args *a, uint32_t *nsplit);
+
+/* ---------------------------------------------------------------------------------------------- GEMM */
+enum { P0_GEPI_F16 = 0, P0_GEPI_F32 = 1, P0_GEPI_BIAS = 2, P0_GEPI_RESADD = 3, P0_GEPI_SWIGLU = 4 };
+enum { P0_ACT_SILU = 0, P0_ACT_GELU = 1 };
+
+/* gemm(gpu, a) -> flops (engine/ops/gemm.js:255-322): Y[m, n] = sum_k X[m, k] * W[n, k], W dequantised in-kernel
+ * to fp16 (q4: f16(q*s + mn), gemm.js:147-148), fp32 accumulation on the tensor cores. x prologue 'f16'.
+ * Fields mirror `a`: w; x {buf, off (bytes), ld (halves, 0 = K), k0}; M, N, K; wr0, wr1, wk0; epi; act;
+ * y {buf, off (bytes), ld (0 = N), n0}; ev {buf, off (floats)} (bias vector for 'bias', gate for 'resadd');
+ * bv {buf, off (floats), up} (resadd / swiglu bias); res; store.
+ * post_gelu (bias epilogue only) applies engine/ops/misc.js ew op 'gelu' to the fp16 result in the same pass:
+ * the pair gemm(epi:'bias') -> ew(op:'gelu') of pocketflux-engine.js:3052-3053 as one call.
+ * acc: 0 = 'f32' (the only mode the tensor-core path computes; 'f16' partial sums are rejected). */
+typedef struct {
+  p0_wview w;
+  p0_buf x;  uint64_t x_off; uint32_t x_ld, x_k0;
+  uint32_t M, N, K;
+  uint32_t wr0, wr1, wk0;
+  uint32_t epi, act, acc;
+  p0_buf y;  uint64_t y_off; uint32_t y_ld, y_n0;
+  p0_buf ev; uint32_t ev_off;
+  p0_buf bv; uint32_t bv_off, bv_up;
+  uint32_t res, store, post_gelu;
+} p0_gemm_args;
+p0_status p0_gemm(p0_ctx *ctx, const p0_gemm_args *a, double *flops);
+
+/* ---------------------------------------------------------------------------------------------- quantiser */
+/* packQ4 (engine/kcheck.js:22-38) on the device, bit for bit: W f32 [N][ldw] at w_off (bytes) -> q4g32a.t64 records
+ * (N*K*5/8 bytes) at out_off. N % 64 == 0, K % 32 == 0. The dequantised value of code q is q*s + mn. */
+p0_status p0_pack_q4(p0_ctx *ctx, p0_buf w, uint64_t w_off, uint32_t ldw, uint32_t N, uint32_t K, p0_buf out, uint64_t out_off);
+
+/* ---------------------------------------------------------------------------------------------- testing aids */
+/* writes the fp16 weight the GEMM tile holds for rows [0, rows) x k [0, cols) of a q4/q8 view, row-major,
+ * into out_f16 (a buffer of rows*cols*2 bytes): the in-kernel dequantisation, dumped for bit-exact checks */
+p0_status p0_dequant_f16(p0_ctx *ctx, const p0_wview *w, p0_buf out_f16);
+/* the library build tag (kernel versions), e.g. "p0mm sm_100a gemv-v1 gemm-tc-v1" */
+const char *p0_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* P0MM_H */

@@ -1,0 +1,423 @@
+// gemm.cu -- the dequant-fused W4A16 GEMM on sm_100a tensor cores: gemm(gpu, a) of engine/ops/gemm.js:255-322 for
+// q4g32a.t64 weights and the 'f16' x prologue, epilogues f16 / f32 / bias (+res, + the ew gelu that follows it) /
+// resadd / swiglu (gemm.js:187-211).
+//
+// Y[m, n] = sum_k X[m, k] * Wdq[n, k], Wdq[n, k] = f16(q * s + mn) (gemm.js:147-148), fp32 accumulation.
+//
+// A CTA owns 128 weight rows x BT tokens (BT = 64 / 128 / 256) and walks K in 64-wide stages:
+//   warp 0      TMA producer: X tile [BT x 64] fp16 -> shared memory ring (128-byte swizzle), no multicast
+//   warp 1      TMEM allocator and the single MMA-issuing thread: tcgen05.mma kind::f16, M = 128 weight rows,
+//               N = BT tokens, K = 16, A (the dequantised weights) read from tensor memory, B (X) from shared
+//               memory, D (fp32) in tensor memory
+//   warps 2..9  dequantisers: thread = one weight row (its TMEM lane), half = one 32-k group of the stage; each
+//               loads its row's 16 code bytes and (s, mn) word straight from the packed record (128-bit loads,
+//               coalesced 512 B per warp), computes f16(fmaf(q, s, mn)) exactly and stores the 16 packed
+//               columns with tcgen05.st: weights never touch shared memory. After the last stage the same warps
+//               are the epilogue: tcgen05.ld -> bias / activation -> shared staging -> coalesced vector stores.
+// Orientation: D = Wdq . X^T, so TMEM lane = output column n and TMEM column = token m.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include "internal.h"
+#include "tc.cuh"
+
+namespace {
+
+constexpr int kBW = 128;        // weight rows per CTA (TMEM lanes, MMA M)
+constexpr int kBK = 64;         // k per stage
+constexpr int kStages = 4;
+constexpr int kDqWarps = 8;     // warps 2..9
+constexpr int kThreads = 32 * (2 + kDqWarps);
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAcol = 256; // first TMEM column of the weight (A) stages; the accumulator holds columns [0, BT)
+constexpr uint32_t kMaxBT = 256;
+constexpr size_t kRingBytes = (size_t)kStages * kMaxBT * kBK * 2;   // 128 KB; also the epilogue staging area
+
+struct GemmParams {
+  const uint8_t *W;   // weight view base
+  uint8_t *Y;         // y buffer + y.off
+  const float *EV, *BV;
+  uint32_t M, N, K, wR0, wR1, wG, wk0, Nw, ldy, ny0, evOff, bvOff, bvUp;
+  int epi, act, res, store, gate, bias, post_gelu;
+  uint32_t BT, nk;
+  uint32_t *err;
+};
+
+// f16(fmaf(q, s, mn)) for the two codes of one byte (low nibble = even k), packed low/high: the GEMM's weight value
+// (gemm.js:147-148 computes cv*sc + mn in f32 and converts to f16; q*s is exact in f32, so one fma is the same f32)
+__device__ __forceinline__ uint32_t deq_pair(uint32_t byte, float s, float mn) {
+  const float lo = __uint_as_float(0x4B000000u | (byte & 15u)) - 8388608.0f;
+  const float hi = __uint_as_float(0x4B000000u | ((byte >> 4) & 15u)) - 8388608.0f;
+  __half2 h = __floats2half2_rn(fmaf(lo, s, mn), fmaf(hi, s, mn));
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+__device__ __forceinline__ void deq_row16(const uint4 c, uint32_t sm, uint32_t (&r)[16]) {
+  const float s = __half2float(__ushort_as_half((unsigned short)(sm & 0xffffu)));
+  const float mn = __half2float(__ushort_as_half((unsigned short)(sm >> 16)));
+  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int b = 0; b < 4; b++) r[i * 4 + b] = deq_pair((w[i] >> (8 * b)) & 0xffu, s, mn);
+}
+
+__device__ __forceinline__ uint4 ldg_w(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t ldg_w32(const void *p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+// activations in the reference's source order (no contraction)
+__device__ __forceinline__ float gelu_g(float g) {   // gemm.js:204
+  float u = __fmul_rn(0.7978845608f, __fadd_rn(g, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, g), g), g)));
+  u = fminf(15.0f, fmaxf(-15.0f, u));
+  return __fmul_rn(__fmul_rn(g, 0.5f), __fadd_rn(1.0f, tanhf(u)));
+}
+__device__ __forceinline__ float gelu_m(float x) {   // ops/misc.js:116
+  float u = __fmul_rn(0.7978845608f, __fadd_rn(x, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x)));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(fminf(15.0f, fmaxf(-15.0f, u)))));
+}
+__device__ __forceinline__ float silu_g(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
+
+__device__ __forceinline__ uint32_t weight_row(const GemmParams &p, uint32_t nB, uint32_t cc) {
+  uint32_t r = p.epi == P0_GEPI_SWIGLU ? ((cc & 1u) == 0u ? p.wR0 : p.wR1) + ((nB + cc) >> 1) : p.wR0 + nB + cc;
+  return r < p.Nw - 1 ? r : p.Nw - 1;   // gemm.js:96 clamps to the last row
+}
+
+__global__ void __launch_bounds__(kThreads, 1) gemm_q4_tc(const __grid_constant__ CUtensorMap tmx, const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t *xring = smem;
+  uint64_t *full_x = (uint64_t *)(smem + kRingBytes);
+  uint64_t *full_a = full_x + kStages;
+  uint64_t *empty = full_a + kStages;
+  uint64_t *accf = empty + kStages;
+  uint32_t *tmem_slot = (uint32_t *)(accf + 1);
+  volatile uint32_t *abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t BT = p.BT, nk = p.nk, nB = blockIdx.x * kBW, m0 = blockIdx.y * BT;
+  const uint32_t stage_bytes = BT * kBK * 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; s++) {
+      tc::mbar_init(&full_x[s], 1);
+      tc::mbar_init(&full_a[s], kDqWarps);
+      tc::mbar_init(&empty[s], 1);
+    }
+    tc::mbar_init(accf, 1);
+    *abort_flag = 0u;
+    tc::fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tc::prefetch_tmap(&tmx);
+      uint32_t issued = 0;
+      for (uint32_t s = 0; s < nk; s++) {
+        const uint32_t slot = s % kStages, ph = (s / kStages) & 1u;
+        if (!tc::mbar_wait(&empty[slot], ph ^ 1u, abort_flag, p.err, 0x101u, P0_SPIN_LIMIT)) break;
+        tc::mbar_expect_tx(&full_x[slot], stage_bytes);
+        tc::tma_load_2d(xring + (size_t)slot * stage_bytes, &tmx, &full_x[slot], (int32_t)(s * kBK), (int32_t)m0);
+        issued++;
+      }
+      // every issued copy has landed before the CTA can exit (bounded; no abort short-cut: copies always finish)
+      volatile uint32_t never = 0;
+      for (uint32_t s = issued > (uint32_t)kStages ? issued - kStages : 0; s < issued; s++)
+        tc::mbar_wait(&full_x[s % kStages], (s / kStages) & 1u, &never, p.err, 0x102u, P0_SPIN_LIMIT);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_f16_f32(kBW, BT);
+      for (uint32_t s = 0; s < nk; s++) {
+        const uint32_t slot = s % kStages, ph = (s / kStages) & 1u;
+        if (!tc::mbar_wait(&full_x[slot], ph, abort_flag, p.err, 0x201u, P0_SPIN_LIMIT)) break;
+        if (!tc::mbar_wait(&full_a[slot], ph, abort_flag, p.err, 0x202u, P0_SPIN_LIMIT)) break;
+        tc::fence_after();
+        const uint32_t xs = tc::smem_u32(xring + (size_t)slot * stage_bytes);
+#pragma unroll
+        for (uint32_t kk = 0; kk < kBK / 16; kk++)
+          tc::mma_ts_f16(tmem, tmem + kAcol + slot * 32u + kk * 8u, tc::desc_sw128(xs + kk * 32u), idesc, (s | kk) != 0u);
+        tc::mma_commit(&empty[slot]);
+      }
+      tc::mma_commit(accf);
+      // the accumulator is complete (or the loop gave up) before TMEM can be released
+      volatile uint32_t never = 0;
+      tc::mbar_wait(accf, 0, &never, p.err, 0x203u, P0_SPIN_LIMIT);
+    }
+  } else {
+    // ---------------------------------------------------------------- dequantisers, then the epilogue
+    const uint32_t q = (uint32_t)warp & 3u, h = (uint32_t)(warp - 2) >> 2;
+    const uint32_t nl = q * 32u + lane;               // this thread's TMEM lane = weight row of the tile
+    const uint32_t row = weight_row(p, nB, nl);
+    const uint8_t *rowrec = p.W + (size_t)(row >> 6) * p.wG * 1280u;
+    const uint32_t rr = row & 63u;
+    const uint32_t tq = tmem + ((q * 32u) << 16);
+    const uint32_t g0 = p.wk0 / 32u;
+    bool ok = true;
+    uint4 cn = make_uint4(0, 0, 0, 0);
+    uint32_t smn = 0;
+    auto fetch = [&](uint32_t s, uint4 &c, uint32_t &sm) {
+      if (s < nk && s * kBK + h * 32u < p.K) {
+        const uint8_t *rec = rowrec + (size_t)(g0 + s * 2u + h) * 1280u;
+        c = ldg_w(rec + rr * 16u);
+        sm = ldg_w32(rec + 1024u + rr * 4u);
+      } else {
+        c = make_uint4(0, 0, 0, 0);   // k beyond K: zero weights (X is zero-filled there as well)
+        sm = 0;
+      }
+    };
+    fetch(0, cn, smn);
+    for (uint32_t s = 0; s < nk; s++) {
+      const uint32_t slot = s % kStages, ph = (s / kStages) & 1u;
+      const uint4 c = cn;
+      const uint32_t sm = smn;
+      fetch(s + 1, cn, smn);   // one stage of loads in flight ahead
+      uint32_t r[16];
+      deq_row16(c, sm, r);
+      const bool got = tc::mbar_wait(&empty[slot], ph ^ 1u, abort_flag, p.err, 0x301u, P0_SPIN_LIMIT);
+      if (!__all_sync(0xffffffffu, got)) { ok = false; break; }   // warp-uniform: tcgen05.st is .sync.aligned
+      tc::tmem_st16(tq + kAcol + slot * 32u + h * 16u, r);
+      tc::tmem_wait_st();
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&full_a[slot]);
+    }
+    // ---- epilogue. Every epilogue thread passes both named barriers whatever happened (the loops above are
+    // bounded), and the work between them is skipped warp-uniformly after a failed wait.
+    asm volatile("bar.sync 1, %0;" ::"n"(kDqWarps * 32) : "memory");
+    bool go = ok && !*abort_flag;
+    if (go) go = tc::mbar_wait(accf, 0, abort_flag, p.err, 0x401u, P0_SPIN_LIMIT);
+    go = __all_sync(0xffffffffu, go);
+    float *stg = reinterpret_cast<float *>(xring);   // [BT][128] f32 (swiglu: [BT][64])
+    const bool swi = p.epi == P0_GEPI_SWIGLU;
+    if (go) {
+      tc::fence_after();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      const uint32_t n = nB + nl;
+      float pre_a = 1.0f, pre_b = 0.0f, gB = 0.0f, uB = 0.0f;   // per-row epilogue constants
+      if (p.epi == P0_GEPI_BIAS) pre_b = n < p.N ? p.EV[p.evOff + n] : 0.0f;
+      if (p.epi == P0_GEPI_RESADD && n < p.N) {
+        pre_a = p.gate ? p.EV[p.evOff + n] : 1.0f;
+        pre_b = p.bias ? p.BV[p.bvOff + n] : 0.0f;
+      }
+      if (swi && p.bias && nB + (nl & ~1u) < p.N) {
+        const uint32_t o = (nB >> 1) + (nl >> 1);
+        gB = p.BV[p.bvOff + o];
+        uB = p.BV[p.bvOff + p.bvUp + o];
+      }
+      for (uint32_t c0 = h * (BT / 2); c0 < (h + 1) * (BT / 2); c0 += 32) {
+        uint32_t r[32];
+        tc::tmem_ld32(tq + c0, r);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          const float v = __uint_as_float(r[j]);
+          const uint32_t ml = c0 + j;
+          if (swi) {
+            const float u = __shfl_down_sync(0xffffffffu, v, 1);
+            if ((lane & 1) == 0) {
+              const float g = __fadd_rn(v, gB), uu = __fadd_rn(u, uB);
+              const float a = p.act == P0_ACT_GELU ? gelu_g(g) : silu_g(g);
+              stg[ml * 64u + (nl >> 1)] = __fmul_rn(a, uu);
+            }
+          } else if (p.epi == P0_GEPI_BIAS) {
+            stg[ml * 128u + nl] = __fadd_rn(v, pre_b);
+          } else if (p.epi == P0_GEPI_RESADD) {
+            stg[ml * 128u + nl] = __fmul_rn(pre_a, __fadd_rn(v, pre_b));
+          } else {
+            stg[ml * 128u + nl] = v;
+          }
+        }
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kDqWarps * 32) : "memory");
+    if (go && !*abort_flag) {
+      // coalesced stores: 4 consecutive columns per thread per step (the reference's vec4 granularity)
+      const uint32_t OC = swi ? 64u : 128u, q4 = OC / 4u, nOut0 = swi ? (nB >> 1) : nB;
+      const uint32_t tid = threadIdx.x - 64u;
+      const bool f32y = p.epi == P0_GEPI_F32 || p.epi == P0_GEPI_RESADD;
+      for (uint32_t idx = tid; idx < BT * q4; idx += kDqWarps * 32u) {
+        const uint32_t ml = idx / q4, cq = idx - ml * q4, m = m0 + ml;
+        const uint32_t colw = swi ? nB + cq * 8u : nB + cq * 4u;   // the ws column the vec4 starts at
+        if (m >= p.M || colw >= p.N) continue;
+        const float4 t = *reinterpret_cast<const float4 *>(stg + ml * OC + cq * 4u);
+        const size_t e = (size_t)m * p.ldy + p.ny0 + nOut0 + cq * 4u;
+        if (f32y) {
+          float4 *yp = reinterpret_cast<float4 *>(p.Y + e * 4);
+          float4 o = t;
+          if (p.epi == P0_GEPI_RESADD && !p.store) {
+            const float4 y0 = *yp;
+            o = make_float4(__fadd_rn(y0.x, t.x), __fadd_rn(y0.y, t.y), __fadd_rn(y0.z, t.z), __fadd_rn(y0.w, t.w));
+          }
+          *yp = o;
+        } else {
+          uint2 *yp = reinterpret_cast<uint2 *>(p.Y + e * 2);
+          float v[4] = {t.x, t.y, t.z, t.w};
+          if (p.epi == P0_GEPI_BIAS && p.res) {
+            const uint2 y0 = *yp;
+            const __half2 a = *reinterpret_cast<const __half2 *>(&y0.x), b = *reinterpret_cast<const __half2 *>(&y0.y);
+            v[0] = __fadd_rn(v[0], __low2float(a));
+            v[1] = __fadd_rn(v[1], __high2float(a));
+            v[2] = __fadd_rn(v[2], __low2float(b));
+            v[3] = __fadd_rn(v[3], __high2float(b));
+          }
+          __half hv[4];
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            hv[i] = __float2half_rn(v[i]);
+            if (p.epi == P0_GEPI_BIAS && p.post_gelu) hv[i] = __float2half_rn(gelu_m(__half2float(hv[i])));
+          }
+          uint2 o;
+          o.x = (uint32_t)__half_as_ushort(hv[0]) | ((uint32_t)__half_as_ushort(hv[1]) << 16);
+          o.y = (uint32_t)__half_as_ushort(hv[2]) | ((uint32_t)__half_as_ushort(hv[3]) << 16);
+          *yp = o;
+        }
+      }
+    }
+  }
+  // ---------------------------------------------------------------- teardown
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// the dequantiser of the GEMM, dumped: out[row][k] = f16(q*s + mn) for a q4 view (bit-exactness checks)
+__global__ void deq_dump_q4(const uint8_t *W, uint32_t rows, uint32_t cols, uint32_t wG, uint16_t *out) {
+  const uint32_t G = cols / 32;
+  const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (uint64_t)rows * G) return;
+  const uint32_t row = (uint32_t)(idx / G), g = (uint32_t)(idx % G);
+  const uint8_t *rec = W + ((size_t)(row >> 6) * wG + g) * 1280u;
+  const uint4 c = *reinterpret_cast<const uint4 *>(rec + (row & 63u) * 16u);
+  const uint32_t sm = *reinterpret_cast<const uint32_t *>(rec + 1024u + (row & 63u) * 4u);
+  uint32_t r[16];
+  deq_row16(c, sm, r);
+  uint32_t *o = reinterpret_cast<uint32_t *>(out + (size_t)row * cols + (size_t)g * 32u);
+#pragma unroll
+  for (int i = 0; i < 16; i++) o[i] = r[i];
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)f;
+  }
+  return fn;
+}
+
+const char *gepi_name(uint32_t e) {
+  static const char *n[] = {"f16", "f32", "bias", "resadd", "swiglu"};
+  return e < 5 ? n[e] : "?";
+}
+
+}  // namespace
+
+extern "C" {
+
+// gemm(gpu, a) (gemm.js:264-322): the reference's checks first, then the kernel's own layout needs
+p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
+  if (!c || !a) return P0_EINVAL;
+  const char *op = "gemm";
+  const uint32_t enc = a->w.enc;
+  if (enc != P0_ENC_Q4G32A_T64 && enc != P0_ENC_Q8G64S_T64 && enc != P0_ENC_F16)
+    return p0_fail(c, P0_EINVAL, "gemm: unsupported weight encoding %u", enc);
+  if (enc != P0_ENC_Q4G32A_T64) return p0_fail(c, P0_EINVAL, "gemm: weight encoding %s is not built in this library yet", enc == 2 ? "q8g64s.t64" : "f16");
+  const uint32_t M = a->M, N = a->N, K = a->K;
+  if (K % 32) return p0_fail(c, P0_EINVAL, "gemm: K must be a multiple of 32");
+  if (a->epi > P0_GEPI_SWIGLU) return p0_fail(c, P0_EINVAL, "gemm: epilogue %u is not built in this library yet", a->epi);
+  if (a->acc != 0) return p0_fail(c, P0_EINVAL, "gemm: acc 'f16' (fp16 partial sums) is not built; the tensor cores accumulate in f32");
+  if (a->post_gelu && a->epi != P0_GEPI_BIAS) return p0_fail(c, P0_EINVAL, "gemm: post_gelu applies to the 'bias' epilogue only");
+  if (!M || !N || !K) return P0_OK;
+  if (a->w.rows == 0 || a->w.cols % 32 || a->wk0 % 32 || a->wk0 + K > a->w.cols)
+    return p0_fail(c, P0_EINVAL, "gemm: weight view %ux%u does not cover k [%u, %u) in whole 32-k groups", a->w.rows, a->w.cols, a->wk0, a->wk0 + K);
+  if (a->w.rows % 64) return p0_fail(c, P0_EINVAL, "gemm: q4g32a.t64 rows must be a multiple of 64");
+  if (N % 4) return p0_fail(c, P0_EALIGN, "gemm: N must be a multiple of 4 (the reference stores whole vec4s)");
+  const uint32_t ldx = a->x_ld ? a->x_ld : K, ldy = a->y_ld ? a->y_ld : N, wG = a->w.cols / 32;
+  const bool swi = a->epi == P0_GEPI_SWIGLU, f32y = a->epi == P0_GEPI_F32 || a->epi == P0_GEPI_RESADD;
+  const uint32_t es = f32y ? 4 : 2, ncols_out = swi ? N / 2 : N;
+  if (ldx % 8 || (a->x_off + 2ull * a->x_k0) % 16)
+    return p0_fail(c, P0_EALIGN, "gemm: x rows must start on 16-byte boundaries (ld %% 8, off + 2*k0 %% 16)");
+  if (ldy % 4 || a->y_n0 % 4 || a->y_off % (4 * es)) return p0_fail(c, P0_EALIGN, "gemm: y must be vec4-aligned (ld %% 4, n0 %% 4, off)");
+  p0_status st;
+  P0Range rw, rx, ry, re, rb;
+  if ((st = p0_range(c, a->w.buf, a->w.off, (uint64_t)(a->w.rows / 64) * wG * 1280u, op, "W", &rw))) return st;
+  if ((uintptr_t)rw.base % 16) return p0_fail(c, P0_EALIGN, "gemm: weight offset must be 16-byte aligned");
+  if ((st = p0_range(c, a->x, a->x_off, ((uint64_t)(M - 1) * ldx + a->x_k0 + K) * 2, op, "X", &rx))) return st;
+  if ((st = p0_range(c, a->y, a->y_off, ((uint64_t)(M - 1) * ldy + a->y_n0 + ncols_out) * es, op, "Y", &ry))) return st;
+  const bool need_ev = a->epi == P0_GEPI_BIAS || (a->epi == P0_GEPI_RESADD && a->ev.id);
+  if (need_ev && (st = p0_range(c, a->ev, 0, ((uint64_t)a->ev_off + N) * 4, op, "EV", &re))) return st;
+  const bool bias = a->bv.id != 0 && (a->epi == P0_GEPI_RESADD || swi);
+  if (bias && (st = p0_range(c, a->bv, 0, ((uint64_t)a->bv_off + (swi ? a->bv_up + N / 2 : N)) * 4, op, "BV", &rb))) return st;
+  if (swi && (a->wr0 + N / 2 > a->w.rows || a->wr1 + N / 2 > a->w.rows)) return p0_fail(c, P0_EINVAL, "gemm: swiglu rows beyond the weight");
+
+  const uint32_t BT = M <= 64 ? 64u : M <= 128 ? 128u : 256u;
+  auto enc_fn = tensor_map_encoder();
+  if (!enc_fn) return p0_fail(c, P0_EDEVICE, "gemm: cuTensorMapEncodeTiled is unavailable");
+  CUtensorMap tm;
+  cuuint64_t dims[2] = {K, M};
+  cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, BT};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult cr = enc_fn(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)(rx.base + 2ull * a->x_k0), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return p0_fail(c, P0_EDEVICE, "gemm: tensor map encode failed (%d)", (int)cr);
+
+  GemmParams p{};
+  p.W = rw.base; p.Y = (uint8_t *)ry.base; p.EV = (const float *)re.base; p.BV = (const float *)rb.base;
+  p.M = M; p.N = N; p.K = K; p.wR0 = a->wr0; p.wR1 = a->wr1; p.wG = wG; p.wk0 = a->wk0; p.Nw = a->w.rows;
+  p.ldy = ldy; p.ny0 = a->y_n0; p.evOff = a->ev_off; p.bvOff = a->bv_off; p.bvUp = a->bv_up;
+  p.epi = (int)a->epi; p.act = (int)a->act; p.res = (int)a->res; p.store = (int)a->store; p.gate = a->ev.id != 0;
+  p.bias = bias; p.post_gelu = (int)a->post_gelu;
+  p.BT = BT; p.nk = (K + kBK - 1) / kBK; p.err = c->d_err;
+  const size_t smem = kRingBytes + 1024 + 256;
+  cudaSetDevice(c->device);
+  cudaFuncSetAttribute(gemm_q4_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
+  gemm_q4_tc<<<grid, kThreads, smem, c->stream>>>(tm, p);
+  if ((st = p0_launched(c, "gemm"))) return st;
+  if (flops) *flops = 2.0 * M * N * K;
+  (void)gepi_name;
+  return P0_OK;
+}
+
+p0_status p0_dequant_f16(p0_ctx *c, const p0_wview *w, p0_buf out) {
+  if (!c || !w) return P0_EINVAL;
+  if (w->enc != P0_ENC_Q4G32A_T64) return p0_fail(c, P0_EINVAL, "dequant: encoding %u is not built in this library yet", w->enc);
+  if (w->rows % 64 || w->cols % 32) return p0_fail(c, P0_EINVAL, "dequant: q4g32a.t64 needs rows %% 64 and cols %% 32");
+  p0_status st;
+  P0Range rw, ro;
+  const uint32_t wG = w->cols / 32;
+  if ((st = p0_range(c, w->buf, w->off, (uint64_t)(w->rows / 64) * wG * 1280u, "dequant", "W", &rw))) return st;
+  if ((uintptr_t)rw.base % 16) return p0_fail(c, P0_EALIGN, "dequant: weight offset must be 16-byte aligned");
+  if ((st = p0_range(c, out, 0, (uint64_t)w->rows * w->cols * 2, "dequant", "out", &ro))) return st;
+  const uint64_t n = (uint64_t)w->rows * wG;
+  cudaSetDevice(c->device);
+  deq_dump_q4<<<(unsigned)((n + 255) / 256), 256, 0, c->stream>>>(rw.base, w->rows, w->cols, wG, (uint16_t *)ro.base);
+  return p0_launched(c, "dequant");
+}
+
+}  // extern "C"

@@ -1,0 +1,104 @@
+"""The three matmul operators with the reference's own argument objects, over the C ABI.
+
+  gemv(g, a)   -> nsplit   engine/llm/lops.js:108-141       (a = {w, x: {buf, rowB}, N, K, kPer, pro, epi, y: {buf},
+                                                            ldy, stat: {buf, off}, norm: {buf, off}, ev: {buf, off},
+                                                            src: {n, ld}, mx: {buf}, cap})
+  gemvM(g, a)  -> nsplit   engine/llm/lops_spec.js:159-191  (adds M, x.ldx, y.ldm / y.ldy, stat.ld, ev.ld)
+  gemm(gpu, a) -> flops    engine/ops/gemm.js:255-322       (a = {w, x: {buf, off, ld, k0}, M, N, K, wr0, wr1, wk0,
+                                                            epi, act, acc, y: {buf, off, ld, n0}, ev: {buf, off},
+                                                            bv: {buf, off, up}, res, store} + post_gelu)
+w = {buf, off (bytes), bytes, enc, rows, cols} as WeightStore.t() returns it (core/store.js:249-253).
+Every call enqueues one kernel on the context's stream; results are read with g.read() after it. Errors raise
+P0Error with the reference's messages. There is no CPU path: these always run the CUDA kernels in libp0mm.so.
+"""
+import ctypes
+
+from . import _lib as L
+from .gpu import P0Error, handle
+
+
+def _wview(w, op="gemv"):
+    enc = w.get("enc")
+    if enc not in L.ENC:
+        # gemm.js:267 and lops.js:115 / lops_spec.js:166 word it differently
+        raise P0Error(L.P0_EINVAL, (op + ": unsupported weight encoding " if op == "gemm" else op + ": encoding ") + str(enc))
+    return L.p0_wview(handle(w["buf"]), int(w.get("off") or 0), int(w.get("bytes") or 0), L.ENC[enc], int(w["rows"]),
+                      int(w["cols"]), int(w.get("ld") or 0))
+
+
+def _b(o):
+    return handle(o.get("buf")) if o else L.p0_buf(0)
+
+
+def gemv(g, a):
+    """gemv(g, a) -> nsplit (lops.js:111-141)"""
+    x, y = a["x"], a["y"]
+    stat, norm, ev, src, mx = a.get("stat"), a.get("norm"), a.get("ev"), a.get("src"), a.get("mx")
+    pro, epi = a.get("pro") or "raw", a.get("epi") or "store"
+    if pro not in L.PRO:
+        raise P0Error(L.P0_EINVAL, "gemv: prologue " + str(pro))
+    if epi not in L.EPI:
+        raise P0Error(L.P0_EINVAL, "gemv: epilogue " + str(epi))
+    args = L.p0_gemv_args(
+        _wview(a["w"]), handle(x["buf"]), int(x.get("rowB") or 0), int(a["N"]), int(a["K"]), int(a.get("kPer") or 0), L.PRO[pro],
+        L.EPI[epi], handle(y["buf"]), int(a.get("ldy") or 0), _b(stat), int((stat or {}).get("off") or 0), _b(norm),
+        int((norm or {}).get("off") or 0), _b(ev), int((ev or {}).get("off") or 0), int((src or {}).get("n") or 0),
+        int((src or {}).get("ld") or 0), _b(mx), float(a.get("cap") or 0.0))
+    ns = ctypes.c_uint32()
+    g._check(g._lib.p0_gemv(g.ctx, ctypes.byref(args), ctypes.byref(ns)))
+    return ns.value
+
+
+def gemvM(g, a):
+    """gemvM(g, a) -> nsplit (lops_spec.js:163-191)"""
+    x, y = a["x"], a["y"]
+    stat, norm, ev, src, mx = a.get("stat"), a.get("norm"), a.get("ev"), a.get("src"), a.get("mx")
+    pro, epi = a.get("pro") or "raw", a.get("epi") or "store"
+    if pro not in L.PRO:
+        raise P0Error(L.P0_EINVAL, "gemvM: prologue " + str(pro))
+    if epi not in L.EPI:
+        raise P0Error(L.P0_EINVAL, "gemvM: epilogue " + str(epi))
+    args = L.p0_gemvM_args(
+        _wview(a["w"], "gemvM"), handle(x["buf"]), int(x.get("rowB") or 0), int(x.get("ldx") or 0), int(a["M"]), int(a["N"]), int(a["K"]),
+        int(a.get("kPer") or 0), L.PRO[pro], L.EPI[epi], handle(y["buf"]), int(y.get("ldy") or 0), int(y.get("ldm") or 0),
+        _b(stat), int((stat or {}).get("off") or 0), int((stat or {}).get("ld") or 0), _b(norm), int((norm or {}).get("off") or 0),
+        _b(ev), int((ev or {}).get("off") or 0), int((ev or {}).get("ld") or 0), int((src or {}).get("n") or 0),
+        int((src or {}).get("ld") or 0), _b(mx), float(a.get("cap") or 0.0))
+    ns = ctypes.c_uint32()
+    g._check(g._lib.p0_gemvM(g.ctx, ctypes.byref(args), ctypes.byref(ns)))
+    return ns.value
+
+
+def gemm(gpu, a):
+    """gemm(gpu, a) -> flops (gemm.js:264-322). x prologue 'f16'; acc 'f32'."""
+    x, y = a["x"], a["y"]
+    ev, bv = a.get("ev"), a.get("bv")
+    epi = a.get("epi") or "f16"
+    if epi not in L.GEPI:
+        raise P0Error(L.P0_EINVAL, "gemm: epilogue %s is not built in this library yet" % epi)
+    if (x.get("mode") or "f16") != "f16" or a.get("conv"):
+        raise P0Error(L.P0_EINVAL, "gemm: x prologue %s is not built in this library yet" % (x.get("mode") or "conv"))
+    acc = a.get("acc") or "f32"
+    args = L.p0_gemm_args(
+        _wview(a["w"], "gemm"), handle(x["buf"]), int(x.get("off") or 0), int(x.get("ld") or 0), int(x.get("k0") or 0), int(a["M"]),
+        int(a["N"]), int(a["K"]), int(a.get("wr0") or 0), int(a.get("wr1") or 0), int(a.get("wk0") or 0), L.GEPI[epi],
+        L.ACT[a.get("act") or "silu"], 0 if acc == "f32" else 1, handle(y["buf"]), int(y.get("off") or 0), int(y.get("ld") or 0),
+        int(y.get("n0") or 0), _b(ev), int((ev or {}).get("off") or 0), _b(bv), int((bv or {}).get("off") or 0),
+        int((bv or {}).get("up") or 0), int(bool(a.get("res"))), int(bool(a.get("store"))), int(bool(a.get("post_gelu"))))
+    fl = ctypes.c_double()
+    gpu._check(gpu._lib.p0_gemm(gpu.ctx, ctypes.byref(args), ctypes.byref(fl)))
+    return fl.value
+
+
+def dequant_f16(g, w, out):
+    """the GEMM's in-kernel dequantisation of a q4 view written to out (rows*cols fp16), for bit-exact checks"""
+    wv = _wview(w, "dequant")
+    g._check(g._lib.p0_dequant_f16(g.ctx, ctypes.byref(wv), handle(out)))
+
+
+def pack_q4(g, w_f32, N, K, out=None, w_off=0, ldw=0, out_off=0):
+    """packQ4 (engine/kcheck.js:22-38) on the device: a W f32 [N][K] buffer -> q4g32a.t64 records; returns the out buffer"""
+    if out is None:
+        out = g.buffer(N * K // 32 * 20, "q4")
+    g._check(g._lib.p0_pack_q4(g.ctx, handle(w_f32), int(w_off), int(ldw), int(N), int(K), handle(out), int(out_off)))
+    return out

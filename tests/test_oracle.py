@@ -1,0 +1,219 @@
+"""Pins the CPU oracle (oracle/oracle.c) before anything is checked against it.
+
+The reference ships no golden vectors and cannot run here (JavaScript + WebGPU), so the pins are:
+  1. hand-derived vectors for f2h (incl. the f64 -> f32 -> f16 double rounding of core/gpu.js:274-289) and rng;
+  2. a second, independent transcription of the JS helpers (tests/jsref.py) agreeing bit for bit;
+  3. the reference's own known-answer checks: kcheck.js:72-88 (q4 gemm, cos > 0.9995), kcheck.js:129-135 (q4 gemv,
+     cos > 0.9999), tune/kshipped.js:17-45 (per-shape gemv, cos > 0.99999 + tile argmax), tune/autotune.js:168-188
+     (engine kernel vs f64 dot, rel-L2 <= 2e-5), lops_spec.js:6-7 (gemvM row == gemv row);
+  4. the committed fixtures under tests/golden/ (oracle outputs; regenerate with tests/golden/make_golden.py).
+"""
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+
+from oracle import ref
+from tests import jsref
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+# ---------------------------------------------------------------- 1. hand-derived vectors
+def test_f2h_vectors():
+    cases = {
+        1.0: 0x3C00, -2.0: 0xC000, 65504.0: 0x7BFF, 65519.0: 0x7BFF, 65520.0: 0x7C00, 1e-8: 0x0000, 6e-8: 0x0001,
+        -0.0: 0x8000, 0.1: 0x2E66, float("inf"): 0x7C00, 2.0 ** -14: 0x0400, 2.0 ** -24: 0x0001, 3 * 2.0 ** -25: 0x0002,
+        # f64 -> f32 first: 1 + 2^-11 + 2^-40 rounds to the f32 1 + 2^-11, an f16 tie that goes to even (1.0);
+        # rounding f64 straight to f16 would give 0x3C01
+        1 + 2.0 ** -11 + 2.0 ** -40: 0x3C00,
+        1 + 2.0 ** -11 + 2.0 ** -20: 0x3C01,
+        1 + 3 * 2.0 ** -11: 0x3C02,   # tie between 0x3C01 and 0x3C02 -> even
+    }
+    got = ref.f2h(list(cases.keys()))
+    assert [int(v) for v in got] == list(cases.values())
+    assert int(ref.f2h([float("nan")])[0]) == 0x7E00
+
+
+def test_f2h_matches_ieee_rne_via_f32():
+    x = np.concatenate([ref.randn(20000, 5, 3.0), ref.randn(20000, 6, 1e-5), ref.randn(2000, 7, 3e4)]).astype(np.float64)
+    # numpy's f32 -> f16 cast is IEEE round-to-nearest-even, with subnormals and overflow to inf
+    want = x.astype(np.float32).astype(np.float16).view(np.uint16)
+    assert np.array_equal(ref.f2h(x), want)
+    h = np.arange(0, 0x7C00, 7, dtype=np.uint16)
+    assert np.array_equal(ref.h2f(h), h.view(np.float16).astype(np.float64))
+
+
+def test_rng_vectors():
+    # xorshift32 with JS's signed `>> 17`: hand-stepped for seed 1 (kcheck.js:10)
+    s = 1
+    s ^= (s << 13) & 0xFFFFFFFF            # 0x00002001
+    s ^= s >> 17                           # positive int32: same as logical
+    s ^= (s << 5) & 0xFFFFFFFF             # 0x00042021
+    assert s == 0x00042021 and ref.rng_state(1, 0) == 0x00042021
+    assert ref.rng_state(0, 0) == ref.rng_state(1, 0)   # seed 0 -> 1 (`seed >>> 0 || 1`)
+    # a state with the top bit set exercises the arithmetic shift: compare with the transcription
+    r = jsref.rng(0xDEADBEEF)
+    for k in range(200):
+        v = r()
+        assert int(round(v * 4294967296)) == ref.rng_state(0xDEADBEEF, k)
+
+
+# ---------------------------------------------------------------- 2. second transcription
+@pytest.mark.parametrize("seed,scale", [(0, 1.0), (7, 1.0), (11, 0.05), (31, 1.0), (0x80000001, 0.02)])
+def test_randn_matches_transcription(seed, scale):
+    n = 2001
+    assert np.array_equal(ref.randn(n, seed, scale), np.array(jsref.randn(n, seed, scale), np.float32))
+
+
+def test_f2h_matches_transcription():
+    xs = list(ref.randn(3000, 9, 2.0).astype(np.float64)) + [65520.0, 1e-7, 3e-5, -7e-6, 2 ** -15 * 1.5]
+    assert [int(v) for v in ref.f2h(xs)] == [jsref.f2h(x) for x in xs]
+
+
+def test_pack_q4_matches_transcription():
+    N, K = 64, 96
+    W = ref.randn(N * K, 11, 0.05)
+    # edge groups: constant (s == 0 -> 1), a tiny-range group (subnormal fp16 scale), large values
+    W[0:32] = 0.25
+    W[K:K + 32] = np.linspace(1.0, 1.0 + 3e-6, 32, dtype=np.float32)
+    W[2 * K:2 * K + 32] = np.linspace(-60000.0, 60000.0, 32, dtype=np.float32)
+    b, deq = ref.pack_q4(W, N, K)
+    jb, jdeq = jsref.pack_q4([float(v) for v in W], N, K)
+    assert bytes(b) == jb
+    assert np.array_equal(deq, np.array(jdeq, np.float32))
+
+
+def test_pack_q4_layout():
+    # one record by hand: row r's 32 codes at bytes r*16.., the (s, mn) word at 1024 + 4r (kcheck.js:32-34)
+    N, K = 64, 32
+    W = np.zeros(N * K, np.float32)
+    W[:32] = np.arange(32, dtype=np.float32) / 31 * 1.5 - 0.5     # row 0: min -0.5, max 1.0
+    b, deq = ref.pack_q4(W, N, K)
+    mn, s = -0.5, float(np.float16(1.5 / 15))
+    sm = int.from_bytes(bytes(b[1024:1028]), "little")
+    assert sm & 0xFFFF == int(np.float16(s).view(np.uint16)) and sm >> 16 == int(np.float16(mn).view(np.uint16))
+    q = [min(15, max(0, int(np.rint((W[i] - mn) / s)))) for i in range(32)]
+    assert list(b[:16]) == [q[2 * j] | (q[2 * j + 1] << 4) for j in range(16)]
+    assert np.array_equal(deq[:32], (np.array(q, np.float64) * s + mn).astype(np.float32))
+    # row 1: all zero -> s = 1, mn = 0, codes 0
+    assert int.from_bytes(bytes(b[1028:1032]), "little") == 0x3C00 and not any(b[16:32])
+
+
+# ---------------------------------------------------------------- 3. the reference's own known-answer checks
+def test_kcheck_gemm_q4():
+    # kcheck.js:72-88: M=32, N=128, K=256, X roundF16(randn(M*K, 7)), W randn(N*K, 11, 0.05), cos > 0.9995
+    M, N, K = 32, 128, 256
+    X = ref.round_f16(ref.randn(M * K, 7))
+    b, deq = ref.pack_q4(ref.randn(N * K, 11, 0.05), N, K)
+    Y = ref.h2f(ref.gemm(b, ref.f2h(X), M, N, K))
+    c = ref.compare(Y, ref.dot64(deq, X.astype(np.float64), M, N, K))
+    assert c["cos"] > 0.9995
+    for acc in ("f16",):   # the DiT's default fp16 partial sums (gemm.js:172-183) pass the same gate
+        c16 = ref.compare(ref.h2f(ref.gemm(b, ref.f2h(X), M, N, K, acc=acc)), ref.dot64(deq, X.astype(np.float64), M, N, K))
+        assert c16["cos"] > 0.9995
+
+
+def test_kcheck_gemv_q4():
+    # kcheck.js:129-135: N=256, K=1536, x randn(K, 31), W randn(N*K, 32, 0.05), cos > 0.9999
+    N, K = 256, 1536
+    x = ref.randn(K, 31)
+    b, deq = ref.pack_q4(ref.randn(N * K, 32, 0.05), N, K)
+    y, _, ns = ref.gemv(b, x, N, K)
+    assert ns == 1
+    assert ref.compare(y, ref.dot64(deq, x.astype(np.float64), 1, N, K).ravel())["cos"] > 0.9999
+
+
+def _gelu64(v):
+    return v * 0.5 * (1 + math.tanh(max(-15.0, min(15.0, 0.7978845608028654 * (v + 0.044715 * v * v * v)))))
+
+
+@pytest.mark.parametrize("pro,epi,K,kPer", [("rms", "softcap", 1536, 0), ("rms", "geglu", 1536, 0), ("raw", "store", 6144, 2048),
+                                            ("rms", "store", 2560, 0), ("raw", "store", 2048, 0), ("pleg", "store", 256, 0)])
+def test_kshipped_gemv(pro, epi, K, kPer):
+    # tune/kshipped.js:17-45: 128 rows, W randn(rows*K, 33+K, 0.05), x randn(K, 34+K), nw 0.9 + 0.2*((i*7919)%100)/100,
+    # ev randn(K, 35+K, 0.5); cos > 0.99999 and each tile's argmax equal or tied within 1e-5
+    N = 128
+    rows = 2 * N if epi == "geglu" else N
+    b, deq = ref.pack_q4(ref.randn(rows * K, 33 + K, 0.05), rows, K)
+    x = ref.randn(K, 34 + K)
+    nw = np.array([0.9 + 0.2 * ((i * 7919) % 100) / 100 for i in range(K)], np.float32)
+    ev = ref.randn(K, 35 + K, 0.5)
+    ss = float(np.sum(x.astype(np.float64) ** 2))
+    rstd = np.float32(1 / math.sqrt(ss / K + 1e-6))
+    NT = N // 64
+    mxb = np.zeros(NT * 2 + 4, np.float32)
+    mxb[NT * 2] = rstd
+    stb = np.array([0, rstd, 0, 0], np.float32)
+    kw = dict(pro=pro, epi=epi, kPer=kPer or None)
+    if pro == "rms":
+        kw.update(norm=nw, stat_buf=stb, stat_off=1)
+        if epi == "softcap":
+            kw.update(stat_off=NT * 2)
+    if pro == "pleg":
+        kw.update(src=(K, 1), ev=ev)
+    if epi == "softcap":
+        kw.update(mx=mxb, cap=30.0)
+    y, MX, ns = ref.gemv(b, x, N, K, **kw)
+    got = y.reshape(ns, -1)[:, :N].sum(0) if epi == "store" else y[:N]
+    xp = [float(x[k]) if pro == "raw" else float(x[k]) * float(rstd) * float(nw[k]) if pro == "rms" else _gelu64(float(x[k])) * float(ev[k])
+          for k in range(K)]
+    dot = ref.dot64(deq, np.array(xp, np.float64), 1, rows, K).ravel()
+    want = np.array([_gelu64(dot[n]) * dot[n + N] if epi == "geglu" else 30 * math.tanh(max(-15, min(15, dot[n] / 30)))
+                     if epi == "softcap" else dot[n] for n in range(N)])
+    assert ref.compare(got, want)["cos"] > 0.99999
+    if epi == "softcap":
+        mxu = MX.view(np.uint32)
+        for t in range(NT):
+            best = t * 64 + int(np.argmax(want[t * 64:(t + 1) * 64]))
+            i = int(mxu[2 * t + 1])
+            assert i == best or abs(want[i] - want[best]) <= 1e-5
+
+
+def test_autotune_gate_rel_l2():
+    # tune/autotune.js:168-188: the engine kernel against an f64 dot product, rel-L2 <= 2e-5 (fill s in [0.006, 0.010],
+    # min = -7.5 s, :83 -- here packQ4 of N(0, 0.02) weights)
+    N, K = 256, 2048
+    b, deq = ref.pack_q4(ref.randn(N * K, 3, 0.02), N, K)
+    x = ref.randn(K, 4)
+    y, _, _ = ref.gemv(b, x, N, K)
+    assert ref.compare(y, ref.dot64(deq, x.astype(np.float64), 1, N, K).ravel())["relL2"] <= 2e-5
+
+
+@pytest.mark.parametrize("M", [1, 2, 4, 8])
+def test_gemvM_rows_equal_gemv(M):
+    # lops_spec.js:6-7: each gemvM row is bit-identical to the engine gemv of that row
+    N, K = 128, 512
+    b, _ = ref.pack_q4(ref.randn(N * K, 21, 0.02), N, K)
+    X = ref.randn(M * K, 22)
+    Y, _, _ = ref.gemvM(b, X, M, N, K)
+    for m in range(M):
+        y1, _, _ = ref.gemv(b, X[m * K:(m + 1) * K], N, K)
+        assert np.array_equal(y1, Y[m * N:(m + 1) * N])
+
+
+def test_gemv_host_errors():
+    b, _ = ref.pack_q4(ref.randn(64 * 64, 1, 0.02), 64, 64)
+    with pytest.raises(ValueError, match="N % 64"):
+        ref.gemv(b, np.zeros(64, np.float32), 32, 64)
+    with pytest.raises(ValueError, match="needs a kPer"):
+        ref.gemv(b, np.zeros(4096, np.float32), 64, 4096)
+    with pytest.raises(ValueError, match="softcap needs one split"):
+        ref.gemv(b, np.zeros(64, np.float32), 64, 64, kPer=32, epi="softcap", mx=np.zeros(8, np.float32))
+
+
+# ---------------------------------------------------------------- 4. committed fixtures
+def test_golden_fixtures():
+    from tests.golden import make_golden
+    with open(os.path.join(GOLD, "manifest.json")) as f:
+        man = json.load(f)
+    cases = make_golden.cases()
+    assert sorted(man) == sorted(cases)
+    for name, fn in cases.items():
+        arrays = fn()
+        ent = man[name]
+        for k, arr in arrays.items():
+            stored = np.fromfile(os.path.join(GOLD, ent[k]["file"]), dtype=ent[k]["dtype"])
+            assert np.array_equal(stored, np.ascontiguousarray(arr).ravel().view(stored.dtype)), (name, k)
