@@ -51,6 +51,8 @@ def peaks():
 
 # ------------------------------------------------------------------------------------------ clocks sampler
 class Clocks:
+    """nvidia-smi sampled every 200 ms in the background; stop(t0, t1) summarises the samples taken inside the wall-clock
+    window [t0, t1] of the timed region (the nearest samples when the window is shorter than the sampling period)."""
     FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
 
@@ -62,36 +64,49 @@ class Clocks:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
                                           "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=self._read, daemon=True).start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 3.0:   # the sampler is running before the timed region starts
+                time.sleep(0.02)
         except Exception:
             self.proc = None
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
 
-    def stop(self):
+    def stop(self, t0=None, t1=None):
+        if t1 is not None:
+            end = time.time() + 0.5
+            while time.time() < end and not any(ts >= t1 for ts, _ in self.lines):
+                time.sleep(0.02)                               # one sample after the window
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(2)
             except Exception:
                 self.proc.kill()
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        rows = []
+        for ts, ln in self.lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
             try:
-                sm.append(float(f[1]))
-                mx = max(mx, float(f[2]))
+                rows.append((ts, float(f[1]), float(f[2]), f))
             except ValueError:
                 continue
-            for nm, v in zip(names, f[5:9]):
+        inside = [r for r in rows if t0 is None or (t0 <= r[0] <= t1)]
+        if not inside and rows and t0 is not None:
+            mid = (t0 + t1) / 2
+            inside = sorted(rows, key=lambda r: abs(r[0] - mid))[:2]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in inside:
+            for nm, v in zip(names, r[3][5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        sm = [r[1] for r in inside]
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max([r[2] for r in inside], default=None),
+                "reasons": sorted(reasons), "samples": len(inside), "window_s": round(t1 - t0, 4) if t0 is not None else None}
 
 
 # ------------------------------------------------------------------------------------------ distributed plumbing
@@ -205,8 +220,10 @@ def run_ours(args, ws, rank, local):
     dist = init_dist(ws, local)
     import p0pc0rn_b200 as p0
     g = p0.Gpu(local)
-    stream = torch.cuda.current_stream()
-    g.set_stream(stream.cuda_stream)          # the library launches on torch's stream: events and NCCL order with it
+    # one non-default stream for everything: torch events / copies / NCCL and the library's launches are ordered on it
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    g.set_stream(stream.cuda_stream)
     sw = Sweep(g, torch, ws, rank)
     torch.cuda.synchronize()
     # one gather buffer: every call's outputs of this rank, concatenated; one all-gather per step
@@ -240,13 +257,14 @@ def run_ours(args, ws, rank, local):
     head_events = []
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    w0 = time.time()
     t0.record()
     for _ in range(args.steps):
         sw.step(head_events)
         gather()
     t1.record()
     torch.cuda.synchronize()
-    clocks = clk.stop()
+    clocks = clk.stop(w0, time.time())
     ms = t0.elapsed_time(t1)
     if dist:
         tt = torch.tensor([ms], device="cuda")
@@ -470,13 +488,64 @@ def run_reference(args, ws, rank):
                     "restated in C (oracle/oracle.c) on the host cores"}
 
 
+def run_case(args):
+    """One operator on cuda:0, `--reps` launches, nothing timed: the small cases ncu captures.
+      --case gemv  --M 1 --N 262144 --K 2048 [--head]   (head: rms prologue + softcap epilogue, as the engine's head)
+      --case gemm  --M 4096 --N 9216 --K 3072 [--gelu]  (bias epilogue)"""
+    import torch
+    import p0pc0rn_b200 as p0
+    torch.cuda.set_device(0)
+    g = p0.Gpu(0)
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1)
+    M, N, Kk = args.M, args.N, args.K
+    wf = torch.randn(N, Kk, generator=gen, device=dev) * 0.02
+    q = p0.pack_q4(g, g.wrap(wf.data_ptr(), wf.numel() * 4, "wf"), N, Kk)
+    g.done()
+    del wf
+    w = {"buf": q, "off": 0, "enc": "q4g32a.t64", "rows": N, "cols": Kk}
+    if args.case == "gemv":
+        x = g.upload(np.random.default_rng(2).standard_normal(M * Kk).astype(np.float32))
+        y = g.buffer(M * N * 4)
+        a = {"w": w, "x": {"buf": x}, "N": N, "K": Kk, "y": {"buf": y}}
+        if args.head:
+            NT = N // 64
+            mx = g.upload(np.full(M * NT * 2 + 8, 0.9, np.float32))
+            a.update(pro="rms", epi="softcap", cap=30.0, norm={"buf": g.upload(np.ones(Kk, np.float32)), "off": 0}, mx={"buf": mx},
+                     stat={"buf": mx, "off": M * NT * 2} if M == 1 else {"buf": g.upload(np.full(8, 0.9, np.float32)), "off": 0, "ld": 1})
+        for _ in range(args.reps):
+            (p0.gemv if M == 1 else p0.gemvM)(g, dict(a, M=M) if M > 1 else a)
+    else:
+        x = torch.randn(M, Kk, generator=gen, device=dev).half()
+        bias = torch.randn(N, generator=gen, device=dev) * 0.01
+        y = torch.empty(M, N, device=dev, dtype=torch.float16)
+        a = {"w": w, "x": {"buf": g.wrap(x.data_ptr(), x.numel() * 2, "x")}, "M": M, "N": N, "K": Kk, "epi": "bias",
+             "ev": {"buf": g.wrap(bias.data_ptr(), bias.numel() * 4, "b"), "off": 0}, "y": {"buf": g.wrap(y.data_ptr(), y.numel() * 2, "y")},
+             "post_gelu": bool(args.gelu)}
+        for _ in range(args.reps):
+            p0.gemm(g, a)
+    g.done()
+    g.close()
+    print(json.dumps({"case": args.case, "M": M, "N": N, "K": Kk, "reps": args.reps, "ok": True}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--case", default=None, choices=["gemv", "gemm"], help="run one operator (for ncu captures)")
+    ap.add_argument("--M", type=int, default=1)
+    ap.add_argument("--N", type=int, default=262144)
+    ap.add_argument("--K", type=int, default=2048)
+    ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--head", action="store_true")
+    ap.add_argument("--gelu", action="store_true")
     args = ap.parse_args()
+    if args.case:
+        return run_case(args)
     args.warmup = max(3, args.warmup)
     ws, rank, local = dist_env()
     if args.impl == "reference":

@@ -44,7 +44,8 @@ enum { P0_ENC_Q4G32A_T64 = 1, P0_ENC_Q8G64S_T64 = 2, P0_ENC_F16 = 3 };
 p0_status p0_init(int device, p0_ctx **out);
 /* Gpu.freeAll + device.destroy (gpu.js) */
 p0_status p0_destroy(p0_ctx *ctx);
-/* run subsequent work on an external cudaStream_t (NULL = the context's own stream) */
+/* run subsequent work on an external cudaStream_t (NULL = the context's own stream; pass cudaStreamLegacy for CUDA's
+ * legacy default stream, whose handle 0 would otherwise mean "own stream") */
 p0_status p0_set_stream(p0_ctx *ctx, void *cuda_stream);
 /* the message of the last failed call, in the reference's wording (e.g. "gemv: N % 64") */
 p0_status p0_last_error(p0_ctx *ctx, char *msg, size_t cap);

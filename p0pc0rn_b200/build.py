@@ -34,17 +34,27 @@ def build(force=False, verbose=False, ptxas_v=False):
     if not force and not _stale():
         return LIB
     host_cc = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++"
-    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC", "-ccbin", host_cc,
-           "-o", LIB + ".tmp"] + [os.path.join(CSRC, s) for s in SOURCES]
+    common = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-ccbin", host_cc]
     if ptxas_v:
-        cmd.insert(1, "-Xptxas=-v")
-    if verbose:
-        print(" ".join(cmd), file=sys.stderr)
-    r = subprocess.run(cmd, capture_output=True, text=True)
+        common.insert(1, "-Xptxas=-v")
+    objdir = os.path.join(HERE, "_build")
+    os.makedirs(objdir, exist_ok=True)
+    objs = [os.path.join(objdir, os.path.splitext(s)[0] + ".o") for s in SOURCES]
+    cmds = [common + ["-c", os.path.join(CSRC, s), "-o", o] for s, o in zip(SOURCES, objs)]
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=len(cmds)) as ex:      # one nvcc per translation unit, in parallel
+        results = list(ex.map(lambda c: subprocess.run(c, capture_output=True, text=True), cmds))
+    for c, r in zip(cmds, results):
+        if verbose:
+            print(" ".join(c), file=sys.stderr)
+        if r.returncode != 0:
+            raise RuntimeError("nvcc failed:\n" + r.stdout + r.stderr)
+        if verbose or ptxas_v:
+            print(r.stdout + r.stderr, file=sys.stderr)
+    link = [nvcc(), *ARCH, "-shared", "-ccbin", host_cc, "-o", LIB + ".tmp"] + objs
+    r = subprocess.run(link, capture_output=True, text=True)
     if r.returncode != 0:
-        raise RuntimeError("nvcc failed:\n" + r.stdout + r.stderr)
-    if verbose or ptxas_v:
-        print(r.stdout + r.stderr, file=sys.stderr)
+        raise RuntimeError("nvcc link failed:\n" + r.stdout + r.stderr)
     os.replace(LIB + ".tmp", LIB)
     return LIB
 

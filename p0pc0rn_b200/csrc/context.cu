@@ -47,6 +47,7 @@ p0_status p0_destroy(p0_ctx *c) {
 
 p0_status p0_set_stream(p0_ctx *c, void *s) {
   if (!c) return P0_EINVAL;
+  // NULL selects the context's own stream; CUDA's legacy default stream is cudaStreamLegacy
   c->stream = s ? (cudaStream_t)s : c->own_stream;
   return P0_OK;
 }

@@ -4,16 +4,17 @@
 //
 // Y[m, n] = sum_k X[m, k] * Wdq[n, k], Wdq[n, k] = f16(q * s + mn) (gemm.js:147-148), fp32 accumulation.
 //
-// A CTA owns 128 weight rows x BT tokens (BT = 64 / 128 / 256) and walks K in 64-wide stages:
-//   warp 0      TMA producer: X tile [BT x 64] fp16 -> shared memory ring (128-byte swizzle), no multicast
-//   warp 1      TMEM allocator and the single MMA-issuing thread: tcgen05.mma kind::f16, M = 128 weight rows,
-//               N = BT tokens, K = 16, A (the dequantised weights) read from tensor memory, B (X) from shared
-//               memory, D (fp32) in tensor memory
-//   warps 2..9  dequantisers: thread = one weight row (its TMEM lane), half = one 32-k group of the stage; each
-//               loads its row's 16 code bytes and (s, mn) word straight from the packed record (128-bit loads,
-//               coalesced 512 B per warp), computes f16(fmaf(q, s, mn)) exactly and stores the 16 packed
-//               columns with tcgen05.st: weights never touch shared memory. After the last stage the same warps
-//               are the epilogue: tcgen05.ld -> bias / activation -> shared staging -> coalesced vector stores.
+// A CTA owns 128 weight rows x BT tokens (BT = 64 / 128 / 256) and walks K in 64-wide stages through a 5-slot ring:
+//   warp 0       producer: X tile [BT x 64] fp16 by TMA (128-byte swizzle, no multicast) and the stage's q4 records
+//                (two 64-row tiles x two 32-k groups, 2 x 2560 contiguous bytes) by cp.async.bulk, on one mbarrier
+//   warp 1       TMEM allocator and the single MMA-issuing thread: tcgen05.mma kind::f16, M = 128 weight rows,
+//                N = BT tokens, K = 16, A (the dequantised weights) read from tensor memory, B (X) from shared
+//                memory, D (fp32) in tensor memory
+//   warps 2..17  dequantisers: thread = one weight row (its TMEM lane), a warp = one 32-k half of every other stage;
+//                each reads its row's 16 code bytes and (s, mn) word from the ring, computes f16(fmaf(q, s, mn))
+//                exactly and writes the 16 packed columns to the stage's TMEM slot with tcgen05.st. After the last
+//                stage the same warps are the epilogue: tcgen05.ld -> bias / activation -> shared staging ->
+//                coalesced vector stores.
 // Orientation: D = Wdq . X^T, so TMEM lane = output column n and TMEM column = token m.
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -26,13 +27,16 @@ namespace {
 
 constexpr int kBW = 128;        // weight rows per CTA (TMEM lanes, MMA M)
 constexpr int kBK = 64;         // k per stage
-constexpr int kStages = 4;
-constexpr int kDqWarps = 8;     // warps 2..9
+constexpr int kStages = 5;
+constexpr int kDqWarps = 16;    // warps 2..17: (lane quarter) x (32-k half of a stage) x (stage parity)
+constexpr int kDqPerStage = 8;  // dequant warps that fill one stage
 constexpr int kThreads = 32 * (2 + kDqWarps);
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAcol = 256; // first TMEM column of the weight (A) stages; the accumulator holds columns [0, BT)
 constexpr uint32_t kMaxBT = 256;
-constexpr size_t kRingBytes = (size_t)kStages * kMaxBT * kBK * 2;   // 128 KB; also the epilogue staging area
+constexpr size_t kXStage = (size_t)kMaxBT * kBK * 2;                // 32 KB X slot (1024-aligned)
+constexpr size_t kRingBytes = (size_t)kStages * kXStage;              // 160 KB; also the epilogue staging area
+constexpr uint32_t kWStage = 2u * 2u * 1280u;                        // weights of a stage: 2 row tiles x 2 groups
 
 struct GemmParams {
   const uint8_t *W;   // weight view base
@@ -41,6 +45,7 @@ struct GemmParams {
   uint32_t M, N, K, wR0, wR1, wG, wk0, Nw, ldy, ny0, evOff, bvOff, bvUp;
   int epi, act, res, store, gate, bias, post_gelu;
   uint32_t BT, nk;
+  int wtma;           // 1: the CTA's 128 rows are two whole 64-row tiles -> records arrive by bulk copy
   uint32_t *err;
 };
 
@@ -90,12 +95,34 @@ __device__ __forceinline__ uint32_t weight_row(const GemmParams &p, uint32_t nB,
   return r < p.Nw - 1 ? r : p.Nw - 1;   // gemm.js:96 clamps to the last row
 }
 
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(tc::smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
+               : "memory");
+}
+
+// the two record-tiles a CTA's 128 TMEM lanes read (bulk-copy path): rows [nB, nB+128) map to tiles T0, T0+1, or for
+// swiglu the gate tile (even lanes) and the up tile (odd lanes); a tile beyond the weight clamps to the last one
+__device__ __forceinline__ void cta_tiles(const GemmParams &p, uint32_t nB, uint32_t &t0, uint32_t &t1) {
+  const uint32_t nt = p.Nw / 64u;
+  if (p.epi == P0_GEPI_SWIGLU) {
+    t0 = (p.wR0 + (nB >> 1)) >> 6;
+    t1 = (p.wR1 + (nB >> 1)) >> 6;
+  } else {
+    t0 = (p.wR0 + nB) >> 6;
+    t1 = t0 + 1;
+  }
+  t0 = t0 < nt ? t0 : nt - 1;
+  t1 = t1 < nt ? t1 : nt - 1;
+}
+
 __global__ void __launch_bounds__(kThreads, 1) gemm_q4_tc(const __grid_constant__ CUtensorMap tmx, const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *xring = smem;
-  uint64_t *full_x = (uint64_t *)(smem + kRingBytes);
-  uint64_t *full_a = full_x + kStages;
+  uint8_t *wring = smem + kRingBytes;                  // kStages x kWStage
+  uint64_t *full = (uint64_t *)(wring + (size_t)kStages * kWStage);
+  uint64_t *full_a = full + kStages;
   uint64_t *empty = full_a + kStages;
   uint64_t *accf = empty + kStages;
   uint32_t *tmem_slot = (uint32_t *)(accf + 1);
@@ -103,12 +130,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4_tc(const __grid_constant_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t BT = p.BT, nk = p.nk, nB = blockIdx.x * kBW, m0 = blockIdx.y * BT;
-  const uint32_t stage_bytes = BT * kBK * 2;
+  const uint32_t xbytes = BT * kBK * 2;
+  const uint32_t g0 = p.wk0 / 32u;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; s++) {
-      tc::mbar_init(&full_x[s], 1);
-      tc::mbar_init(&full_a[s], kDqWarps);
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&full_a[s], kDqPerStage);
       tc::mbar_init(&empty[s], 1);
     }
     tc::mbar_init(accf, 1);
@@ -125,21 +153,49 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4_tc(const __grid_constant_
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      tc::prefetch_tmap(&tmx);
-      uint32_t issued = 0;
-      for (uint32_t s = 0; s < nk; s++) {
-        const uint32_t slot = s % kStages, ph = (s / kStages) & 1u;
-        if (!tc::mbar_wait(&empty[slot], ph ^ 1u, abort_flag, p.err, 0x101u, P0_SPIN_LIMIT)) break;
-        tc::mbar_expect_tx(&full_x[slot], stage_bytes);
-        tc::tma_load_2d(xring + (size_t)slot * stage_bytes, &tmx, &full_x[slot], (int32_t)(s * kBK), (int32_t)m0);
-        issued++;
+    // ---------------------------------------------------------------- producer: X by TMA, weight records by bulk copy
+    uint32_t t0 = 0, t1 = 0;
+    cta_tiles(p, nB, t0, t1);
+    if (lane == 0) tc::prefetch_tmap(&tmx);
+    uint32_t issued = 0;
+    for (uint32_t s = 0; s < nk; s++) {
+      const uint32_t slot = s % kStages, ph = (s / kStages) & 1u;
+      bool got = true;
+      if (lane == 0) got = tc::mbar_wait(&empty[slot], ph ^ 1u, abort_flag, p.err, 0x101u, P0_SPIN_LIMIT);
+      if (!__shfl_sync(0xffffffffu, (int)got, 0)) break;
+      uint8_t *ws = wring + (size_t)slot * kWStage;
+      const uint32_t ng = min(2u, (p.K - s * kBK) / 32u);   // groups in this stage (the last may hold one)
+      if (p.wtma) {
+        if (lane == 0) {
+          tc::mbar_expect_tx(&full[slot], xbytes + 2u * ng * 1280u);
+          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), (int32_t)m0);
+          bulk_g2s(ws, p.W + ((size_t)t0 * p.wG + g0 + 2u * s) * 1280u, ng * 1280u, &full[slot]);
+          bulk_g2s(ws + 2560u, p.W + ((size_t)t1 * p.wG + g0 + 2u * s) * 1280u, ng * 1280u, &full[slot]);
+        }
+      } else {
+        // rows that are not whole tiles: the warp gathers them into lane order ([h][lane] 16-byte codes, then tails)
+        for (uint32_t i = 0; i < 4; i++) {
+          const uint32_t nl = i * 32u + lane, row = weight_row(p, nB, nl);
+          const uint8_t *rowrec = p.W + (size_t)(row >> 6) * p.wG * 1280u;
+          for (uint32_t h = 0; h < ng; h++) {
+            const uint8_t *rec = rowrec + (size_t)(g0 + 2u * s + h) * 1280u;
+            *reinterpret_cast<uint4 *>(ws + (h * 128u + nl) * 16u) = ldg_w(rec + (row & 63u) * 16u);
+            *reinterpret_cast<uint32_t *>(ws + 4096u + (h * 128u + nl) * 4u) = ldg_w32(rec + 1024u + (row & 63u) * 4u);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_expect_tx(&full[slot], xbytes);
+          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), (int32_t)m0);
+        }
       }
-      // every issued copy has landed before the CTA can exit (bounded; no abort short-cut: copies always finish)
+      issued++;
+    }
+    // every issued copy has landed before the CTA can exit (bounded; no abort short-cut: copies always finish)
+    if (lane == 0) {
       volatile uint32_t never = 0;
       for (uint32_t s = issued > (uint32_t)kStages ? issued - kStages : 0; s < issued; s++)
-        tc::mbar_wait(&full_x[s % kStages], (s / kStages) & 1u, &never, p.err, 0x102u, P0_SPIN_LIMIT);
+        tc::mbar_wait(&full[s % kStages], (s / kStages) & 1u, &never, p.err, 0x102u, P0_SPIN_LIMIT);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
@@ -147,10 +203,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4_tc(const __grid_constant_
       const uint32_t idesc = tc::idesc_f16_f32(kBW, BT);
       for (uint32_t s = 0; s < nk; s++) {
         const uint32_t slot = s % kStages, ph = (s / kStages) & 1u;
-        if (!tc::mbar_wait(&full_x[slot], ph, abort_flag, p.err, 0x201u, P0_SPIN_LIMIT)) break;
-        if (!tc::mbar_wait(&full_a[slot], ph, abort_flag, p.err, 0x202u, P0_SPIN_LIMIT)) break;
+        if (!tc::mbar_wait(&full_a[slot], ph, abort_flag, p.err, 0x202u, P0_SPIN_LIMIT)) break;   // implies X landed
         tc::fence_after();
-        const uint32_t xs = tc::smem_u32(xring + (size_t)slot * stage_bytes);
+        const uint32_t xs = tc::smem_u32(xring + (size_t)slot * kXStage);
 #pragma unroll
         for (uint32_t kk = 0; kk < kBK / 16; kk++)
           tc::mma_ts_f16(tmem, tmem + kAcol + slot * 32u + kk * 8u, tc::desc_sw128(xs + kk * 32u), idesc, (s | kk) != 0u);
@@ -163,36 +218,32 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4_tc(const __grid_constant_
     }
   } else {
     // ---------------------------------------------------------------- dequantisers, then the epilogue
-    const uint32_t q = (uint32_t)warp & 3u, h = (uint32_t)(warp - 2) >> 2;
+    const uint32_t d = (uint32_t)warp - 2u, q = (uint32_t)warp & 3u, h = (d >> 2) & 1u, par = d >> 3;
     const uint32_t nl = q * 32u + lane;               // this thread's TMEM lane = weight row of the tile
-    const uint32_t row = weight_row(p, nB, nl);
-    const uint8_t *rowrec = p.W + (size_t)(row >> 6) * p.wG * 1280u;
-    const uint32_t rr = row & 63u;
     const uint32_t tq = tmem + ((q * 32u) << 16);
-    const uint32_t g0 = p.wk0 / 32u;
+    // where this thread's 16 code bytes and (s, mn) word sit in a weight stage
+    uint32_t code_off, tail_off;
+    if (p.wtma) {
+      const uint32_t ts = p.epi == P0_GEPI_SWIGLU ? (nl & 1u) : (nl >> 6), r = p.epi == P0_GEPI_SWIGLU ? (nl >> 1) : (nl & 63u);
+      code_off = ts * 2560u + h * 1280u + r * 16u;
+      tail_off = ts * 2560u + h * 1280u + 1024u + r * 4u;
+    } else {
+      code_off = (h * 128u + nl) * 16u;
+      tail_off = 4096u + (h * 128u + nl) * 4u;
+    }
     bool ok = true;
-    uint4 cn = make_uint4(0, 0, 0, 0);
-    uint32_t smn = 0;
-    auto fetch = [&](uint32_t s, uint4 &c, uint32_t &sm) {
-      if (s < nk && s * kBK + h * 32u < p.K) {
-        const uint8_t *rec = rowrec + (size_t)(g0 + s * 2u + h) * 1280u;
-        c = ldg_w(rec + rr * 16u);
-        sm = ldg_w32(rec + 1024u + rr * 4u);
-      } else {
-        c = make_uint4(0, 0, 0, 0);   // k beyond K: zero weights (X is zero-filled there as well)
-        sm = 0;
-      }
-    };
-    fetch(0, cn, smn);
-    for (uint32_t s = 0; s < nk; s++) {
+    for (uint32_t s = par; s < nk; s += 2) {   // this warp fills every other stage
       const uint32_t slot = s % kStages, ph = (s / kStages) & 1u;
-      const uint4 c = cn;
-      const uint32_t sm = smn;
-      fetch(s + 1, cn, smn);   // one stage of loads in flight ahead
-      uint32_t r[16];
-      deq_row16(c, sm, r);
-      const bool got = tc::mbar_wait(&empty[slot], ph ^ 1u, abort_flag, p.err, 0x301u, P0_SPIN_LIMIT);
+      const bool got = tc::mbar_wait(&full[slot], ph, abort_flag, p.err, 0x301u, P0_SPIN_LIMIT);
       if (!__all_sync(0xffffffffu, got)) { ok = false; break; }   // warp-uniform: tcgen05.st is .sync.aligned
+      uint32_t r[16];
+      if (s * kBK + h * 32u < p.K) {
+        const uint8_t *ws = wring + (size_t)slot * kWStage;
+        deq_row16(*reinterpret_cast<const uint4 *>(ws + code_off), *reinterpret_cast<const uint32_t *>(ws + tail_off), r);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; i++) r[i] = 0u;   // k beyond K: zero weights (X is zero-filled there as well)
+      }
       tc::tmem_st16(tq + kAcol + slot * 32u + h * 16u, r);
       tc::tmem_wait_st();
       tc::fence_before();
@@ -222,12 +273,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4_tc(const __grid_constant_
         gB = p.BV[p.bvOff + o];
         uB = p.BV[p.bvOff + p.bvUp + o];
       }
-      for (uint32_t c0 = h * (BT / 2); c0 < (h + 1) * (BT / 2); c0 += 32) {
-        uint32_t r[32];
-        tc::tmem_ld32(tq + c0, r);
+      const uint32_t e = d >> 2, cpw = BT / 4;   // 16 warps: quarter q of the lanes, columns [e*BT/4, (e+1)*BT/4)
+      for (uint32_t c0 = e * cpw; c0 < (e + 1) * cpw; c0 += 16) {
+        uint32_t r[16];
+        tc::tmem_ld16(tq + c0, r);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
+        for (int j = 0; j < 16; j++) {
           const float v = __uint_as_float(r[j]);
           const uint32_t ml = c0 + j;
           if (swi) {
@@ -251,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4_tc(const __grid_constant_
     if (go && !*abort_flag) {
       // coalesced stores: 4 consecutive columns per thread per step (the reference's vec4 granularity)
       const uint32_t OC = swi ? 64u : 128u, q4 = OC / 4u, nOut0 = swi ? (nB >> 1) : nB;
-      const uint32_t tid = threadIdx.x - 64u;
+      const uint32_t tid = threadIdx.x - 64u;   // 0 .. kDqWarps*32-1
       const bool f32y = p.epi == P0_GEPI_F32 || p.epi == P0_GEPI_RESADD;
       for (uint32_t idx = tid; idx < BT * q4; idx += kDqWarps * 32u) {
         const uint32_t ml = idx / q4, cq = idx - ml * q4, m = m0 + ml;
@@ -393,7 +445,9 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   p.epi = (int)a->epi; p.act = (int)a->act; p.res = (int)a->res; p.store = (int)a->store; p.gate = a->ev.id != 0;
   p.bias = bias; p.post_gelu = (int)a->post_gelu;
   p.BT = BT; p.nk = (K + kBK - 1) / kBK; p.err = c->d_err;
-  const size_t smem = kRingBytes + 1024 + 256;
+  // bulk-copy weight path: every CTA's 128 lanes read two whole 64-row tiles
+  p.wtma = swi ? (a->wr0 % 64 == 0 && a->wr1 % 64 == 0 && (N / 2) % 64 == 0) : (a->wr0 % 64 == 0);
+  const size_t smem = kRingBytes + (size_t)kStages * kWStage + 1024 + 256;
   cudaSetDevice(c->device);
   cudaFuncSetAttribute(gemm_q4_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);

@@ -372,7 +372,8 @@ def test_gemm_swiglu(g, act):
     b, _ = ref.pack_q4(ref.randn(N * K, 140, 0.02), N, K)
     X = ref.f2h(ref.round_f16(ref.randn(M * K, 141)))
     bv = ref.randn(N, 142, 0.01)
-    y = run_gemm(g, b, X, M, N, K, epi="swiglu", act=act, wr0=0, wr1=N // 2, bv=(bv, 0, N // 2))
+    # y.ld defaults to N (the weight-column count, gemm.js:313) even for swiglu: the output rows are N/2 wide here
+    y = run_gemm(g, b, X, M, N, K, epi="swiglu", act=act, wr0=0, wr1=N // 2, bv=(bv, 0, N // 2), y={"ld": N // 2})
     want = ref.gemm(b, X, M, N, K, epi="swiglu", act=act, wr0=0, wr1=N // 2, bv=bv, bv_up=N // 2, ldy=N // 2)
     assert_close(ref.h2f(y), ref.h2f(want))
 
@@ -381,7 +382,7 @@ def test_gemm_swiglu_fixture(g):
     M, N, K = 40, 256, 256
     b, _ = ref.pack_q4(ref.randn(N * K, 15, 0.02), N, K)
     y = run_gemm(g, b, ref.f2h(ref.round_f16(ref.randn(M * K, 17))), M, N, K, epi="swiglu", act="gelu", wr0=0, wr1=N // 2,
-                 bv=(ref.randn(N, 16, 0.01), 0, N // 2))
+                 bv=(ref.randn(N, 16, 0.01), 0, N // 2), y={"ld": N // 2})
     assert_close(ref.h2f(y), ref.h2f(gold("gemm_swiglu", "y")))
 
 
