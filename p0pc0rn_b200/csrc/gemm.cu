@@ -57,14 +57,49 @@ __device__ __forceinline__ uint32_t deq_pair(uint32_t byte, float s, float mn) {
   __half2 h = __floats2half2_rn(fmaf(lo, s, mn), fmaf(hi, s, mn));
   return *reinterpret_cast<uint32_t *>(&h);
 }
+// The same values on the fp16 pipe. q*s + mn rounded once to fp16 (HFMA2) equals the reference's f16(f32(q*s + mn))
+// whenever q*s + mn is exact in f32, so that the f32 rounding is the identity. With s = S * 2^(Es-25) and
+// mn = Mn * 2^(Em-25) (S, Mn < 2^11 integers; E = max(exponent field, 1)), q*s + mn is an integer multiple of
+// 2^(min(Es,Em)-25) below 2^(16 + Es - Em) (Es >= Em) or 2^(12 + Em - Es) (Em > Es): exact in f32's 24 bits when
+// -12 <= Es - Em <= 8. deq_fast_ok() checks that (and finiteness) per row-group; other groups take deq_pair().
+__device__ __forceinline__ bool deq_fast_ok(uint32_t sm) {
+  const int es = (int)((sm >> 10) & 31u), em = (int)((sm >> 26) & 31u);
+  const int Es = es > 1 ? es : 1, Em = em > 1 ? em : 1, d = Es - Em;
+  return es != 31 && em != 31 && d <= 8 && d >= -12;
+}
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 __device__ __forceinline__ void deq_row16(const uint4 c, uint32_t sm, uint32_t (&r)[16]) {
-  const float s = __half2float(__ushort_as_half((unsigned short)(sm & 0xffffu)));
-  const float mn = __half2float(__ushort_as_half((unsigned short)(sm >> 16)));
   const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+  if (deq_fast_ok(sm)) {
+    const uint32_t s2 = __byte_perm(sm, 0, 0x1010), mn2 = __byte_perm(sm, 0, 0x3232);   // (s, s), (mn, mn)
 #pragma unroll
-  for (int i = 0; i < 4; i++)
+    for (int i = 0; i < 4; i++) {
+      const uint32_t w4 = w[i] >> 4;
 #pragma unroll
-    for (int b = 0; b < 4; b++) r[i * 4 + b] = deq_pair((w[i] >> (8 * b)) & 0xffu, s, mn);
+      for (int b = 0; b < 4; b++) {
+        // byte b of w (low code in bits 0-3) and byte b of w >> 4 (high code in bits 0-3) -> halves 0 and 1
+        const uint32_t x = __byte_perm(w[i], w4, (uint32_t)(b | (b << 4) | ((4 + b) << 8) | ((4 + b) << 12)));
+        const uint32_t q2 = hsub2_u32((x & 0x000F000Fu) | 0x64006400u, 0x64006400u);   // (1024 + q) - 1024, exact
+        r[i * 4 + b] = hfma2_u32(q2, s2, mn2);
+      }
+    }
+  } else {
+    const float s = __half2float(__ushort_as_half((unsigned short)(sm & 0xffffu)));
+    const float mn = __half2float(__ushort_as_half((unsigned short)(sm >> 16)));
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int b = 0; b < 4; b++) r[i * 4 + b] = deq_pair((w[i] >> (8 * b)) & 0xffu, s, mn);
+  }
 }
 
 __device__ __forceinline__ uint4 ldg_w(const void *p) {
@@ -118,7 +153,8 @@ __device__ __forceinline__ void cta_tiles(const GemmParams &p, uint32_t nB, uint
 
 __global__ void __launch_bounds__(kThreads, 1) gemm_q4_tc(const __grid_constant__ CUtensorMap tmx, const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  // 1024-byte aligned base by pointer arithmetic on the shared array (keeps shared-space loads and stores)
+  uint8_t *smem = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t *xring = smem;
   uint8_t *wring = smem + kRingBytes;                  // kStages x kWStage
   uint64_t *full = (uint64_t *)(wring + (size_t)kStages * kWStage);

@@ -75,6 +75,31 @@ def test_dequant_bit_exact(g, N, K):
     assert np.array_equal(g.read(out, 0, N * K * 2, np.uint16), ref.deq16(b, N, K).ravel())
 
 
+def test_dequant_edge_groups(g):
+    # groups whose q*s + mn is not exact in f32 (scale and min far apart in exponent) take the f32 path of the
+    # dequantiser, the others its fp16 fma path: both must give f16(f32(q*s + mn)) bit for bit
+    N, K = 128, 512
+    W = ref.randn(N * K, 9, 0.02).reshape(N, K)
+    rng = np.random.default_rng(5)
+    for r in range(N):
+        for gi in range(K // 32):
+            kind = (r * 7 + gi) % 6
+            sl = W[r, gi * 32:(gi + 1) * 32]
+            if kind == 1:      # large offset, tiny range: Em - Es large
+                sl[:] = np.float32(1000.0 + rng.uniform(0, 1e-3, 32))
+            elif kind == 2:    # minimum near zero, wide range: Es - Em large
+                sl[:] = np.float32(rng.uniform(0, 50.0, 32))
+                sl[0] = np.float32(1e-7)
+            elif kind == 3:    # negative offset, subnormal scale
+                sl[:] = np.float32(-2.0 - rng.uniform(0, 2e-6, 32))
+            elif kind == 4:    # huge values near the fp16 limit
+                sl[:] = np.float32(rng.uniform(-60000, 60000, 32))
+    b, _ = ref.pack_q4(W.ravel(), N, K)
+    out = g.buffer(N * K * 2)
+    p0.dequant_f16(g, wview(g.upload(b), N, K), out)
+    assert np.array_equal(g.read(out, 0, N * K * 2, np.uint16), ref.deq16(b, N, K).ravel())
+
+
 def test_dequant_fixture(g):
     b = gold("pack", "bytes")
     out = g.buffer(64 * 256 * 2)
