@@ -12,58 +12,10 @@
 // f32 rounding only.
 #include <cuda_fp16.h>
 
-#include "internal.h"
-#include "tc.cuh"
+#include "gemv_common.cuh"
 
 namespace {
-
-constexpr int kThreads = 256;   // 8 warps; a CTA = one 64-row tile x one k-split
-constexpr int kWarps = kThreads / 32;
-
-struct GemvParams {
-  const float *X;    // x rows (f32)
-  const uint8_t *W;  // the weight view's first byte (tile 0, group 0)
-  float *Y;
-  const float *NW;   // rms weights
-  const float *EV;   // pleg per-layer vector
-  const float *ST;   // rms rstd slots (gemv: the buffer lops.js:125 binds as MX)
-  float *MX;         // softcap per-tile {max, idx}
-  uint32_t M, N, K, wG, kPer, ldy, ldm, ldx, rowB, nOff, statOff, statLd, evOff, evLd, ldp, nsrc, ntile, xc;
-  float cap;
-  int pro, epi;
-  uint32_t *err;
-};
-
-__device__ __forceinline__ uint4 ldg_stream(const void *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ uint32_t ldg_u32(const void *p) {
-  uint32_t v;
-  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
-  return v;
-}
-
-// GELU as lops.js:26 writes it, in source order (no contraction)
-__device__ __forceinline__ float gelu_l(float v) {
-  float v3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, v), v), v);
-  float u = __fmul_rn(0.7978845608028654f, __fadd_rn(v, v3));
-  u = fminf(15.0f, fmaxf(-15.0f, u));
-  return __fmul_rn(__fmul_rn(v, 0.5f), __fadd_rn(1.0f, tanhf(u)));
-}
-
-// the prologue value x'(m, k) (lops.js:49-53 / lops_spec.js:60-64)
-__device__ __forceinline__ float prologue(const GemvParams &p, uint32_t m, uint32_t k) {
-  if (p.pro == P0_PRO_RAW) return p.X[m * p.ldx + p.rowB + k];
-  if (p.pro == P0_PRO_RMS)
-    return __fmul_rn(__fmul_rn(p.X[m * p.ldx + p.rowB + k], p.ST[p.statOff + m * p.statLd]), p.NW[p.nOff + k]);
-  float s = 0.0f;
-  for (uint32_t j = 0; j < p.nsrc; j++) s = __fadd_rn(s, p.X[j * p.ldp + m * p.ldx + k]);
-  if (p.pro == P0_PRO_SUM) return s;
-  return __fmul_rn(gelu_l(s), p.EV[p.evOff + m * p.evLd + k]);
-}
+using namespace p0gemv;
 
 // 8 codes of one u32 word (k = 8w .. 8w+7, low nibble first) dotted with 8 staged x values, as v_i = 1 + q_i/16
 __device__ __forceinline__ float dot8(uint32_t q, const float4 a, const float4 b, float acc) {
@@ -226,16 +178,6 @@ struct V2Plan {
   uint32_t units_per_item, items_per_split, nitems, gmax;
 };
 
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
-  __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t *>(&h);
-}
-
 // x of one split -> B fragments (hi/lo, permuted) + per-group sums; returns f = 2^24 / sigma
 template <int MT>
 __device__ float stage_x_v2(const GemvParams &p, uint32_t k0, uint32_t G, uint4 *xb, float *xsum, float *scratch) {
@@ -296,7 +238,7 @@ __device__ float stage_x_v2(const GemvParams &p, uint32_t k0, uint32_t G, uint4 
 // one warp unit = RW row-blocks of 16 rows (RW = 4: a whole 64-row tile) over one k-slice
 template <int MT, bool PAIR, int RW>
 __global__ void __launch_bounds__(kThreads) gemv_q4_v2(const GemvParams p, const V2Plan plan) {
-  extern __shared__ __align__(16) uint8_t smem8[];
+  extern __shared__ __align__(128) uint8_t smem8[];
   constexpr int NP = PAIR ? 2 : 1;
   uint4 *xb = reinterpret_cast<uint4 *>(smem8);                                        // [gmax][MT][4][2] uint4
   float *xsum = reinterpret_cast<float *>(smem8 + (size_t)plan.gmax * MT * 128);        // [gmax][MT]
@@ -451,289 +393,6 @@ __global__ void __launch_bounds__(kThreads) gemv_q4_v2(const GemvParams p, const
     }
     if (KS > 1) __syncthreads();   // red is reused by the next item
   }
-}
-
-// ================================================================================================================ v3: TMA-fed
-// The v2 datapath fed by bulk copies. Each of the 16 warps owns whole 64-row tiles (units) w, w + 16*grid, ... and a
-// private ring of shared-memory slots (a slot = two consecutive groups of its tile, 2560 contiguous bytes; geglu: one
-// group of the gate tile and the same group of the up tile). Lane 0 keeps the ring full with cp.async.bulk: after the
-// warp has read a slot it refills it with the stage kV3 slots ahead. Up to 160 KB of weights are in flight per SM,
-// and no warp waits on another. One k-split (nsplit == 1).
-// For M <= 4 the B operand's 8 columns carry x-hi of tokens 0..3 (columns 0..3) and x-lo (columns 4..7): one MMA per
-// k16 instead of two; lanes c = 2, 3 then hold the lo parts, added to lanes c = 0, 1 once per tile.
-constexpr int kV3Warps = 16;
-constexpr int kV3Threads = 32 * kV3Warps;
-constexpr uint32_t kV3Slot = 2560;
-constexpr uint32_t kV3MaxSlots = 4;
-
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(tc::smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
-               : "memory");
-}
-
-// x staging of v2 over the kernel's 512 threads
-template <int MT>
-__device__ float stage_x_v3(const GemvParams &p, uint32_t G, uint4 *xb, float *xsum, float *scratch) {
-  constexpr uint32_t T = kV3Threads;
-  const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5, len = G * 32;
-  float mx = 0.0f;
-  for (uint32_t i = t; i < MT * len; i += T) {
-    const uint32_t m = i / len, k = i - m * len;
-    mx = fmaxf(mx, fabsf(prologue(p, m, k)));
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if (lane == 0) scratch[warp] = mx;
-  __syncthreads();
-  mx = scratch[0];
-#pragma unroll
-  for (int w = 1; w < kV3Warps; w++) mx = fmaxf(mx, scratch[w]);
-  int e = 0;
-  if (mx > 0.0f && mx < INFINITY) frexpf(mx, &e);
-  const float sigma = ldexpf(1.0f, 14 - e), f = ldexpf(1.0f, 10 + e), finv = ldexpf(1.0f, -10 - e);
-  const uint32_t units = G * MT * 4, ulim = (units + T - 1) / T * T;
-  for (uint32_t u = t; u < ulim; u += T) {
-    float part = 0.0f;
-    if (u < units) {
-      const uint32_t gg = u / (MT * 4), rem = u - gg * (MT * 4), m = rem >> 2, c = rem & 3u;
-      const uint32_t kb = gg * 32 + c * 8;
-      float v[8], hv[8], lv[8];
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        v[i] = prologue(p, m, kb + i);
-        part += v[i];
-      }
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const float vs = v[i] * sigma * ((i & 1) ? 0.0625f : 1.0f);
-        const float h = __half2float(__float2half_rn(vs));
-        hv[i] = h;
-        lv[i] = vs - h;
-      }
-      xb[u * 2] = make_uint4(pack_h2(hv[0], hv[4]), pack_h2(hv[1], hv[5]), pack_h2(hv[2], hv[6]), pack_h2(hv[3], hv[7]));
-      xb[u * 2 + 1] = make_uint4(pack_h2(lv[0], lv[4]), pack_h2(lv[1], lv[5]), pack_h2(lv[2], lv[6]), pack_h2(lv[3], lv[7]));
-    }
-    part += __shfl_xor_sync(0xffffffffu, part, 1);
-    part += __shfl_xor_sync(0xffffffffu, part, 2);
-    if (u < units && (u & 3u) == 0) xsum[u >> 2] = part * finv;
-  }
-  __syncthreads();
-  return f;
-}
-
-template <int MT, bool PAIR>
-__global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, const uint32_t gx, const uint32_t nslot) {
-  constexpr bool PACK = MT <= 4;
-  constexpr int NP = PAIR ? 2 : 1;
-  extern __shared__ __align__(128) uint8_t smem8[];
-  uint8_t *ring = smem8;                                                             // [warp][slot] x 2560 B
-  uint64_t *full = reinterpret_cast<uint64_t *>(ring + (size_t)kV3Warps * nslot * kV3Slot);
-  float *scratch = reinterpret_cast<float *>(full + kV3Warps * kV3MaxSlots);          // 32 floats
-  volatile uint32_t *abort_flag = reinterpret_cast<volatile uint32_t *>(scratch + 24);
-  uint4 *xb = reinterpret_cast<uint4 *>(scratch + 32);                             // [G][MT][4][2]
-  const uint32_t G = p.K / 32;
-  float *xsum = reinterpret_cast<float *>(xb + (size_t)G * MT * 8);               // [G][MT]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t g = lane >> 2, c = lane & 3;
-  const uint32_t ntile = p.N / 64, stages_per_tile = PAIR ? G : (G + 1) / 2;
-  const size_t tile_bytes = (size_t)p.wG * 1280u, pair_off = (size_t)ntile * tile_bytes;
-  const uint32_t unit0 = blockIdx.x * kV3Warps + warp, ustride = gx * kV3Warps;
-  const uint32_t nunits = unit0 < ntile ? (ntile - unit0 + ustride - 1) / ustride : 0;
-  const uint32_t nstage = nunits * stages_per_tile;
-  uint8_t *myring = ring + (size_t)warp * nslot * kV3Slot;
-  uint64_t *myfull = full + warp * kV3MaxSlots;
-  if (lane == 0) {
-    for (uint32_t i = 0; i < nslot; i++) tc::mbar_init(&myfull[i], 1);
-    tc::fence_mbar_init();
-  }
-  if (threadIdx.x == 0) *abort_flag = 0u;
-  __syncwarp();
-  // stage j of this warp -> its slot (lane 0 only)
-  auto issue = [&](uint32_t j) {
-    const uint32_t ti = j / stages_per_tile, st = j - ti * stages_per_tile, slot = j % nslot;
-    const uint8_t *src = p.W + (size_t)(unit0 + ti * ustride) * tile_bytes;
-    uint8_t *dst = myring + (size_t)slot * kV3Slot;
-    if (PAIR) {
-      tc::mbar_expect_tx(&myfull[slot], 2560u);
-      bulk_g2s(dst, src + (size_t)st * 1280u, 1280u, &myfull[slot]);
-      bulk_g2s(dst + 1280u, src + pair_off + (size_t)st * 1280u, 1280u, &myfull[slot]);
-    } else {
-      const uint32_t ng = min(2u, G - 2u * st);
-      tc::mbar_expect_tx(&myfull[slot], ng * 1280u);
-      bulk_g2s(dst, src + (size_t)(2u * st) * 1280u, ng * 1280u, &myfull[slot]);
-    }
-  };
-  // the first copies fly while x is staged
-  if (lane == 0)
-    for (uint32_t j = 0; j < nslot && j < nstage; j++) issue(j);
-  const float f = stage_x_v3<MT>(p, G, xb, xsum, scratch);
-
-  const uint32_t btok = PACK ? (g & 3u) : g, bsel = PACK ? (g >> 2) : 0u;   // B column of this lane
-  const bool tok_ok = btok < MT, xs_lane = !PACK || c < 2;
-  uint32_t j = 0;
-  bool ok = true;
-  for (uint32_t ui = 0; ui < nunits && ok; ui++) {
-    const uint32_t tile = unit0 + ui * ustride;
-    float acc[NP][4][4];
-#pragma unroll
-    for (int a = 0; a < NP; a++)
-#pragma unroll
-      for (int r = 0; r < 4; r++) acc[a][r][0] = acc[a][r][1] = acc[a][r][2] = acc[a][r][3] = 0.0f;
-    for (uint32_t st = 0; st < stages_per_tile; st++, j++) {
-      const uint32_t slot = j % nslot, ph = (j / nslot) & 1u;
-      const bool got = tc::mbar_wait(&myfull[slot], ph, abort_flag, p.err, 0x511u, P0_SPIN_LIMIT);
-      if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
-      const uint8_t *sl = myring + (size_t)slot * kV3Slot;
-      const uint32_t ng = PAIR ? 1u : min(2u, G - 2u * st);
-      for (uint32_t h = 0; h < ng; h++) {
-        const uint32_t gg = PAIR ? st : 2u * st + h;
-        uint4 bh = make_uint4(0, 0, 0, 0), bl = bh;
-        if (tok_ok) {
-          const uint4 *bp = xb + ((size_t)(gg * MT + btok) * 4 + c) * 2;
-          bh = bp[bsel];
-          if (!PACK) bl = bp[1];
-        }
-        float xs0 = 0.0f, xs1 = 0.0f;
-        if (xs_lane) {
-          xs0 = 2 * c < MT ? xsum[gg * MT + 2 * c] : 0.0f;
-          xs1 = 2 * c + 1 < MT ? xsum[gg * MT + 2 * c + 1] : 0.0f;
-        }
-#pragma unroll
-        for (int a = 0; a < NP; a++) {
-          const uint8_t *rec = sl + (PAIR ? a : h) * 1280u;
-#pragma unroll
-          for (int r = 0; r < 4; r++) {
-            const uint32_t w0 = *reinterpret_cast<const uint32_t *>(rec + (16 * r + g) * 16 + c * 4);
-            const uint32_t w1 = *reinterpret_cast<const uint32_t *>(rec + (16 * r + g + 8) * 16 + c * 4);
-            const uint32_t t0 = *reinterpret_cast<const uint32_t *>(rec + 1024 + (16 * r + g) * 4);
-            const uint32_t t1 = *reinterpret_cast<const uint32_t *>(rec + 1024 + (16 * r + g + 8) * 4);
-            const uint32_t w0s = w0 >> 8, w1s = w1 >> 8;
-            const uint32_t A0[4] = {w0 & 0x000F000Fu, w1 & 0x000F000Fu, w0 & 0x00F000F0u, w1 & 0x00F000F0u};
-            const uint32_t A1[4] = {w0s & 0x000F000Fu, w1s & 0x000F000Fu, w0s & 0x00F000F0u, w1s & 0x00F000F0u};
-            float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            mma16816(d, A0, bh.x, bh.y);
-            mma16816(d, A1, bh.z, bh.w);
-            if (!PACK) {
-              mma16816(d, A0, bl.x, bl.y);
-              mma16816(d, A1, bl.z, bl.w);
-            }
-            const float s0 = __half2float(__ushort_as_half((unsigned short)(t0 & 0xffffu)));
-            const float m0 = __half2float(__ushort_as_half((unsigned short)(t0 >> 16)));
-            const float s1 = __half2float(__ushort_as_half((unsigned short)(t1 & 0xffffu)));
-            const float m1 = __half2float(__ushort_as_half((unsigned short)(t1 >> 16)));
-            acc[a][r][0] = fmaf(s0, d[0], fmaf(m0, xs0, acc[a][r][0]));
-            acc[a][r][1] = fmaf(s0, d[1], fmaf(m0, xs1, acc[a][r][1]));
-            acc[a][r][2] = fmaf(s1, d[2], fmaf(m1, xs0, acc[a][r][2]));
-            acc[a][r][3] = fmaf(s1, d[3], fmaf(m1, xs1, acc[a][r][3]));
-          }
-        }
-      }
-      // every lane has read the slot: lane 0 refills it with the stage nslot ahead (generic reads before the
-      // async-proxy write: warp sync, then a proxy fence)
-      __syncwarp();
-      if (lane == 0 && j + nslot < nstage) {
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        issue(j + nslot);
-      }
-    }
-    if (!ok) break;
-    if (PACK) {   // lanes c = 2, 3 hold the x-lo parts of lanes c = 0, 1
-#pragma unroll
-      for (int a = 0; a < NP; a++)
-#pragma unroll
-        for (int r = 0; r < 4; r++)
-#pragma unroll
-          for (int i = 0; i < 4; i++) acc[a][r][i] += __shfl_xor_sync(0xffffffffu, acc[a][r][i], 2);
-    }
-    // ---- epilogue of the tile (same contract as v2, RW = 4); PACK: lanes c < 2 hold the tokens
-    const uint32_t R0 = tile * 64, tk0 = 2u * c, tk1 = 2u * c + 1u;
-    if (p.epi == P0_EPI_SOFTCAP) {
-      float bv0 = -INFINITY, bv1 = -INFINITY;
-      uint32_t bi0 = 0xffffffffu, bi1 = 0xffffffffu;
-#pragma unroll
-      for (int r = 0; r < 4; r++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const uint32_t n = R0 + 16 * r + g + (i >= 2 ? 8 : 0), m = (i & 1) ? tk1 : tk0;
-          const float v = __fmul_rn(p.cap, tanhf(fminf(15.0f, fmaxf(-15.0f, __fdiv_rn(acc[0][r][i] * f, p.cap)))));
-          if (m < MT) p.Y[(size_t)m * p.ldm + n] = v;
-          const uint32_t rr = n & 63u;
-          if (i & 1) { if (v > bv1 || (v == bv1 && rr < bi1)) { bv1 = v; bi1 = rr; } }
-          else { if (v > bv0 || (v == bv0 && rr < bi0)) { bv0 = v; bi0 = rr; } }
-        }
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, bv0, o);
-        uint32_t oi = __shfl_xor_sync(0xffffffffu, bi0, o);
-        if (ov > bv0 || (ov == bv0 && oi < bi0)) { bv0 = ov; bi0 = oi; }
-        ov = __shfl_xor_sync(0xffffffffu, bv1, o);
-        oi = __shfl_xor_sync(0xffffffffu, bi1, o);
-        if (ov > bv1 || (ov == bv1 && oi < bi1)) { bv1 = ov; bi1 = oi; }
-      }
-      if (g == 0) {
-        if (tk0 < MT) { const size_t o = ((size_t)tk0 * p.ntile + tile) * 2; p.MX[o] = bv0; p.MX[o + 1] = __uint_as_float(tile * 64 + bi0); }
-        if (tk1 < MT) { const size_t o = ((size_t)tk1 * p.ntile + tile) * 2; p.MX[o] = bv1; p.MX[o + 1] = __uint_as_float(tile * 64 + bi1); }
-      }
-    } else {
-#pragma unroll
-      for (int r = 0; r < 4; r++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const uint32_t n = R0 + 16 * r + g + (i >= 2 ? 8 : 0), m = (i & 1) ? tk1 : tk0;
-          if (m >= MT) continue;
-          float v = acc[0][r][i] * f;
-          if (PAIR) v = __fmul_rn(gelu_l(v), acc[NP - 1][r][i] * f);
-          p.Y[(size_t)m * p.ldm + n] = v;
-        }
-    }
-  }
-  // copies this warp issued but did not consume (only after a failed wait) land before the CTA exits (bounded)
-  if (lane == 0 && !ok) {
-    volatile uint32_t never = 0;
-    const uint32_t issued = nstage < j + nslot ? nstage : j + nslot;
-    for (uint32_t k = j; k < issued; k++) tc::mbar_wait(&myfull[k % nslot], (k / nslot) & 1u, &never, p.err, 0x512u, P0_SPIN_LIMIT);
-  }
-}
-
-typedef void (*V3Kernel)(const GemvParams, const uint32_t, const uint32_t);
-template <int MT>
-V3Kernel v3_kernel_m(bool pair) { return pair ? gemv_q4_v3<MT, true> : gemv_q4_v3<MT, false>; }
-V3Kernel v3_kernel_for(uint32_t M, bool pair) {
-  switch (M) {
-    case 1: return v3_kernel_m<1>(pair);
-    case 2: return v3_kernel_m<2>(pair);
-    case 3: return v3_kernel_m<3>(pair);
-    case 4: return v3_kernel_m<4>(pair);
-    case 5: return v3_kernel_m<5>(pair);
-    case 6: return v3_kernel_m<6>(pair);
-    case 7: return v3_kernel_m<7>(pair);
-    default: return v3_kernel_m<8>(pair);
-  }
-}
-size_t v3_smem(uint32_t M, uint32_t G, uint32_t nslot) {
-  return (size_t)kV3Warps * nslot * kV3Slot + kV3Warps * kV3MaxSlots * 8 + 32 * 4 + (size_t)G * M * 128 + (size_t)G * M * 4;
-}
-uint32_t v3_slots(uint32_t M, uint32_t G) {
-  for (uint32_t n = kV3MaxSlots; n >= 2; n--)
-    if (v3_smem(M, G, n) <= 220u * 1024u) return n;
-  return 0;
-}
-// v3: one split, enough tiles to give every warp of every SM a tile, shared memory for a ring of >= 2 slots
-bool v3_fits(uint32_t M, uint32_t K, uint32_t nsplit, uint32_t ntile, int sms) {
-  return nsplit == 1 && v3_slots(M, K / 32) >= 2 && ntile >= (uint32_t)sms * kV3Warps;
-}
-cudaError_t launch_v3(const GemvParams &p, int sms, cudaStream_t s) {
-  const bool pair = p.epi == P0_EPI_GEGLU;
-  V3Kernel k = v3_kernel_for(p.M, pair);
-  const uint32_t G = p.K / 32, nslot = v3_slots(p.M, G);
-  const size_t smem = v3_smem(p.M, G, nslot);
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  const uint32_t ntile = p.N / 64, need = (ntile + kV3Warps - 1) / kV3Warps;
-  uint32_t gx = (uint32_t)sms;
-  if (gx > need) gx = need;
-  k<<<gx, kV3Threads, smem, s>>>(p, gx, nslot);
-  return cudaGetLastError();
 }
 
 typedef void (*V2Kernel)(const GemvParams, const V2Plan);

@@ -1,0 +1,356 @@
+// gemv_v3.cu -- the bulk-copy fed tensor-core GEMV (see the v3 notes below) and its launcher.
+#include "gemv_common.cuh"
+
+namespace p0gemv {
+namespace {
+
+// ================================================================================================================ v3: TMA-fed
+// The v2 arithmetic fed by bulk copies, for one k-split (nsplit == 1) and many tiles (the vocabulary head and other
+// wide projections). Each of 16 warps owns whole 64-row tiles (units) w, w + 16*grid, ... and a private ring of
+// shared-memory slots (a slot = two consecutive groups of its tile, 2560 contiguous bytes; geglu: one group of the gate
+// tile and the same group of the up tile). Lane 0 keeps the ring full with cp.async.bulk: when the warp has read a slot
+// it refills it with the stage nslot ahead. Up to 160 KB of weights are in flight per SM; no warp waits on another.
+// Per group the warp fetches each lane's code words with two ldmatrix.x4 (word c of rows g, g+8, ... of 32 rows each)
+// and runs v2's arithmetic: code MMAs (A = codes as fp16 subnormals, B = x hi/lo), then acc += s * D + mn * sum(x) in
+// f32. Both groups of a slot are loaded before any math and accumulate separately (summed per tile), so their MMA and
+// FMA chains interleave.
+// For M <= 4 the B operands' 8 columns carry the x-hi parts of tokens 0..3 (columns 0..3) and the x-lo parts (columns
+// 4..7): one MMA per k16 instead of two; lanes c = 2, 3 then hold the lo parts, added to lanes c = 0, 1 once per tile.
+constexpr int kV3Warps = 16;
+constexpr int kV3Threads = 32 * kV3Warps;
+constexpr uint32_t kV3Slot = 2560;
+constexpr uint32_t kV3MaxSlots = 4;
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(tc::smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
+               : "memory");
+}
+// shared loads stay ordered against the barrier waits and slot refills around them (volatile); the arithmetic between
+// them is free to interleave
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
+  return v;
+}
+// four 8x8 b16 matrices of 8 consecutive 16-byte rows each (lane l addresses row l): lane (g, c) receives b32 element
+// (g, c) of each, i.e. code word c of rows g, g+8, g+16, g+24 of the 32 rows starting at the lane-0 address
+__device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a)
+               : "memory");
+}
+
+// One group of one record (64 rows): its code words (two ldmatrix.x4) and (s, mn) words, loaded before any math
+struct V3Rec {
+  uint32_t w[4][2], t[4][2];
+};
+__device__ __forceinline__ void v3_load(V3Rec &q, uint32_t rec, uint32_t lane_row16, uint32_t tail_off) {
+  ldsm_x4(rec + lane_row16, q.w[0][0], q.w[0][1], q.w[1][0], q.w[1][1]);
+  ldsm_x4(rec + 512u + lane_row16, q.w[2][0], q.w[2][1], q.w[3][0], q.w[3][1]);
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    q.t[r][0] = lds32(rec + tail_off + r * 64);
+    q.t[r][1] = lds32(rec + tail_off + r * 64 + 32);
+  }
+}
+// the code MMAs and acc += s * D + mn * sum(x) for the 4 row-blocks (xs0 / xs1: this lane's x sums, 0 where they do
+// not apply)
+template <bool PACK>
+__device__ __forceinline__ void v3_math(float (&acc)[4][4], const V3Rec &q, const uint4 bh, const uint4 bl, float xs0, float xs1) {
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    const uint32_t w0 = q.w[r][0], w1 = q.w[r][1];
+    const uint32_t w0s = __umulhi(w0, 1u << 24), w1s = __umulhi(w1, 1u << 24);   // >> 8 on the multiplier pipe
+    const uint32_t A0[4] = {w0 & 0x000F000Fu, w1 & 0x000F000Fu, w0 & 0x00F000F0u, w1 & 0x00F000F0u};
+    const uint32_t A1[4] = {w0s & 0x000F000Fu, w1s & 0x000F000Fu, w0s & 0x00F000F0u, w1s & 0x00F000F0u};
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    mma16816(d, A0, bh.x, bh.y);
+    mma16816(d, A1, bh.z, bh.w);
+    if (!PACK) {
+      mma16816(d, A0, bl.x, bl.y);
+      mma16816(d, A1, bl.z, bl.w);
+    }
+    const __half2 h0 = *reinterpret_cast<const __half2 *>(&q.t[r][0]), h1 = *reinterpret_cast<const __half2 *>(&q.t[r][1]);
+    const float s0 = __low2float(h0), m0 = __high2float(h0), s1 = __low2float(h1), m1 = __high2float(h1);
+    acc[r][0] = fmaf(s0, d[0], fmaf(m0, xs0, acc[r][0]));
+    acc[r][1] = fmaf(s0, d[1], fmaf(m0, xs1, acc[r][1]));
+    acc[r][2] = fmaf(s1, d[2], fmaf(m1, xs0, acc[r][2]));
+    acc[r][3] = fmaf(s1, d[3], fmaf(m1, xs1, acc[r][3]));
+  }
+}
+
+// x staging (v2's): B fragments of x * sigma as fp16 hi / lo in the permuted k order, and per (group, token) sum(x) / f
+// in f32. Returns f = 2^24 / sigma.
+template <int MT>
+__device__ float stage_x_v3(const GemvParams &p, uint32_t G, uint4 *xb, float *xsum, float *scratch) {
+  constexpr uint32_t T = kV3Threads;
+  const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5, len = G * 32;
+  float mx = 0.0f;
+  for (uint32_t i = t; i < MT * len; i += T) {
+    const uint32_t m = i / len, k = i - m * len;
+    mx = fmaxf(mx, fabsf(prologue(p, m, k)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) scratch[warp] = mx;
+  __syncthreads();
+  mx = scratch[0];
+#pragma unroll
+  for (int w = 1; w < kV3Warps; w++) mx = fmaxf(mx, scratch[w]);
+  int e = 0;
+  if (mx > 0.0f && mx < INFINITY) frexpf(mx, &e);
+  const float sigma = ldexpf(1.0f, 14 - e), f = ldexpf(1.0f, 10 + e), finv = ldexpf(1.0f, -10 - e);
+  const uint32_t units = G * MT * 4, ulim = (units + T - 1) / T * T;
+  for (uint32_t u = t; u < ulim; u += T) {
+    float part = 0.0f;
+    if (u < units) {
+      const uint32_t gg = u / (MT * 4), rem = u - gg * (MT * 4), m = rem >> 2, c = rem & 3u;
+      const uint32_t kb = gg * 32 + c * 8;
+      float v[8], hv[8], lv[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        v[i] = prologue(p, m, kb + i);
+        part += v[i];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const float vs = v[i] * sigma * ((i & 1) ? 0.0625f : 1.0f);
+        const float h = __half2float(__float2half_rn(vs));
+        hv[i] = h;
+        lv[i] = vs - h;
+      }
+      xb[u * 2] = make_uint4(pack_h2(hv[0], hv[4]), pack_h2(hv[1], hv[5]), pack_h2(hv[2], hv[6]), pack_h2(hv[3], hv[7]));
+      xb[u * 2 + 1] = make_uint4(pack_h2(lv[0], lv[4]), pack_h2(lv[1], lv[5]), pack_h2(lv[2], lv[6]), pack_h2(lv[3], lv[7]));
+    }
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    if (u < units && (u & 3u) == 0) xsum[u >> 2] = part * finv;
+  }
+  __syncthreads();
+  return f;
+}
+
+template <int MT, bool PAIR>
+__global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, const uint32_t gx, const uint32_t nslot) {
+  constexpr bool PACK = MT <= 4;
+  constexpr int NP = PAIR ? 2 : 1;
+  extern __shared__ __align__(128) uint8_t smem8[];
+  uint8_t *ring = smem8;                                                              // [warp][slot] x 2560 B
+  uint64_t *full = reinterpret_cast<uint64_t *>(ring + (size_t)kV3Warps * nslot * kV3Slot);
+  float *scratch = reinterpret_cast<float *>(full + kV3Warps * kV3MaxSlots);          // 32 floats
+  volatile uint32_t *abort_flag = reinterpret_cast<volatile uint32_t *>(scratch + 24);
+  uint4 *xb = reinterpret_cast<uint4 *>(scratch + 32);                                // [G][MT][4][2]
+  const uint32_t G = p.K / 32;
+  float *xsum = reinterpret_cast<float *>(xb + (size_t)G * MT * 8);                   // [G][MT]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t g = lane >> 2, c = lane & 3;
+  const uint32_t ntile = p.N / 64, spt = PAIR ? G : (G + 1) / 2;   // stages per tile
+  const size_t tile_bytes = (size_t)p.wG * 1280u, pair_off = (size_t)ntile * tile_bytes;
+  const uint32_t unit0 = blockIdx.x * kV3Warps + warp, ustride = gx * kV3Warps;
+  const uint32_t nunits = unit0 < ntile ? (ntile - unit0 + ustride - 1) / ustride : 0;
+  const uint32_t nstage = nunits * spt;
+  uint8_t *myring = ring + (size_t)warp * nslot * kV3Slot;
+  uint64_t *myfull = full + warp * kV3MaxSlots;
+  if (lane == 0) {
+    for (uint32_t i = 0; i < nslot; i++) tc::mbar_init(&myfull[i], 1);
+    tc::fence_mbar_init();
+  }
+  if (threadIdx.x == 0) *abort_flag = 0u;
+  __syncwarp();
+  // the issue side: next stage (tile index ni_t, stage ni_s in it), counted incrementally (lane 0 only uses it)
+  uint32_t ni_t = 0, ni_s = 0, issued = 0;
+  const uint8_t *ni_src = p.W + (size_t)unit0 * tile_bytes;
+  const size_t ustride_bytes = (size_t)ustride * tile_bytes;
+  auto issue_next = [&](uint32_t slot) {
+    uint8_t *dst = myring + (size_t)slot * kV3Slot;
+    if (PAIR) {
+      tc::mbar_expect_tx(&myfull[slot], 2560u);
+      bulk_g2s(dst, ni_src + (size_t)ni_s * 1280u, 1280u, &myfull[slot]);
+      bulk_g2s(dst + 1280u, ni_src + pair_off + (size_t)ni_s * 1280u, 1280u, &myfull[slot]);
+    } else {
+      const uint32_t bytes = 2u * ni_s + 1u < G ? 2560u : 1280u;
+      tc::mbar_expect_tx(&myfull[slot], bytes);
+      bulk_g2s(dst, ni_src + (size_t)ni_s * 2560u, bytes, &myfull[slot]);
+    }
+    issued++;
+    if (++ni_s == spt) { ni_s = 0; ni_t++; ni_src += ustride_bytes; }
+  };
+  // the first copies fly while x is staged
+  if (lane == 0)
+    for (uint32_t j = 0; j < nslot && j < nstage; j++) issue_next(j);
+  const float f = stage_x_v3<MT>(p, G, xb, xsum, scratch);
+
+  const uint32_t btok = PACK ? (g & 3u) : g, bsel = PACK ? (g >> 2) : 0u;   // B column of this lane
+  const bool tok_ok = btok < MT, xs_lane = !PACK || c < 2;   // PACK: the x-sum term belongs to the hi columns
+  const uint32_t ring_s = tc::smem_u32(myring), xb_s = tc::smem_u32(xb), xsum_s = tc::smem_u32(xsum);
+  const uint32_t lane_row16 = (uint32_t)lane * 16u, tail_off = 1024u + g * 4u;
+  // this lane's addresses for group gg: B fragments at xb_lane + gg * MT * 128, x sums at xs_addr + gg * MT * 4
+  const uint32_t xb_lane = xb_s + btok * 128u + c * 32u + bsel * 16u, xs_addr = xsum_s + 2u * c * 4u;
+  uint32_t cs = 0, cph = 0;   // consumed slot and its phase
+  bool ok = true;
+  for (uint32_t ui = 0; ui < nunits && ok; ui++) {
+    const uint32_t tile = unit0 + ui * ustride;
+    float acc[2][NP][4][4];   // [group parity] -> independent FMA chains for the two groups of a slot
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+      for (int a = 0; a < NP; a++)
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+#pragma unroll
+          for (int i = 0; i < 4; i++) acc[h][a][r][i] = 0.0f;
+    for (uint32_t st = 0; st < spt; st++) {
+      const bool got = tc::mbar_wait(&myfull[cs], cph, abort_flag, p.err, 0x511u, P0_SPIN_LIMIT);
+      if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+      const uint32_t sl = ring_s + cs * kV3Slot;
+      const bool two = PAIR || 2u * st + 1u < G;   // PAIR: gate and up records of one group; else two groups
+      const uint32_t gg0 = PAIR ? st : 2u * st, gg1 = PAIR ? st : gg0 + 1u;
+      // all shared loads of the slot first
+      V3Rec q0, q1;
+      v3_load(q0, sl, lane_row16, tail_off);
+      if (two) v3_load(q1, sl + 1280u, lane_row16, tail_off);
+      uint4 bh0 = make_uint4(0, 0, 0, 0), bl0 = bh0, bh1 = bh0, bl1 = bh0;
+      float x00 = 0.0f, x01 = 0.0f, x10 = 0.0f, x11 = 0.0f;
+      if (tok_ok) {
+        bh0 = lds128(xb_lane + gg0 * MT * 128u);
+        if (!PACK) bl0 = lds128(xb_lane + gg0 * MT * 128u + 16u);
+        if (!PAIR && two) {
+          bh1 = lds128(xb_lane + gg1 * MT * 128u);
+          if (!PACK) bl1 = lds128(xb_lane + gg1 * MT * 128u + 16u);
+        }
+      }
+      if (xs_lane) {
+        if (2 * c < MT) { x00 = __uint_as_float(lds32(xs_addr + gg0 * MT * 4u)); x10 = __uint_as_float(lds32(xs_addr + gg1 * MT * 4u)); }
+        if (2 * c + 1 < MT) { x01 = __uint_as_float(lds32(xs_addr + gg0 * MT * 4u + 4u)); x11 = __uint_as_float(lds32(xs_addr + gg1 * MT * 4u + 4u)); }
+      }
+      // every lane has read the slot: lane 0 refills it with the stage nslot ahead (generic reads before the
+      // async-proxy write: warp sync, then a proxy fence); the math below uses registers only
+      __syncwarp();
+      if (lane == 0 && issued < nstage) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue_next(cs);
+      }
+      if (++cs == nslot) { cs = 0; cph ^= 1u; }
+      if (PAIR) {
+        v3_math<PACK>(acc[0][0], q0, bh0, bl0, x00, x01);
+        v3_math<PACK>(acc[1][NP - 1], q1, bh0, bl0, x00, x01);
+      } else {
+        v3_math<PACK>(acc[0][0], q0, bh0, bl0, x00, x01);
+        if (two) v3_math<PACK>(acc[1][0], q1, bh1, bl1, x10, x11);
+      }
+    }
+    if (!ok) break;
+    // row totals: f * (the two parities' sums); PACK: add the x-lo lanes c = 2, 3
+    float tot[NP][4][4];
+#pragma unroll
+    for (int a = 0; a < NP; a++)
+#pragma unroll
+      for (int r = 0; r < 4; r++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          float v = PAIR ? acc[a][a][r][i] * f : (acc[0][a][r][i] + acc[1][a][r][i]) * f;
+          if (PACK) v += __shfl_xor_sync(0xffffffffu, v, 2);
+          tot[a][r][i] = v;
+        }
+    // ---- epilogue of the tile (same contract as v2); PACK: lanes c < 2 hold the tokens
+    const uint32_t R0 = tile * 64, tk0 = 2u * c, tk1 = 2u * c + 1u;
+    if (p.epi == P0_EPI_SOFTCAP) {
+      float bv0 = -INFINITY, bv1 = -INFINITY;
+      uint32_t bi0 = 0xffffffffu, bi1 = 0xffffffffu;
+#pragma unroll
+      for (int r = 0; r < 4; r++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const uint32_t n = R0 + 16 * r + g + (i >= 2 ? 8 : 0), m = (i & 1) ? tk1 : tk0;
+          const float v = __fmul_rn(p.cap, tanhf(fminf(15.0f, fmaxf(-15.0f, __fdiv_rn(tot[0][r][i], p.cap)))));
+          if (m < MT) p.Y[(size_t)m * p.ldm + n] = v;
+          const uint32_t rr = n & 63u;
+          if (i & 1) { if (v > bv1 || (v == bv1 && rr < bi1)) { bv1 = v; bi1 = rr; } }
+          else { if (v > bv0 || (v == bv0 && rr < bi0)) { bv0 = v; bi0 = rr; } }
+        }
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, bv0, o);
+        uint32_t oi = __shfl_xor_sync(0xffffffffu, bi0, o);
+        if (ov > bv0 || (ov == bv0 && oi < bi0)) { bv0 = ov; bi0 = oi; }
+        ov = __shfl_xor_sync(0xffffffffu, bv1, o);
+        oi = __shfl_xor_sync(0xffffffffu, bi1, o);
+        if (ov > bv1 || (ov == bv1 && oi < bi1)) { bv1 = ov; bi1 = oi; }
+      }
+      if (g == 0) {
+        if (tk0 < MT) { const size_t o = ((size_t)tk0 * p.ntile + tile) * 2; p.MX[o] = bv0; p.MX[o + 1] = __uint_as_float(tile * 64 + bi0); }
+        if (tk1 < MT) { const size_t o = ((size_t)tk1 * p.ntile + tile) * 2; p.MX[o] = bv1; p.MX[o + 1] = __uint_as_float(tile * 64 + bi1); }
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < 4; r++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const uint32_t n = R0 + 16 * r + g + (i >= 2 ? 8 : 0), m = (i & 1) ? tk1 : tk0;
+          if (m >= MT) continue;
+          float v = tot[0][r][i];
+          if (PAIR) v = __fmul_rn(gelu_l(v), tot[NP - 1][r][i]);
+          p.Y[(size_t)m * p.ldm + n] = v;
+        }
+    }
+  }
+  // copies this warp issued but did not consume (only after a failed wait) land before the CTA exits (bounded)
+  if (lane == 0 && !ok) {
+    volatile uint32_t never = 0;
+    uint32_t slot = cs, ph = cph;
+    for (uint32_t k = 0; k < nslot; k++) {
+      tc::mbar_wait(&myfull[slot], ph, &never, p.err, 0x512u, P0_SPIN_LIMIT);
+      if (++slot == nslot) { slot = 0; ph ^= 1u; }
+    }
+  }
+}
+
+typedef void (*V3Kernel)(const GemvParams, const uint32_t, const uint32_t);
+template <int MT>
+V3Kernel v3_kernel_m(bool pair) { return pair ? gemv_q4_v3<MT, true> : gemv_q4_v3<MT, false>; }
+V3Kernel v3_kernel_for(uint32_t M, bool pair) {
+  switch (M) {
+    case 1: return v3_kernel_m<1>(pair);
+    case 2: return v3_kernel_m<2>(pair);
+    case 3: return v3_kernel_m<3>(pair);
+    case 4: return v3_kernel_m<4>(pair);
+    case 5: return v3_kernel_m<5>(pair);
+    case 6: return v3_kernel_m<6>(pair);
+    case 7: return v3_kernel_m<7>(pair);
+    default: return v3_kernel_m<8>(pair);
+  }
+}
+size_t v3_smem(uint32_t M, uint32_t G, uint32_t nslot) {
+  return (size_t)kV3Warps * nslot * kV3Slot + kV3Warps * kV3MaxSlots * 8 + 32 * 4 + (size_t)G * M * 128 + (size_t)G * M * 4;
+}
+uint32_t v3_slots(uint32_t M, uint32_t G) {
+  for (uint32_t n = kV3MaxSlots; n >= 2; n--)
+    if (v3_smem(M, G, n) <= 220u * 1024u) return n;
+  return 0;
+}
+}  // namespace
+
+// v3: one split, enough tiles to give every warp of every SM a tile, shared memory for a ring of >= 2 slots
+bool v3_fits(uint32_t M, uint32_t K, uint32_t nsplit, uint32_t ntile, int sms) {
+  return nsplit == 1 && v3_slots(M, K / 32) >= 2 && ntile >= (uint32_t)sms * kV3Warps;
+}
+cudaError_t launch_v3(const GemvParams &p, int sms, cudaStream_t s) {
+  const bool pair = p.epi == P0_EPI_GEGLU;
+  V3Kernel k = v3_kernel_for(p.M, pair);
+  const uint32_t G = p.K / 32, nslot = v3_slots(p.M, G);
+  const size_t smem = v3_smem(p.M, G, nslot);
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const uint32_t ntile = p.N / 64, need = (ntile + kV3Warps - 1) / kV3Warps;
+  uint32_t gx = (uint32_t)sms;
+  if (gx > need) gx = need;
+  k<<<gx, kV3Threads, smem, s>>>(p, gx, nslot);
+  return cudaGetLastError();
+}
+
+
+}  // namespace p0gemv
