@@ -31,6 +31,8 @@ K = 2048
 MS = (1, 2, 4, 8)
 NS = (2048, 16384, 262144)
 HEAD_N = 262144
+# DRAM bytes (read + write) of one head GEMV launch (N = 262144, K = 2048) from ncu captures at M = 1 and M = 8
+HEAD_TRAFFIC = 343.45e6
 
 
 def gemv_bytes(M, N, K, head):
@@ -295,7 +297,9 @@ def run_ours(args, ws, rank, local):
             "config": {"workload": "config2_gemv_sweep", "M": list(MS), "N": list(NS), "K": K, "parallelism": "column-split x%d + all-gather" % ws,
                        "l2": "weight rings >= 2x L2 per small-N call; head 335 MB > L2", "bytes_per_step": sw.step_bytes * ws},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                         "traffic": None, "kernel": "gemv head (rms+softcap) N=%d/rank K=%d, M=1/2/4/8" % (HEAD_N // ws, K),
+                         "traffic": HEAD_TRAFFIC if ws == 1 else None,
+                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per head launch, one ncu capture each at "
+                                         "M=1 (342.4 MB) and M=8 (344.5 MB), mean; algorithmic 336.6 / 344.5 MB", "kernel": "gemv head (rms+softcap) N=%d/rank K=%d, M=1/2/4/8" % (HEAD_N // ws, K),
                          "per_M_us": {str(k): round(v * 1e3, 2) for k, v in sorted(per_m.items())}, "peak_source": src},
             "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clocks, "gemm": gemm,
         }
