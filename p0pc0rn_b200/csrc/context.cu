@@ -7,6 +7,32 @@
 
 #include "internal.h"
 
+p0_status p0_workspace(p0_ctx *c, size_t cnt_bytes, size_t scratch_bytes, uint32_t **cnt, void **scratch) {
+  const size_t MB = (size_t)1 << 20;
+  cnt_bytes = (cnt_bytes + 255) / 256 * 256;
+  if (cnt_bytes > c->ws_cnt_bytes || c->ws_cnt_bytes + scratch_bytes > c->ws_bytes) {
+    const size_t ncnt = cnt_bytes > c->ws_cnt_bytes ? (cnt_bytes < 65536 ? 65536 : cnt_bytes) : c->ws_cnt_bytes;
+    size_t want = ncnt + scratch_bytes;
+    want = want < MB ? MB : (want + MB - 1) / MB * MB;
+    if (want < c->ws_bytes) want = c->ws_bytes;
+    if (c->ws) {
+      p0_status st = p0_cuda(c, cudaStreamSynchronize(c->stream), "workspace");   // queued kernels may still use it
+      if (st) return st;
+      cudaFree(c->ws);
+      c->ws = nullptr;
+      c->ws_bytes = c->ws_cnt_bytes = 0;
+    }
+    cudaError_t e = cudaMalloc(&c->ws, want);
+    if (e != cudaSuccess) { cudaGetLastError(); c->ws = nullptr; return p0_fail(c, P0_ENOMEM, "workspace %zu B: %s", want, cudaGetErrorString(e)); }
+    if ((e = cudaMemsetAsync(c->ws, 0, want, c->stream)) != cudaSuccess) return p0_cuda(c, e, "workspace zero-fill");
+    c->ws_bytes = want;
+    c->ws_cnt_bytes = ncnt;
+  }
+  *cnt = (uint32_t *)c->ws;
+  *scratch = (uint8_t *)c->ws + c->ws_cnt_bytes;
+  return P0_OK;
+}
+
 extern "C" {
 
 p0_status p0_init(int device, p0_ctx **out) {
@@ -38,6 +64,7 @@ p0_status p0_destroy(p0_ctx *c) {
   for (auto &kv : c->bufs)
     if (kv.second.owned) cudaFree(kv.second.ptr);
   c->bufs.clear();
+  if (c->ws) cudaFree(c->ws);
   if (c->d_err) cudaFree(c->d_err);
   if (c->h_err) cudaFreeHost(c->h_err);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
@@ -153,6 +180,8 @@ p0_status p0_done(p0_ctx *c, uint32_t timeout_ms) {
   if (c->h_err[0]) {
     uint32_t code = c->h_err[0];
     cudaMemset(c->d_err, 0, 4);
+    // a kernel that gave up may have left workspace counters mid-count: start the next call from zero
+    if (c->ws) cudaMemset(c->ws, 0, c->ws_bytes);
     return p0_fail(c, P0_ETIMEOUT, "done: a kernel gave up a bounded wait (code 0x%x)", code);
   }
   return P0_OK;
@@ -166,6 +195,6 @@ p0_status p0_device_ptr(p0_ctx *c, p0_buf b, uint64_t *out) {
   return P0_OK;
 }
 
-const char *p0_version(void) { return "p0mm sm_100a gemv-v1 gemm-tc-v1"; }
+const char *p0_version(void) { return "p0mm sm_100a gemv-v4 gemm-tc-v1"; }
 
 }  // extern "C"

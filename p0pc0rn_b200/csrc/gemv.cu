@@ -509,7 +509,9 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
   const uint32_t wG = w.cols / G, NT = N / 64, ntw = epi == P0_EPI_GEGLU ? 2 * NT : NT;
   // bind and bounds-check every view, as WebGPU validates bindings
   P0Range rw, rx, ry, rn, re, rs, rm;
-  uint64_t wneed = (uint64_t)ntw * wG * 1280u;
+  // the records the call reads: every tile's first K/32 groups, tiles wG records apart (a view may start at a later
+  // group of tile 0, as a k-slice of a wider weight does)
+  uint64_t wneed = ((uint64_t)(ntw - 1) * wG + K / G) * 1280u;
   if (w.bytes && wneed > w.bytes) return p0_fail(c, P0_EINVAL, "%s: weight view of %llu bytes holds fewer than %u tiles", op, (unsigned long long)w.bytes, ntw);
   if ((st = p0_range(c, w.buf, w.off, wneed, op, "W", &rw))) return st;
   if ((uintptr_t)rw.base % 16) return p0_fail(c, P0_EALIGN, "%s: weight offset (16-byte aligned records needed)", op);
@@ -543,7 +545,14 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
   p.xc = xc;
   cudaSetDevice(c->device);
   cudaError_t e;
-  if (v3_fits(M, K, nsplit, N / 64, c->sm_count)) e = launch_v3(p, c->sm_count, c->stream);
+  V4Plan pl{};
+  size_t scratch_bytes = 0;
+  if (v4_plan(p, nsplit, c->sm_count, &pl, &scratch_bytes)) {
+    void *scratch = nullptr;
+    if ((st = p0_workspace(c, v4_counter_bytes(pl), scratch_bytes, &pl.cnt, &scratch))) return st;
+    pl.part = (float *)scratch;
+    e = launch_v4(p, pl, c->stream);
+  } else if (v3_fits(M, K, nsplit, N / 64, c->sm_count)) e = launch_v3(p, c->sm_count, c->stream);
   else if (v2_fits(M, span)) e = launch_v2(p, nsplit, c->sm_count, c->stream);
   else e = launch_gemv(p, nsplit, c->stream);
   if ((st = p0_cuda(c, e, op))) return st;

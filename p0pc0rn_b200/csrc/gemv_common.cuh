@@ -70,8 +70,91 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 }
 
 
-// the v3 (bulk-copy fed) kernels, in gemv_v3.cu
+// ---------------------------------------------------------------- bulk-copy fed kernels (v3, v4)
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(tc::smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
+               : "memory");
+}
+// shared loads stay ordered against the barrier waits and slot refills around them (volatile); the arithmetic between
+// them is free to interleave
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
+  return v;
+}
+// four 8x8 b16 matrices of 8 consecutive 16-byte rows each (lane l addresses row l): lane (g, c) receives b32 element
+// (g, c) of each, i.e. code word c of rows g, g+8, g+16, g+24 of the 32 rows starting at the lane-0 address
+__device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a)
+               : "memory");
+}
+
+// One group of one record (64 rows): its code words (two ldmatrix.x4) and (s, mn) words, loaded before any math
+struct Rec {
+  uint32_t w[4][2], t[4][2];
+};
+__device__ __forceinline__ void rec_load(Rec &q, uint32_t rec, uint32_t lane_row16, uint32_t tail_off) {
+  ldsm_x4(rec + lane_row16, q.w[0][0], q.w[0][1], q.w[1][0], q.w[1][1]);
+  ldsm_x4(rec + 512u + lane_row16, q.w[2][0], q.w[2][1], q.w[3][0], q.w[3][1]);
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    q.t[r][0] = lds32(rec + tail_off + r * 64);
+    q.t[r][1] = lds32(rec + tail_off + r * 64 + 32);
+  }
+}
+// the code MMAs and acc += s * D + mn * sum(x) for the 4 row-blocks (xs0 / xs1: this lane's x sums, 0 where they do
+// not apply)
+template <bool PACK>
+__device__ __forceinline__ void rec_math(float (&acc)[4][4], const Rec &q, const uint4 bh, const uint4 bl, float xs0, float xs1) {
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    const uint32_t w0 = q.w[r][0], w1 = q.w[r][1];
+    const uint32_t w0s = __umulhi(w0, 1u << 24), w1s = __umulhi(w1, 1u << 24);   // >> 8 on the multiplier pipe
+    const uint32_t A0[4] = {w0 & 0x000F000Fu, w1 & 0x000F000Fu, w0 & 0x00F000F0u, w1 & 0x00F000F0u};
+    const uint32_t A1[4] = {w0s & 0x000F000Fu, w1s & 0x000F000Fu, w0s & 0x00F000F0u, w1s & 0x00F000F0u};
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    mma16816(d, A0, bh.x, bh.y);
+    mma16816(d, A1, bh.z, bh.w);
+    if (!PACK) {
+      mma16816(d, A0, bl.x, bl.y);
+      mma16816(d, A1, bl.z, bl.w);
+    }
+    const __half2 h0 = *reinterpret_cast<const __half2 *>(&q.t[r][0]), h1 = *reinterpret_cast<const __half2 *>(&q.t[r][1]);
+    const float s0 = __low2float(h0), m0 = __high2float(h0), s1 = __low2float(h1), m1 = __high2float(h1);
+    acc[r][0] = fmaf(s0, d[0], fmaf(m0, xs0, acc[r][0]));
+    acc[r][1] = fmaf(s0, d[1], fmaf(m0, xs1, acc[r][1]));
+    acc[r][2] = fmaf(s1, d[2], fmaf(m1, xs0, acc[r][2]));
+    acc[r][3] = fmaf(s1, d[3], fmaf(m1, xs1, acc[r][3]));
+  }
+}
+
+
+// the v3 (bulk-copy fed, whole tiles per warp) kernels, in gemv_v3.cu
 bool v3_fits(uint32_t M, uint32_t K, uint32_t nsplit, uint32_t ntile, int sms);
 cudaError_t launch_v3(const GemvParams &p, int sms, cudaStream_t s);
+
+// the v4 (stream-K) kernels, in gemv_v4.cu
+struct V4Plan {
+  uint32_t R;       // records of the call: ntile * G
+  uint32_t G;       // groups (records) per tile = K / 32
+  uint32_t Gs;      // groups per k-split
+  uint32_t nsplit;
+  uint32_t NW;      // warps of the grid (a multiple of 16, <= R)
+  uint32_t nslot;   // ring slots per warp
+  uint32_t *cnt;    // workspace: [ntile * nsplit] arrival counters, zero between calls
+  float *part;      // workspace: [ntile * nsplit + NW][M][64] partial sums of shared units
+};
+// false when the call does not fit v4 (geglu, weight columns < K, staged x too large, fewer records than warps);
+// else fills the plan (without the workspace pointers) and the scratch bytes its partial sums need
+bool v4_plan(const GemvParams &p, uint32_t nsplit, int sms, V4Plan *pl, size_t *scratch_bytes);
+// bytes of arrival counters the plan needs (one u32 per unit)
+size_t v4_counter_bytes(const V4Plan &pl);
+cudaError_t launch_v4(const GemvParams &p, const V4Plan &pl, cudaStream_t s);
 
 }  // namespace p0gemv

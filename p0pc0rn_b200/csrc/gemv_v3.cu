@@ -21,69 +21,6 @@ constexpr int kV3Threads = 32 * kV3Warps;
 constexpr uint32_t kV3Slot = 2560;
 constexpr uint32_t kV3MaxSlots = 4;
 
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(tc::smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
-               : "memory");
-}
-// shared loads stay ordered against the barrier waits and slot refills around them (volatile); the arithmetic between
-// them is free to interleave
-__device__ __forceinline__ uint32_t lds32(uint32_t a) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
-  return v;
-}
-__device__ __forceinline__ uint4 lds128(uint32_t a) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
-  return v;
-}
-// four 8x8 b16 matrices of 8 consecutive 16-byte rows each (lane l addresses row l): lane (g, c) receives b32 element
-// (g, c) of each, i.e. code word c of rows g, g+8, g+16, g+24 of the 32 rows starting at the lane-0 address
-__device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a)
-               : "memory");
-}
-
-// One group of one record (64 rows): its code words (two ldmatrix.x4) and (s, mn) words, loaded before any math
-struct V3Rec {
-  uint32_t w[4][2], t[4][2];
-};
-__device__ __forceinline__ void v3_load(V3Rec &q, uint32_t rec, uint32_t lane_row16, uint32_t tail_off) {
-  ldsm_x4(rec + lane_row16, q.w[0][0], q.w[0][1], q.w[1][0], q.w[1][1]);
-  ldsm_x4(rec + 512u + lane_row16, q.w[2][0], q.w[2][1], q.w[3][0], q.w[3][1]);
-#pragma unroll
-  for (int r = 0; r < 4; r++) {
-    q.t[r][0] = lds32(rec + tail_off + r * 64);
-    q.t[r][1] = lds32(rec + tail_off + r * 64 + 32);
-  }
-}
-// the code MMAs and acc += s * D + mn * sum(x) for the 4 row-blocks (xs0 / xs1: this lane's x sums, 0 where they do
-// not apply)
-template <bool PACK>
-__device__ __forceinline__ void v3_math(float (&acc)[4][4], const V3Rec &q, const uint4 bh, const uint4 bl, float xs0, float xs1) {
-#pragma unroll
-  for (int r = 0; r < 4; r++) {
-    const uint32_t w0 = q.w[r][0], w1 = q.w[r][1];
-    const uint32_t w0s = __umulhi(w0, 1u << 24), w1s = __umulhi(w1, 1u << 24);   // >> 8 on the multiplier pipe
-    const uint32_t A0[4] = {w0 & 0x000F000Fu, w1 & 0x000F000Fu, w0 & 0x00F000F0u, w1 & 0x00F000F0u};
-    const uint32_t A1[4] = {w0s & 0x000F000Fu, w1s & 0x000F000Fu, w0s & 0x00F000F0u, w1s & 0x00F000F0u};
-    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    mma16816(d, A0, bh.x, bh.y);
-    mma16816(d, A1, bh.z, bh.w);
-    if (!PACK) {
-      mma16816(d, A0, bl.x, bl.y);
-      mma16816(d, A1, bl.z, bl.w);
-    }
-    const __half2 h0 = *reinterpret_cast<const __half2 *>(&q.t[r][0]), h1 = *reinterpret_cast<const __half2 *>(&q.t[r][1]);
-    const float s0 = __low2float(h0), m0 = __high2float(h0), s1 = __low2float(h1), m1 = __high2float(h1);
-    acc[r][0] = fmaf(s0, d[0], fmaf(m0, xs0, acc[r][0]));
-    acc[r][1] = fmaf(s0, d[1], fmaf(m0, xs1, acc[r][1]));
-    acc[r][2] = fmaf(s1, d[2], fmaf(m1, xs0, acc[r][2]));
-    acc[r][3] = fmaf(s1, d[3], fmaf(m1, xs1, acc[r][3]));
-  }
-}
-
 // x staging (v2's): B fragments of x * sigma as fp16 hi / lo in the permuted k order, and per (group, token) sum(x) / f
 // in f32. Returns f = 2^24 / sigma.
 template <int MT>
@@ -191,7 +128,7 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
   const uint32_t lane_row16 = (uint32_t)lane * 16u, tail_off = 1024u + g * 4u;
   // this lane's addresses for group gg: B fragments at xb_lane + gg * MT * 128, x sums at xs_addr + gg * MT * 4
   const uint32_t xb_lane = xb_s + btok * 128u + c * 32u + bsel * 16u, xs_addr = xsum_s + 2u * c * 4u;
-  uint32_t cs = 0, cph = 0;   // consumed slot and its phase
+  uint32_t cs = 0, cph = 0, consumed = 0;   // consumed slot and its phase; slots consumed so far
   bool ok = true;
   for (uint32_t ui = 0; ui < nunits && ok; ui++) {
     const uint32_t tile = unit0 + ui * ustride;
@@ -207,13 +144,14 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
     for (uint32_t st = 0; st < spt; st++) {
       const bool got = tc::mbar_wait(&myfull[cs], cph, abort_flag, p.err, 0x511u, P0_SPIN_LIMIT);
       if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+      consumed++;
       const uint32_t sl = ring_s + cs * kV3Slot;
       const bool two = PAIR || 2u * st + 1u < G;   // PAIR: gate and up records of one group; else two groups
       const uint32_t gg0 = PAIR ? st : 2u * st, gg1 = PAIR ? st : gg0 + 1u;
       // all shared loads of the slot first
-      V3Rec q0, q1;
-      v3_load(q0, sl, lane_row16, tail_off);
-      if (two) v3_load(q1, sl + 1280u, lane_row16, tail_off);
+      Rec q0, q1;
+      rec_load(q0, sl, lane_row16, tail_off);
+      if (two) rec_load(q1, sl + 1280u, lane_row16, tail_off);
       uint4 bh0 = make_uint4(0, 0, 0, 0), bl0 = bh0, bh1 = bh0, bl1 = bh0;
       float x00 = 0.0f, x01 = 0.0f, x10 = 0.0f, x11 = 0.0f;
       if (tok_ok) {
@@ -237,11 +175,11 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
       }
       if (++cs == nslot) { cs = 0; cph ^= 1u; }
       if (PAIR) {
-        v3_math<PACK>(acc[0][0], q0, bh0, bl0, x00, x01);
-        v3_math<PACK>(acc[1][NP - 1], q1, bh0, bl0, x00, x01);
+        rec_math<PACK>(acc[0][0], q0, bh0, bl0, x00, x01);
+        rec_math<PACK>(acc[1][NP - 1], q1, bh0, bl0, x00, x01);
       } else {
-        v3_math<PACK>(acc[0][0], q0, bh0, bl0, x00, x01);
-        if (two) v3_math<PACK>(acc[1][0], q1, bh1, bl1, x10, x11);
+        rec_math<PACK>(acc[0][0], q0, bh0, bl0, x00, x01);
+        if (two) rec_math<PACK>(acc[1][0], q1, bh1, bl1, x10, x11);
       }
     }
     if (!ok) break;
@@ -303,7 +241,7 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
   if (lane == 0 && !ok) {
     volatile uint32_t never = 0;
     uint32_t slot = cs, ph = cph;
-    for (uint32_t k = 0; k < nslot; k++) {
+    for (uint32_t k = consumed; k < issued; k++) {
       tc::mbar_wait(&myfull[slot], ph, &never, p.err, 0x512u, P0_SPIN_LIMIT);
       if (++slot == nslot) { slot = 0; ph ^= 1u; }
     }

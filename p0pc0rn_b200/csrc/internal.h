@@ -29,8 +29,17 @@ struct p0_ctx {
   std::string last_error;
   uint32_t *d_err = nullptr;     // device word: kernels record a bounded-wait timeout here (never trap)
   uint32_t *h_err = nullptr;     // pinned mirror read by p0_done
+  // kernel workspace, grown on demand: [counters: ws_cnt_bytes][scratch: the rest]. The counter region never moves
+  // or shrinks while the workspace lives, so one call's scratch never lands on another call's counters.
+  void *ws = nullptr;
+  size_t ws_bytes = 0, ws_cnt_bytes = 0;
   std::mutex mu;
 };
+
+// the context's workspace with at least `cnt_bytes` of counters (zero between calls) and `scratch_bytes` of scratch
+// after them. Zero-filled when (re)allocated; kernels that use it leave every counter at zero when they finish, so it
+// is never cleared between calls. Growing it waits for the stream first.
+p0_status p0_workspace(p0_ctx *c, size_t cnt_bytes, size_t scratch_bytes, uint32_t **cnt, void **scratch);
 
 // records the message and returns the status (message wording follows the reference's `throw new Error(...)`)
 inline p0_status p0_fail(p0_ctx *c, p0_status st, const char *fmt, ...) {
