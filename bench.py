@@ -216,6 +216,14 @@ class Sweep:
         return n
 
 
+def capture(torch, stream, fn):
+    """a CUDA graph of the library launches `fn` issues on `stream` (the library launches on the stream it was given)"""
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream, capture_error_mode="relaxed"):
+        fn()
+    return gr
+
+
 def run_ours(args, ws, rank, local):
     import torch
     torch.cuda.set_device(local)
@@ -231,25 +239,54 @@ def run_ours(args, ws, rank, local):
     # one gather buffer: every call's outputs of this rank, concatenated; one all-gather per step
     gather_src = torch.empty(sw.out_floats, dtype=torch.float32, device="cuda")
     gather_dst = torch.empty(sw.out_floats * ws, dtype=torch.float32, device="cuda")
-    # device views of each call's output for the gather copy
     outs = []
     for c in sw.calls:
         buf = c["mxb"] if c["head"] else c["y"]
         n = c["M"] * (c["N"] // 64) * 2 if c["head"] else c["M"] * c["N"]
         outs.append((c["out_off"], n, buf.ptr))
 
+    def copies():
+        for off, n, ptr in outs:
+            _memcpy_d2d(gather_src.data_ptr() + off * 4, ptr, n * 4, stream.cuda_stream)
+
     def gather():
         """every call's outputs of this rank -> one buffer -> one NCCL all-gather (stream-ordered)"""
         if dist is None:
             return
-        for off, n, ptr in outs:
-            _memcpy_d2d(gather_src.data_ptr() + off * 4, ptr, n * 4, stream.cuda_stream)
+        copies()
         dist.all_gather_into_tensor(gather_dst, gather_src)
 
-    launches_per_step = len(sw.calls)
+    # eager warm-up (sizes the library's workspace before any capture), then the step as CUDA graphs: the 8 small-N calls
+    # as one graph per weight-ring position, each head call as its own graph (events between graph launches time the
+    # head inside the timed region), the gather copies as one graph; the NCCL all-gather stays eager
     for _ in range(args.warmup):
         sw.step()
         gather()
+    torch.cuda.synchronize()
+    small = [c for c in sw.calls if not c["head"]]
+    heads = [c for c in sw.calls if c["head"]]
+    R = max(len(c["ring"]) for c in small)
+    g_small = [capture(torch, stream, lambda: [sw.launch(c) for c in small]) for _ in range(R)]
+    g_head = [(c, capture(torch, stream, lambda c=c: sw.launch(c))) for c in heads]
+    g_copy = capture(torch, stream, copies) if dist else None
+
+    def step(s, head_events=None):
+        g_small[s % R].replay()
+        for c, gr in g_head:
+            if head_events is not None:
+                e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                e[0].record()
+                gr.replay()
+                e[1].record()
+                head_events.append((c, e))
+            else:
+                gr.replay()
+        if dist:
+            g_copy.replay()
+            dist.all_gather_into_tensor(gather_dst, gather_src)
+
+    for s in range(max(3, args.warmup)):
+        step(s)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -257,13 +294,13 @@ def run_ours(args, ws, rank, local):
     clk = Clocks(local)
     clk.start()
     head_events = []
+    every = max(1, args.steps // 100)   # head events on ~100 of the timed steps
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     w0 = time.time()
     t0.record()
-    for _ in range(args.steps):
-        sw.step(head_events)
-        gather()
+    for s in range(args.steps):
+        step(s, head_events if s % every == 0 else None)
     t1.record()
     torch.cuda.synchronize()
     clocks = clk.stop(w0, time.time())
@@ -275,10 +312,25 @@ def run_ours(args, ws, rank, local):
     head_ms = {}
     for c, (a, b) in head_events:
         head_ms.setdefault(c["M"], []).append(a.elapsed_time(b))
+    # ---- per-call device time after the timed region: each call launched once per ring copy (cold weights) in one graph
+    calls_us = {}
+    for c in sw.calls:
+        n = len(c["ring"]) if not c["head"] else 8
+        gr = capture(torch, stream, lambda c=c, n=n: [sw.launch(c) for _ in range(n)])
+        gr.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        calls_us["M%d_N%d" % (c["M"], c["Nfull"])] = round(e0.elapsed_time(e1) * 1e3 / n, 2)
+        del gr
+    del g_small, g_head, g_copy
     # ---- e2e: host inputs (pinned) -> device, the public API calls, results -> host, every step
     e2e = run_e2e(args, sw, g, torch, dist, gather)
-    # ---- secondary: GEMM configs 3 and 4
+    # ---- secondary: GEMM configs 3 and 4; config 5 decode chain (one GPU)
     gemm = run_gemm_secondary(args, g, torch, ws, rank, dist)
+    decode = run_decode_chain(args, g, torch, stream) if ws == 1 else None
     res = None
     if rank == 0:
         hbm, tfl, src = peaks()
@@ -295,13 +347,16 @@ def run_ours(args, ws, rank, local):
             "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "q4 weights, f32 x/accumulate", "data": "synthetic (seeded N(0,0.02) weights packed to q4g32a.t64 on device; N(0,1) fp16 x)",
             "config": {"workload": "config2_gemv_sweep", "M": list(MS), "N": list(NS), "K": K, "parallelism": "column-split x%d + all-gather" % ws,
-                       "l2": "weight rings >= 2x L2 per small-N call; head 335 MB > L2", "bytes_per_step": sw.step_bytes * ws},
+                       "l2": "weight rings >= 2x L2 per small-N call; head 335 MB > L2", "bytes_per_step": sw.step_bytes * ws,
+                       "launch": "CUDA graphs of the library's calls (small-N calls per ring position, one per head call); "
+                                 "events between graph launches time the head"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "traffic": HEAD_TRAFFIC if ws == 1 else None,
                          "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per head launch, one ncu capture each at "
                                          "M=1 (342.4 MB) and M=8 (344.5 MB), mean; algorithmic 336.6 / 344.5 MB", "kernel": "gemv head (rms+softcap) N=%d/rank K=%d, M=1/2/4/8" % (HEAD_N // ws, K),
                          "per_M_us": {str(k): round(v * 1e3, 2) for k, v in sorted(per_m.items())}, "peak_source": src},
-            "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clocks, "gemm": gemm,
+            "e2e": e2e, "gpu_launches": len(sw.calls) * args.steps, "clocks": clocks, "gemm": gemm,
+            "calls_us": calls_us, "decode": decode,
         }
         res["cpu_baseline"] = cpu_baseline(args) if ws == 1 else None
     if dist:
@@ -390,6 +445,107 @@ def _memcpy_kind(dst, src, nbytes, stream, kind):
     r = _cudart.cudaMemcpyAsync(ctypes.c_void_p(dst), ctypes.c_void_p(src), nbytes, kind, ctypes.c_void_p(stream))
     if r != 0:
         raise RuntimeError("cudaMemcpyAsync failed: %d" % r)
+
+
+# ------------------------------------------------------------------------------------------ decode chain (secondary)
+CHAIN_LAYERS, CHAIN_D, CHAIN_QKV, CHAIN_FF = 26, 2048, 2560, 8192
+
+
+def run_decode_chain(args, g, torch, stream):
+    """config 5: the linear chain of one decode pass of a random-init 26-layer decoder (hidden 2048): per layer QKV
+    2560x2048 (rms prologue), O 2048x2048, GeGLU 2x8192x2048 (rms prologue), down 2048x8192 (kPer 2048 -> 4 split
+    partials, as gemma4.js runs it), then the head 262144x2048 (rms prologue, softcap + per-tile argmax). Attention,
+    norms and residual adds are excluded (as config 5 states): each matmul reads a resident synthetic activation.
+    Every weight is its own q4g32a.t64 matrix (1.31 GB per pass > L2). One pass = one CUDA graph of the 105 calls;
+    tok/s = M tokens per pass / pass time (M = 1 decode, M = 4 draft-verify)."""
+    import p0pc0rn_b200 as p0
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev)
+    D = CHAIN_D
+
+    def packed(rows, cols, seed):
+        gen.manual_seed(seed)
+        wf = torch.randn(rows, cols, generator=gen, device=dev) * 0.02
+        wb = g.wrap(wf.data_ptr(), wf.numel() * 4, "wf")
+        q = p0.pack_q4(g, wb, rows, cols)
+        g.done()
+        g.free(wb)
+        del wf
+        return {"buf": q, "off": 0, "enc": "q4g32a.t64", "rows": rows, "cols": cols}
+
+    layers = []
+    for l in range(CHAIN_LAYERS):
+        layers.append((packed(CHAIN_QKV, D, 7000 + 4 * l), packed(D, D, 7001 + 4 * l), packed(2 * CHAIN_FF, D, 7002 + 4 * l),
+                       packed(D, CHAIN_FF, 7003 + 4 * l)))
+    head = packed(HEAD_N, D, 7999)
+    wbytes = (sum(w["rows"] * w["cols"] for ws_ in layers for w in ws_) + HEAD_N * D) * 0.625
+    rng = np.random.default_rng(5)
+    out = {}
+    for M in (1, 4):
+        xd = g.upload(rng.standard_normal(M * CHAIN_FF).astype(np.float32), "x")
+        nw = g.upload((1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32), "nw")
+        st = g.upload(np.full(8, 0.9, np.float32), "st")
+        y = g.buffer(4 * M * 2 * CHAIN_FF * 4, "y")
+        mx = g.buffer(M * (HEAD_N // 64) * 8 + 64, "mx")
+        yh = g.buffer(M * HEAD_N * 4, "yh")
+
+        def call(w, N, Kk, pro="raw", epi="store", kPer=0, yb=y, extra=None):
+            a = {"w": w, "x": {"buf": xd}, "N": N, "K": Kk, "y": {"buf": yb}, "pro": pro, "epi": epi}
+            if kPer:
+                a["kPer"] = kPer
+            if pro == "rms":
+                a["norm"] = {"buf": nw, "off": 0}
+                a["stat"] = {"buf": st, "off": 0, "ld": 1}
+            if extra:
+                a.update(extra)
+            if M == 1:
+                if pro == "rms" and epi != "softcap":
+                    a["stat"] = {"buf": st, "off": 0}
+                p0.gemv(g, a)
+            else:
+                p0.gemvM(g, dict(a, M=M))
+
+        def one_pass():
+            for wq, wo, wg, wd in layers:
+                call(wq, CHAIN_QKV, D, pro="rms")
+                call(wo, D, D)
+                call(wg, CHAIN_FF, D, pro="rms", epi="geglu")
+                call(wd, D, CHAIN_FF, kPer=2048)
+            if M == 1:   # the head's rstd is read from the mx buffer past the tile slots (lops.js:125)
+                call(head, HEAD_N, D, pro="rms", epi="softcap", yb=yh,
+                     extra={"mx": {"buf": mx}, "stat": {"buf": mx, "off": HEAD_N // 64 * 2}, "cap": 30.0})
+            else:
+                call(head, HEAD_N, D, pro="rms", epi="softcap", yb=yh, extra={"mx": {"buf": mx}, "cap": 30.0})
+
+        one_pass()
+        torch.cuda.synchronize()
+        gr = capture(torch, stream, one_pass)
+        for _ in range(2):
+            gr.replay()
+        reps = max(3, min(50, args.steps // 40))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        # algorithmic bytes: weights + x reads + outputs (down: 4 split partials; head: logits + MX)
+        act = (M * D * 4 + M * CHAIN_QKV * 4) + (M * D * 4 * 2) + (M * D * 4 + M * CHAIN_FF * 4) + (M * CHAIN_FF * 4 + 4 * M * D * 4)
+        pass_bytes = wbytes + CHAIN_LAYERS * act + M * D * 4 + M * HEAD_N * 4 + M * (HEAD_N // 64) * 8
+        out["M%d" % M] = {"ms_per_pass": round(ms, 4), "tok_s": round(M / (ms / 1e3), 1), "GB_s": round(pass_bytes / (ms / 1e3) / 1e9, 1),
+                          "calls_per_pass": CHAIN_LAYERS * 4 + 1}
+        del gr
+        for b in (xd, nw, st, y, mx, yh):
+            g.free(b)
+    for ws_ in layers:
+        for w in ws_:
+            g.free(w["buf"])
+    g.free(head["buf"])
+    hbm, _, _ = peaks()
+    return {"metric": "linear-chain decode tok/s (config 5: 26 x [QKV, O, GeGLU, down] + head, attention excluded)",
+            "weights_GB": round(wbytes / 1e9, 3), "hbm_peak_gbs": hbm, "passes": out,
+            "frac_of_hbm_M1": round(out["M1"]["GB_s"] / hbm, 4), "launch": "one CUDA graph per pass"}
 
 
 # ------------------------------------------------------------------------------------------ GEMM (secondary)
@@ -556,7 +712,7 @@ def run_case(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--case", default=None, choices=["gemv", "gemm"], help="run one operator (for ncu captures)")

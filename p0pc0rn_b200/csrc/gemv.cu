@@ -12,6 +12,9 @@
 // f32 rounding only.
 #include <cuda_fp16.h>
 
+#include <cstdlib>
+#include <cstring>
+
 #include "gemv_common.cuh"
 
 namespace {
@@ -545,14 +548,19 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
   p.xc = xc;
   cudaSetDevice(c->device);
   cudaError_t e;
+  // tuning override for comparisons: P0MM_GEMV=v2 or v3 keeps the newer kernels out of the dispatch
+  static const int newest = [] {
+    const char *s = getenv("P0MM_GEMV");
+    return s && !strcmp(s, "v2") ? 2 : s && !strcmp(s, "v3") ? 3 : 4;
+  }();
   V4Plan pl{};
   size_t scratch_bytes = 0;
-  if (v4_plan(p, nsplit, c->sm_count, &pl, &scratch_bytes)) {
+  if (newest >= 4 && v4_plan(p, nsplit, c->sm_count, &pl, &scratch_bytes)) {
     void *scratch = nullptr;
     if ((st = p0_workspace(c, v4_counter_bytes(pl), scratch_bytes, &pl.cnt, &scratch))) return st;
     pl.part = (float *)scratch;
     e = launch_v4(p, pl, c->stream);
-  } else if (v3_fits(M, K, nsplit, N / 64, c->sm_count)) e = launch_v3(p, c->sm_count, c->stream);
+  } else if (newest >= 3 && v3_fits(M, K, nsplit, N / 64, c->sm_count)) e = launch_v3(p, c->sm_count, c->stream);
   else if (v2_fits(M, span)) e = launch_v2(p, nsplit, c->sm_count, c->stream);
   else e = launch_gemv(p, nsplit, c->stream);
   if ((st = p0_cuda(c, e, op))) return st;

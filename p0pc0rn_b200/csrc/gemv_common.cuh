@@ -141,16 +141,18 @@ cudaError_t launch_v3(const GemvParams &p, int sms, cudaStream_t s);
 
 // the v4 (stream-K) kernels, in gemv_v4.cu
 struct V4Plan {
-  uint32_t R;       // records of the call: ntile * G
-  uint32_t G;       // groups (records) per tile = K / 32
-  uint32_t Gs;      // groups per k-split
+  uint32_t R;       // records of the call: ntile * Gt
+  uint32_t G;       // groups per tile = K / 32
+  uint32_t Gt;      // records per tile in the stream: G, or 2G for geglu (the gate tile's G, then the up tile's G)
+  uint32_t Gs;      // records per k-split (geglu: Gt, one unit per tile)
   uint32_t nsplit;
+  uint32_t ntile;   // 64-row tiles of the output (geglu: the up tiles follow at tile + ntile)
   uint32_t NW;      // warps of the grid (a multiple of 16, <= R)
   uint32_t nslot;   // ring slots per warp
   uint32_t *cnt;    // workspace: [ntile * nsplit] arrival counters, zero between calls
-  float *part;      // workspace: [ntile * nsplit + NW][M][64] partial sums of shared units
+  float *part;      // workspace: [ntile * nsplit + NW][halves][M][64] partial sums of shared units (geglu: 2 halves)
 };
-// false when the call does not fit v4 (geglu, weight columns < K, staged x too large, fewer records than warps);
+// false when the call does not fit v4 (weight columns < K, staged x too large, fewer records than warps);
 // else fills the plan (without the workspace pointers) and the scratch bytes its partial sums need
 bool v4_plan(const GemvParams &p, uint32_t nsplit, int sms, V4Plan *pl, size_t *scratch_bytes);
 // bytes of arrival counters the plan needs (one u32 per unit)

@@ -6,7 +6,7 @@ namespace {
 
 // ================================================================================================================ v3: TMA-fed
 // The v2 arithmetic fed by bulk copies, for one k-split (nsplit == 1) and many tiles (the vocabulary head and other
-// wide projections). Each of 16 warps owns whole 64-row tiles (units) w, w + 16*grid, ... and a private ring of
+// wide projections). Each of 16 warps owns whole 64-row tiles (units) of its CTA's contiguous share and a private ring of
 // shared-memory slots (a slot = two consecutive groups of its tile, 2560 contiguous bytes; geglu: one group of the gate
 // tile and the same group of the up tile). Lane 0 keeps the ring full with cp.async.bulk: when the warp has read a slot
 // it refills it with the stage nslot ahead. Up to 160 KB of weights are in flight per SM; no warp waits on another.
@@ -88,8 +88,11 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
   const uint32_t g = lane >> 2, c = lane & 3;
   const uint32_t ntile = p.N / 64, spt = PAIR ? G : (G + 1) / 2;   // stages per tile
   const size_t tile_bytes = (size_t)p.wG * 1280u, pair_off = (size_t)ntile * tile_bytes;
-  const uint32_t unit0 = blockIdx.x * kV3Warps + warp, ustride = gx * kV3Warps;
-  const uint32_t nunits = unit0 < ntile ? (ntile - unit0 + ustride - 1) / ustride : 0;
+  // CTA b owns the contiguous tiles [b*ntile/gx, (b+1)*ntile/gx) (27 or 28 of the head's 4096 on 148 SMs), dealt to its
+  // warps round-robin: every SM gets the same share of the work
+  const uint32_t T0 = (uint32_t)((uint64_t)blockIdx.x * ntile / gx), T1 = (uint32_t)((uint64_t)(blockIdx.x + 1u) * ntile / gx);
+  const uint32_t unit0 = T0 + warp, ustride = kV3Warps;
+  const uint32_t nunits = unit0 < T1 ? (T1 - unit0 + ustride - 1) / ustride : 0;
   const uint32_t nstage = nunits * spt;
   uint8_t *myring = ring + (size_t)warp * nslot * kV3Slot;
   uint64_t *myfull = full + warp * kV3MaxSlots;

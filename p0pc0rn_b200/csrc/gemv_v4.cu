@@ -99,51 +99,67 @@ struct V4Tot {
   float v[4][4];
 };
 
+// the first and last record (in the call's record stream) of unit u
+__device__ __forceinline__ void v4_unit_range(const V4Plan &pl, uint32_t u, uint32_t &rf, uint32_t &rl) {
+  const uint32_t tile = u / pl.nsplit, split = u - tile * pl.nsplit;
+  rf = tile * pl.Gt + split * pl.Gs;
+  rl = min(rf + pl.Gs, tile * pl.Gt + pl.Gt) - 1u;
+}
+
 // completes unit u for this warp: the epilogue directly when the warp holds the whole unit, else the workspace
-// hand-off described at the top of the file
-template <int MT>
-__device__ __noinline__ void v4_flush(const GemvParams &p, const V4Plan &pl, V4Tot t, uint32_t u, bool whole, uint32_t w) {
+// hand-off described at the top of the file. PAIR (geglu): `a` holds the gate rows' totals, `b` the up rows' (zeros for
+// a half this warp has no records of); else `a` holds the unit's totals.
+template <int MT, bool PAIR>
+__device__ __noinline__ void v4_flush(const GemvParams &p, const V4Plan &pl, V4Tot a, V4Tot b, uint32_t u, bool whole, uint32_t w) {
   constexpr bool PACK = MT <= 4;
+  constexpr uint32_t H = PAIR ? 2u : 1u;
   const uint32_t lane = threadIdx.x & 31u, g = lane >> 2, c = lane & 3u;
   const bool holder = !PACK || c < 2u;   // lanes whose values are the unit's (PACK: c = 2, 3 hold copies)
   const uint32_t tile = u / pl.nsplit, split = u - tile * pl.nsplit;
   if (!whole) {
-    float *ps = pl.part + (size_t)(u + w) * (MT * 64u);
+    float *ps = pl.part + (size_t)(u + w) * (H * MT * 64u);
 #pragma unroll
     for (int r = 0; r < 4; r++)
 #pragma unroll
       for (int i = 0; i < 4; i++) {
         const uint32_t n = 16u * r + g + (i >= 2 ? 8u : 0u), m = 2u * c + (i & 1);
-        if (holder && m < MT) ps[m * 64u + n] = t.v[r][i];
+        if (holder && m < MT) {
+          ps[m * 64u + n] = a.v[r][i];
+          if (PAIR) ps[MT * 64u + m * 64u + n] = b.v[r][i];
+        }
       }
     __threadfence();
     __syncwarp();
     uint32_t old = 0;
     if (lane == 0) old = atomicAdd(&pl.cnt[u], 1u);
     old = __shfl_sync(0xffffffffu, old, 0);
-    const uint32_t rf = tile * pl.G + split * pl.Gs, rl = min(rf + pl.Gs, tile * pl.G + pl.G) - 1u;
+    uint32_t rf, rl;
+    v4_unit_range(pl, u, rf, rl);
     const uint32_t wf = v4_owner(rf, pl.R, pl.NW), nparts = v4_owner(rl, pl.R, pl.NW) - wf + 1u;
     if (old + 1u != nparts) return;   // another warp completes the unit
     __threadfence();
 #pragma unroll
     for (int r = 0; r < 4; r++)
 #pragma unroll
-      for (int i = 0; i < 4; i++) t.v[r][i] = 0.0f;
+      for (int i = 0; i < 4; i++) a.v[r][i] = b.v[r][i] = 0.0f;
     for (uint32_t k = 0; k < nparts; k++) {
-      const float *pk = pl.part + (size_t)(u + wf + k) * (MT * 64u);
+      const float *pk = pl.part + (size_t)(u + wf + k) * (H * MT * 64u);
 #pragma unroll
       for (int r = 0; r < 4; r++)
 #pragma unroll
         for (int i = 0; i < 4; i++) {
           const uint32_t n = 16u * r + g + (i >= 2 ? 8u : 0u), m = 2u * c + (i & 1);
-          if (holder && m < MT) t.v[r][i] += __ldcg(pk + m * 64u + n);
+          if (holder && m < MT) {
+            a.v[r][i] += __ldcg(pk + m * 64u + n);
+            if (PAIR) b.v[r][i] += __ldcg(pk + MT * 64u + m * 64u + n);
+          }
         }
     }
     if (lane == 0) pl.cnt[u] = 0u;   // every part has arrived: the counter is free for the next call
   }
   // ---- epilogue of the unit (the v2 / v3 contract)
   const uint32_t R0 = tile * 64u, tk0 = 2u * c, tk1 = 2u * c + 1u;
-  if (p.epi == P0_EPI_SOFTCAP) {
+  if (!PAIR && p.epi == P0_EPI_SOFTCAP) {
     float bv0 = -INFINITY, bv1 = -INFINITY;
     uint32_t bi0 = 0xffffffffu, bi1 = 0xffffffffu;
 #pragma unroll
@@ -151,7 +167,7 @@ __device__ __noinline__ void v4_flush(const GemvParams &p, const V4Plan &pl, V4T
 #pragma unroll
       for (int i = 0; i < 4; i++) {
         const uint32_t n = R0 + 16u * r + g + (i >= 2 ? 8u : 0u), m = (i & 1) ? tk1 : tk0;
-        const float v = __fmul_rn(p.cap, tanhf(fminf(15.0f, fmaxf(-15.0f, __fdiv_rn(t.v[r][i], p.cap)))));
+        const float v = __fmul_rn(p.cap, tanhf(fminf(15.0f, fmaxf(-15.0f, __fdiv_rn(a.v[r][i], p.cap)))));
         if (m < MT) p.Y[(size_t)m * p.ldm + n] = v;
         const uint32_t rr = n & 63u;
         if (i & 1) { if (v > bv1 || (v == bv1 && rr < bi1)) { bv1 = v; bi1 = rr; } }
@@ -177,7 +193,9 @@ __device__ __noinline__ void v4_flush(const GemvParams &p, const V4Plan &pl, V4T
 #pragma unroll
       for (int i = 0; i < 4; i++) {
         const uint32_t n = R0 + 16u * r + g + (i >= 2 ? 8u : 0u), m = (i & 1) ? tk1 : tk0;
-        if (m < MT) p.Y[so + (size_t)m * p.ldm + n] = t.v[r][i];
+        if (m >= MT) continue;
+        if (PAIR) p.Y[(size_t)m * p.ldm + n] = __fmul_rn(gelu_l(a.v[r][i]), b.v[r][i]);
+        else p.Y[so + (size_t)m * p.ldm + n] = a.v[r][i];
       }
   }
 }
@@ -186,42 +204,33 @@ __device__ __noinline__ void v4_flush(const GemvParams &p, const V4Plan &pl, V4T
 // counter returns to zero; the results of the call are void (its error is reported)
 __device__ __noinline__ void v4_arrive_only(const V4Plan &pl, uint32_t u0, uint32_t r1) {
   if ((threadIdx.x & 31u) != 0u) return;
-  const uint32_t ulast = ((r1 - 1u) / pl.G) * pl.nsplit + ((r1 - 1u) % pl.G) / pl.Gs;
+  const uint32_t tl = (r1 - 1u) / pl.Gt, gl = (r1 - 1u) - tl * pl.Gt;
+  const uint32_t ulast = tl * pl.nsplit + (pl.nsplit > 1u ? gl / pl.Gs : 0u);
   for (uint32_t u = u0; u <= ulast; u++) {
-    const uint32_t tile = u / pl.nsplit, split = u - tile * pl.nsplit;
-    const uint32_t rf = tile * pl.G + split * pl.Gs, rl = min(rf + pl.Gs, tile * pl.G + pl.G) - 1u;
+    uint32_t rf, rl;
+    v4_unit_range(pl, u, rf, rl);
     const uint32_t nparts = v4_owner(rl, pl.R, pl.NW) - v4_owner(rf, pl.R, pl.NW) + 1u;
     if (nparts > 1u && atomicAdd(&pl.cnt[u], 1u) + 1u == nparts) pl.cnt[u] = 0u;
   }
 }
 
-// the record cursor of a warp: tile ct, group cg in the tile, split cs, group cgs in the split; `starts` = the record
-// is the first of its unit
-struct V4Cursor {
-  uint32_t ct, cg, cs, cgs;
-  bool starts;
-  __device__ __forceinline__ void init(uint32_t rec, const V4Plan &pl) {
-    ct = rec / pl.G;
-    cg = rec - ct * pl.G;
-    cs = cg / pl.Gs;
-    cgs = cg - cs * pl.Gs;
-    starts = cgs == 0u;
-  }
-  __device__ __forceinline__ uint32_t unit(const V4Plan &pl) const { return ct * pl.nsplit + cs; }
-  __device__ __forceinline__ void next(const V4Plan &pl) {
-    cg++;
-    cgs++;
-    starts = false;
-    if (cg == pl.G) { ct++; cg = 0; cs = 0; cgs = 0; starts = true; }
-    else if (cgs == pl.Gs) { cs++; cgs = 0; starts = true; }
-  }
-};
+// The warp's range is walked as segments: maximal runs of records inside one unit and (geglu) one half of it. Within a
+// segment the records are consecutive groups of one tile, so the per-slot work is the same as v3's; the unit
+// bookkeeping runs only where a segment ends.
+// seg_end(rec, r1): the end (exclusive) of the segment that starts at stream record rec
+__device__ __forceinline__ uint32_t v4_seg_end(const V4Plan &pl, uint32_t rec, uint32_t r1) {
+  const uint32_t t = rec / pl.Gt, j = rec - t * pl.Gt;
+  uint32_t e = (t + 1u) * pl.Gt;                                       // tile end
+  if (pl.Gt != pl.G) { if (j < pl.G) e = t * pl.Gt + pl.G; }          // geglu: end of the gate half
+  else if (pl.nsplit > 1u) e = min(e, t * pl.Gt + (j / pl.Gs + 1u) * pl.Gs);   // end of the k-split
+  return min(e, r1);
+}
 
-template <int MT>
+template <int MT, bool PAIR>
 __global__ void __launch_bounds__(kV4Threads, 1) gemv_q4_v4(const __grid_constant__ GemvParams p, const __grid_constant__ V4Plan pl) {
   constexpr bool PACK = MT <= 4;
   extern __shared__ __align__(128) uint8_t smem8[];
-  const uint32_t nslot = pl.nslot, G = pl.G;
+  const uint32_t nslot = pl.nslot, G = pl.G, Gt = pl.Gt;
   uint8_t *ring = smem8;                                                              // [warp][slot] x 2560 B
   uint64_t *full = reinterpret_cast<uint64_t *>(ring + (size_t)kV4Warps * nslot * kV4Slot);
   float *red = reinterpret_cast<float *>(full + kV4Warps * kV4MaxSlots);              // 32 floats
@@ -232,7 +241,6 @@ __global__ void __launch_bounds__(kV4Threads, 1) gemv_q4_v4(const __grid_constan
   const uint32_t g = lane >> 2, c = lane & 3;
   const uint32_t w = blockIdx.x * kV4Warps + warp;
   const uint32_t r0 = (uint32_t)((uint64_t)w * pl.R / pl.NW), r1 = (uint32_t)((uint64_t)(w + 1u) * pl.R / pl.NW);
-  const uint32_t nrec = r1 - r0, nstage = (nrec + 1u) / 2u;   // nrec >= 1 (NW <= R)
   uint8_t *myring = ring + (size_t)warp * nslot * kV4Slot;
   uint64_t *myfull = full + warp * kV4MaxSlots;
   if (lane == 0) {
@@ -241,29 +249,22 @@ __global__ void __launch_bounds__(kV4Threads, 1) gemv_q4_v4(const __grid_constan
   }
   if (threadIdx.x == 0) *abort_flag = 0u;
   __syncwarp();
-  // the issue side (lane 0): stage j = records r0 + 2j, r0 + 2j + 1 (the last stage may hold one). Record (t, g) sits
-  // at (t * wG + g) * 1280: a pair inside one tile is one 2560-byte copy, a pair across a tile boundary two copies.
-  uint32_t ig = r0 % G, issued = 0;
-  const uint8_t *src = p.W + ((size_t)(r0 / G) * p.wG + ig) * 1280u;
-  const size_t tile_skip = ((size_t)p.wG - G) * 1280u;   // from past a tile's last used record to the next tile's first
+  // ---- the issue side (lane 0 only): the same segments, one or two records per slot (a slot never crosses a
+  // segment). Stream record (t, j) sits at (t * wG + j) * 1280; geglu: j >= G is record j - G of up tile t + ntile.
+  uint32_t i_rec = r0, i_end = v4_seg_end(pl, r0, r1), issued = 0;
   auto issue_next = [&](uint32_t slot) {
-    const bool two = 2u * issued + 1u < nrec;
-    uint8_t *dst = myring + (size_t)slot * kV4Slot;
-    tc::mbar_expect_tx(&myfull[slot], two ? 2560u : 1280u);
-    if (two && ig + 1u == G) {
-      bulk_g2s(dst, src, 1280u, &myfull[slot]);
-      bulk_g2s(dst + 1280u, src + 1280u + tile_skip, 1280u, &myfull[slot]);
-    } else {
-      bulk_g2s(dst, src, two ? 2560u : 1280u, &myfull[slot]);
-    }
-    for (int k = 0; k < 2; k++) {   // advance two records
-      src += 1280u;
-      if (++ig == G) { ig = 0; src += tile_skip; }
-    }
+    uint32_t t = i_rec / Gt, j = i_rec - t * Gt;
+    if (PAIR && j >= G) { t += pl.ntile; j -= G; }
+    const uint8_t *src = p.W + ((size_t)t * p.wG + j) * 1280u;
+    const uint32_t n = i_end - i_rec >= 2u ? 2u : 1u;
+    tc::mbar_expect_tx(&myfull[slot], n * 1280u);
+    bulk_g2s(myring + (size_t)slot * kV4Slot, src, n * 1280u, &myfull[slot]);
+    i_rec += n;
+    if (i_rec == i_end && i_rec < r1) i_end = v4_seg_end(pl, i_rec, r1);
     issued++;
   };
   if (lane == 0)
-    for (uint32_t j = 0; j < nslot && j < nstage; j++) issue_next(j);   // these fly while x is staged
+    for (uint32_t k = 0; k < nslot && i_rec < r1; k++) issue_next(k);   // these fly while x is staged
   const float f = stage_x_v4<MT>(p, G, xb, xsum, red);
 
   const uint32_t btok = PACK ? (g & 3u) : g, bsel = PACK ? (g >> 2) : 0u;   // B column of this lane
@@ -273,6 +274,7 @@ __global__ void __launch_bounds__(kV4Threads, 1) gemv_q4_v4(const __grid_constan
   const uint32_t xb_lane = xb_s + btok * 128u + c * 32u + bsel * 16u, xs_addr = xsum_s + 2u * c * 4u;
 
   float acc[2][4][4];   // [record parity]: independent FMA chains for the two records of a slot
+  V4Tot gate;           // geglu: the gate half's totals once the warp has moved on to the up half
   auto zero = [&]() {
 #pragma unroll
     for (int h = 0; h < 2; h++)
@@ -293,74 +295,85 @@ __global__ void __launch_bounds__(kV4Threads, 1) gemv_q4_v4(const __grid_constan
       }
     return t;
   };
+  auto clear = [&](V4Tot &t) {
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) t.v[r][i] = 0.0f;
+  };
   zero();
-  V4Cursor cur;
-  cur.init(r0, pl);
-  uint32_t u = cur.unit(pl);   // the unit being accumulated
-  bool from_start = cur.starts, have = false;
+  clear(gate);
   uint32_t cs = 0, cph = 0, consumed = 0;
-  bool ok = true;
-  for (uint32_t st = 0; st < nstage; st++) {
-    const bool got = tc::mbar_wait(&myfull[cs], cph, abort_flag, p.err, 0x611u, P0_SPIN_LIMIT);
-    if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
-    consumed++;
-    const uint32_t sl = ring_s + cs * kV4Slot;
-    const bool two = 2u * st + 1u < nrec;
-    // record A at the cursor; record B after it
-    const bool startsA = cur.starts;
-    const uint32_t uA = cur.unit(pl), gA = cur.cg;
-    cur.next(pl);
-    const bool startsB = two && cur.starts;
-    const uint32_t uB = cur.unit(pl), gB = two ? cur.cg : gA;
-    if (two) cur.next(pl);
-    // all shared loads of the slot first
-    Rec q0, q1;
-    rec_load(q0, sl, lane_row16, tail_off);
-    if (two) rec_load(q1, sl + 1280u, lane_row16, tail_off);
-    uint4 bh0 = make_uint4(0, 0, 0, 0), bl0 = bh0, bh1 = bh0, bl1 = bh0;
-    float x00 = 0.0f, x01 = 0.0f, x10 = 0.0f, x11 = 0.0f;
-    if (tok_ok) {
-      bh0 = lds128(xb_lane + gA * MT * 128u);
-      if (!PACK) bl0 = lds128(xb_lane + gA * MT * 128u + 16u);
-      bh1 = lds128(xb_lane + gB * MT * 128u);
-      if (!PACK) bl1 = lds128(xb_lane + gB * MT * 128u + 16u);
-    }
-    if (xs_lane) {
-      if (2 * c < MT) { x00 = __uint_as_float(lds32(xs_addr + gA * MT * 4u)); x10 = __uint_as_float(lds32(xs_addr + gB * MT * 4u)); }
-      if (2 * c + 1 < MT) { x01 = __uint_as_float(lds32(xs_addr + gA * MT * 4u + 4u)); x11 = __uint_as_float(lds32(xs_addr + gB * MT * 4u + 4u)); }
-    }
-    // every lane has read the slot: lane 0 refills it (generic reads before the async-proxy write: warp sync, then a
-    // proxy fence); the math below uses registers only
-    __syncwarp();
-    if (lane == 0 && issued < nstage) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue_next(cs);
-    }
-    if (++cs == nslot) { cs = 0; cph ^= 1u; }
-    if (have && startsA) {   // A opens a new unit: the previous one is complete
-      v4_flush<MT>(p, pl, totals(), u, from_start, w);
-      zero();
-    }
-    if (!have || startsA) { u = uA; from_start = startsA; have = true; }
-    if (two && !startsB) {
-      rec_math<PACK>(acc[0], q0, bh0, bl0, x00, x01);
-      rec_math<PACK>(acc[1], q1, bh1, bl1, x10, x11);
-    } else {
-      rec_math<PACK>(acc[0], q0, bh0, bl0, x00, x01);
-      if (two) {   // B opens a new unit
-        v4_flush<MT>(p, pl, totals(), u, from_start, w);
-        zero();
-        u = uB;
-        from_start = true;
-        rec_math<PACK>(acc[1], q1, bh1, bl1, x10, x11);
+  bool ok = true, from_start = false, in_up = false;
+  uint32_t rec = r0;
+  while (rec < r1 && ok) {
+    const uint32_t e = v4_seg_end(pl, rec, r1);
+    const uint32_t t = rec / Gt, j = rec - t * Gt;
+    const uint32_t u = t * pl.nsplit + (pl.nsplit > 1u ? j / pl.Gs : 0u);
+    const bool ustart = j == 0u || (pl.nsplit > 1u && j % pl.Gs == 0u);
+    if (ustart || rec == r0) { from_start = ustart; in_up = PAIR && j >= G; }
+    const uint32_t g0 = PAIR && j >= G ? j - G : j, len = e - rec;
+    for (uint32_t k = 0; 2u * k < len; k++) {
+      const bool got = tc::mbar_wait(&myfull[cs], cph, abort_flag, p.err, 0x611u, P0_SPIN_LIMIT);
+      if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+      consumed++;
+      const uint32_t sl = ring_s + cs * kV4Slot;
+      const bool two = 2u * k + 1u < len;
+      const uint32_t gA = g0 + 2u * k, gB = two ? gA + 1u : gA;
+      // all shared loads of the slot first
+      Rec q0, q1;
+      rec_load(q0, sl, lane_row16, tail_off);
+      if (two) rec_load(q1, sl + 1280u, lane_row16, tail_off);
+      uint4 bh0 = make_uint4(0, 0, 0, 0), bl0 = bh0, bh1 = bh0, bl1 = bh0;
+      float x00 = 0.0f, x01 = 0.0f, x10 = 0.0f, x11 = 0.0f;
+      if (tok_ok) {
+        bh0 = lds128(xb_lane + gA * MT * 128u);
+        if (!PACK) bl0 = lds128(xb_lane + gA * MT * 128u + 16u);
+        bh1 = lds128(xb_lane + gB * MT * 128u);
+        if (!PACK) bl1 = lds128(xb_lane + gB * MT * 128u + 16u);
       }
+      if (xs_lane) {
+        if (2 * c < MT) { x00 = __uint_as_float(lds32(xs_addr + gA * MT * 4u)); x10 = __uint_as_float(lds32(xs_addr + gB * MT * 4u)); }
+        if (2 * c + 1 < MT) { x01 = __uint_as_float(lds32(xs_addr + gA * MT * 4u + 4u)); x11 = __uint_as_float(lds32(xs_addr + gB * MT * 4u + 4u)); }
+      }
+      // every lane has read the slot: lane 0 refills it (generic reads before the async-proxy write: warp sync, then a
+      // proxy fence); the math below uses registers only
+      __syncwarp();
+      if (lane == 0 && i_rec < r1) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue_next(cs);
+      }
+      if (++cs == nslot) { cs = 0; cph ^= 1u; }
+      rec_math<PACK>(acc[0], q0, bh0, bl0, x00, x01);
+      if (two) rec_math<PACK>(acc[1], q1, bh1, bl1, x10, x11);
     }
+    if (!ok) break;
+    rec = e;
+    // the segment ends at the end of its unit, at the end of the range, or (geglu) at the end of the gate half
+    uint32_t rf, rl;
+    v4_unit_range(pl, u, rf, rl);
+    if (PAIR && !in_up && e <= rl && e < r1) {   // gate half done, the up half follows in this warp
+      gate = totals();
+      zero();
+      in_up = true;
+      continue;
+    }
+    const bool whole = from_start && e == rl + 1u;
+    if (PAIR) {
+      V4Tot z;
+      clear(z);
+      if (in_up) v4_flush<MT, PAIR>(p, pl, gate, totals(), u, whole, w);
+      else v4_flush<MT, PAIR>(p, pl, totals(), z, u, whole, w);
+      clear(gate);
+    } else {
+      const V4Tot tt = totals();
+      v4_flush<MT, PAIR>(p, pl, tt, tt, u, whole, w);
+    }
+    zero();
   }
-  if (ok) {
-    // the last unit is whole for this warp when it began at the unit's first record and the range ends at its last
-    v4_flush<MT>(p, pl, totals(), u, from_start && cur.starts, w);
-  } else {
-    v4_arrive_only(pl, have ? u : cur.unit(pl), r1);
+  if (!ok) {
+    const uint32_t t = rec / Gt, j = rec - t * Gt;
+    v4_arrive_only(pl, t * pl.nsplit + (pl.nsplit > 1u ? j / pl.Gs : 0u), r1);
     // copies this warp issued but did not consume land before the CTA exits (bounded)
     if (lane == 0) {
       volatile uint32_t never = 0;
@@ -374,16 +387,18 @@ __global__ void __launch_bounds__(kV4Threads, 1) gemv_q4_v4(const __grid_constan
 }
 
 typedef void (*V4Kernel)(const GemvParams, const V4Plan);
-V4Kernel v4_kernel_for(uint32_t M) {
+template <int MT>
+V4Kernel v4_kernel_m(bool pair) { return pair ? gemv_q4_v4<MT, true> : gemv_q4_v4<MT, false>; }
+V4Kernel v4_kernel_for(uint32_t M, bool pair) {
   switch (M) {
-    case 1: return gemv_q4_v4<1>;
-    case 2: return gemv_q4_v4<2>;
-    case 3: return gemv_q4_v4<3>;
-    case 4: return gemv_q4_v4<4>;
-    case 5: return gemv_q4_v4<5>;
-    case 6: return gemv_q4_v4<6>;
-    case 7: return gemv_q4_v4<7>;
-    default: return gemv_q4_v4<8>;
+    case 1: return v4_kernel_m<1>(pair);
+    case 2: return v4_kernel_m<2>(pair);
+    case 3: return v4_kernel_m<3>(pair);
+    case 4: return v4_kernel_m<4>(pair);
+    case 5: return v4_kernel_m<5>(pair);
+    case 6: return v4_kernel_m<6>(pair);
+    case 7: return v4_kernel_m<7>(pair);
+    default: return v4_kernel_m<8>(pair);
   }
 }
 size_t v4_smem(uint32_t M, uint32_t G, uint32_t nslot) {
@@ -401,10 +416,11 @@ uint32_t v4_min_records() {
 
 bool v4_plan(const GemvParams &p, uint32_t nsplit, int sms, V4Plan *pl, size_t *scratch_bytes) {
   const uint32_t G = p.K / 32;
-  if (p.epi == P0_EPI_GEGLU || p.wG < G || G == 0) return false;
+  const bool pair = p.epi == P0_EPI_GEGLU;
+  if (p.wG < G || G == 0 || (pair && nsplit != 1)) return false;
   if ((uint64_t)G * p.M * 4 > (uint64_t)kV4XUnits * kV4Threads) return false;
-  const uint32_t ntile = p.N / 64, Gs = p.kPer / 32 < G ? p.kPer / 32 : G;
-  const uint64_t R = (uint64_t)ntile * G;
+  const uint32_t ntile = p.N / 64, Gt = pair ? 2 * G : G, Gs = pair ? Gt : (p.kPer / 32 < G ? p.kPer / 32 : G);
+  const uint64_t R = (uint64_t)ntile * Gt;
   if (R == 0 || R > 0x7fffffffull) return false;
   // warps: one per v4_min_records() records, at most 16 per SM, whole CTAs
   uint64_t nw = R / v4_min_records();
@@ -413,24 +429,25 @@ bool v4_plan(const GemvParams &p, uint32_t nsplit, int sms, V4Plan *pl, size_t *
   nw = nw / kV4Warps * kV4Warps;
   if (nw < (uint64_t)kV4Warps) nw = kV4Warps;
   if (nw > R) return false;   // fewer records than one CTA's warps: v2 handles it
-  const uint32_t per = (uint32_t)((R + nw - 1) / nw), stages = (per + 1) / 2;
+  const uint32_t per = (uint32_t)((R + nw - 1) / nw), stages = (per + 1) / 2 + 2;   // + segment ends
   uint32_t nslot = 0;
   for (uint32_t n = kV4MaxSlots; n >= 2; n--)
     if (v4_smem(p.M, G, n) <= 220u * 1024u) { nslot = n; break; }
   if (!nslot) return false;
-  if (nslot > stages) nslot = stages < 2 ? 2 : stages;
+  if (nslot > stages) nslot = stages;
   const uint32_t nunit = ntile * nsplit;
-  pl->R = (uint32_t)R; pl->G = G; pl->Gs = Gs; pl->nsplit = nsplit; pl->NW = (uint32_t)nw; pl->nslot = nslot;
+  pl->R = (uint32_t)R; pl->G = G; pl->Gt = Gt; pl->Gs = Gs; pl->nsplit = nsplit; pl->ntile = ntile; pl->NW = (uint32_t)nw;
+  pl->nslot = nslot;
   pl->cnt = nullptr;
   pl->part = nullptr;
-  *scratch_bytes = ((size_t)nunit + nw) * p.M * 64 * 4;
+  *scratch_bytes = ((size_t)nunit + nw) * (pair ? 2 : 1) * p.M * 64 * 4;
   return true;
 }
 
-size_t v4_counter_bytes(const V4Plan &pl) { return (size_t)pl.R / pl.G * pl.nsplit * 4; }
+size_t v4_counter_bytes(const V4Plan &pl) { return (size_t)pl.ntile * pl.nsplit * 4; }
 
 cudaError_t launch_v4(const GemvParams &p, const V4Plan &pl, cudaStream_t s) {
-  V4Kernel k = v4_kernel_for(p.M);
+  V4Kernel k = v4_kernel_for(p.M, pl.Gt != pl.G);
   const size_t smem = v4_smem(p.M, pl.G, pl.nslot);
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   k<<<pl.NW / kV4Warps, kV4Threads, smem, s>>>(p, pl);

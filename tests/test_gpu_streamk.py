@@ -133,3 +133,19 @@ def test_streamk_kslice_view(g, M, s0, s1):
     got = g.read(yb, 0, ns * M * N * 4, np.float32)
     want, _, _ = ref.gemvM(b, X, M, N, K, kPer=kPer)
     assert_close(got, want.reshape(K // kPer, M * N)[s0:s1].reshape(-1))
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 64, 2048), (8, 192, 416), (3, 8192, 2048), (2, 1024, 96)])
+def test_streamk_geglu(g, M, N, K):
+    # geglu units (the gate tile's records, then the up tile's) split across warps, some at the gate / up boundary
+    b, _ = ref.pack_q4(ref.randn(2 * N * K, 260 + K, 0.02), 2 * N, K)
+    X = ref.randn(M * K, 261)
+    nw = ref.randn(K, 262, 0.1) + 1
+    st = np.array([0.7 + 0.05 * m for m in range(M)], np.float32)
+    wb, xb = g.upload(b), g.upload(X)
+    yb = nan_buf(g, M * N * 4)
+    a = {"w": wview(wb, 2 * N, K), "x": {"buf": xb}, "M": M, "N": N, "K": K, "y": {"buf": yb}, "pro": "rms", "epi": "geglu",
+         "norm": {"buf": g.upload(nw), "off": 0}, "stat": {"buf": g.upload(st), "off": 0, "ld": 1}}
+    assert p0.gemvM(g, a) == 1
+    want, _, _ = ref.gemvM(b, X, M, N, K, pro="rms", epi="geglu", norm=nw, stat=st, stat_off=0, stat_ld=1)
+    assert_close(g.read(yb, 0, M * N * 4, np.float32), want)
