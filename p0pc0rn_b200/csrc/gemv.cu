@@ -548,19 +548,23 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
   p.xc = xc;
   cudaSetDevice(c->device);
   cudaError_t e;
-  // tuning override for comparisons: P0MM_GEMV=v2 or v3 keeps the newer kernels out of the dispatch
-  static const int newest = [] {
-    const char *s = getenv("P0MM_GEMV");
-    return s && !strcmp(s, "v2") ? 2 : s && !strcmp(s, "v3") ? 3 : 4;
-  }();
+  // tuning override, read on every call: P0MM_GEMV=v2 or v3 keeps the newer kernels out of the dispatch, v4 prefers v4
+  const char *force = getenv("P0MM_GEMV");
+  const int newest = force && !strcmp(force, "v2") ? 2 : force && !strcmp(force, "v3") ? 3 : force && !strcmp(force, "v4") ? 5 : 4;
+  // Measured on B200 (config-2 sweep and the config-5 chain, graph-launched): v3 leads wherever it fits (the head);
+  // v4 leads for M >= 5 on mid-sized calls (>= 8192 records, no geglu), where v2 needs two MMAs per k16 for hi / lo x;
+  // v2 leads on the rest. P0MM_GEMV=v4 prefers v4 wherever it fits.
   V4Plan pl{};
   size_t scratch_bytes = 0;
-  if (newest >= 4 && v4_plan(p, nsplit, c->sm_count, &pl, &scratch_bytes)) {
+  const bool v3ok = newest >= 3 && newest != 5 && v3_fits(M, K, nsplit, N / 64, c->sm_count);
+  const bool v4ok = newest >= 4 && !v3ok && v4_plan(p, nsplit, c->sm_count, &pl, &scratch_bytes) &&
+                    (newest == 5 || (M >= 5 && epi != P0_EPI_GEGLU && pl.R >= 8192u));
+  if (v4ok) {
     void *scratch = nullptr;
     if ((st = p0_workspace(c, v4_counter_bytes(pl), scratch_bytes, &pl.cnt, &scratch))) return st;
     pl.part = (float *)scratch;
     e = launch_v4(p, pl, c->stream);
-  } else if (newest >= 3 && v3_fits(M, K, nsplit, N / 64, c->sm_count)) e = launch_v3(p, c->sm_count, c->stream);
+  } else if (v3ok) e = launch_v3(p, c->sm_count, c->stream);
   else if (v2_fits(M, span)) e = launch_v2(p, nsplit, c->sm_count, c->stream);
   else e = launch_gemv(p, nsplit, c->stream);
   if ((st = p0_cuda(c, e, op))) return st;

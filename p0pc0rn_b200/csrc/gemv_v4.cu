@@ -251,16 +251,25 @@ __global__ void __launch_bounds__(kV4Threads, 1) gemv_q4_v4(const __grid_constan
   __syncwarp();
   // ---- the issue side (lane 0 only): the same segments, one or two records per slot (a slot never crosses a
   // segment). Stream record (t, j) sits at (t * wG + j) * 1280; geglu: j >= G is record j - G of up tile t + ntile.
-  uint32_t i_rec = r0, i_end = v4_seg_end(pl, r0, r1), issued = 0;
-  auto issue_next = [&](uint32_t slot) {
-    uint32_t t = i_rec / Gt, j = i_rec - t * Gt;
+  // Incremental: the address advances by 1280 per record inside a segment; divisions run only at segment starts.
+  auto seg_src = [&](uint32_t rec) -> const uint8_t * {
+    uint32_t t = rec / Gt, j = rec - t * Gt;
     if (PAIR && j >= G) { t += pl.ntile; j -= G; }
-    const uint8_t *src = p.W + ((size_t)t * p.wG + j) * 1280u;
-    const uint32_t n = i_end - i_rec >= 2u ? 2u : 1u;
+    return p.W + ((size_t)t * p.wG + j) * 1280u;
+  };
+  uint32_t i_rec = r0, i_left = v4_seg_end(pl, r0, r1) - r0, issued = 0;
+  const uint8_t *i_src = seg_src(r0);
+  auto issue_next = [&](uint32_t slot) {
+    const uint32_t n = i_left >= 2u ? 2u : 1u;
     tc::mbar_expect_tx(&myfull[slot], n * 1280u);
-    bulk_g2s(myring + (size_t)slot * kV4Slot, src, n * 1280u, &myfull[slot]);
+    bulk_g2s(myring + (size_t)slot * kV4Slot, i_src, n * 1280u, &myfull[slot]);
     i_rec += n;
-    if (i_rec == i_end && i_rec < r1) i_end = v4_seg_end(pl, i_rec, r1);
+    i_left -= n;
+    i_src += n * 1280u;
+    if (i_left == 0u && i_rec < r1) {
+      i_left = v4_seg_end(pl, i_rec, r1) - i_rec;
+      i_src = seg_src(i_rec);
+    }
     issued++;
   };
   if (lane == 0)
