@@ -122,6 +122,25 @@ typedef struct {
 } p0_gemvM_args;
 p0_status p0_gemvM(p0_ctx *ctx, const p0_gemvM_args *a, uint32_t *nsplit);
 
+/* gemvM without any device allocation. No counterpart in the reference (its WebGPU runtime has no such constraint).
+ * Same arguments, checks, outputs and error messages as p0_gemvM, always computed by the stream-K GEMV kernel.
+ * p0_gemvM keeps that kernel's counters and partial sums in a context workspace that it allocates on first use and
+ * re-allocates (cudaFree, which waits for the whole device, then cudaMalloc) when a larger call needs more. Callers
+ * that cannot allocate device memory in the middle of their work use this entry point instead: a decode loop with a
+ * latency budget that a device-wide wait would break, or a process whose device memory is all owned by another
+ * allocator (for example a framework's caching allocator that has reserved the HBM). The scratch lives in a
+ * file-scope device array of P0_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until the process
+ * exits: P0_NOALLOC_COUNTER_BYTES of per-unit arrival counters (one u32 per 64-row tile x k-split), cleared on the
+ * stream by each call, then the partial sums ((tiles x splits + warps of the grid) x halves x M x 64 floats, halves
+ * = 2 for geglu). A call that needs more returns P0_EINVAL and says how much; so does a call the stream-K kernel does
+ * not take (geglu with k-splits, weight columns < K, M*K > 16384, fewer than 16 weight records).
+ * The first call on each device looks up the array's device address; make that first call before any stream
+ * capture. Every call on a device shares the one array and keeps the last call's contents: calls whose kernels can
+ * overlap on the GPU (other streams, contexts or threads on the same device) race and give wrong results. */
+#define P0_NOALLOC_SCRATCH_BYTES (16u << 20)
+#define P0_NOALLOC_COUNTER_BYTES (64u << 10)
+p0_status p0_gemvM_noalloc(p0_ctx *ctx, const p0_gemvM_args *a, uint32_t *nsplit);
+
 /* ---------------------------------------------------------------------------------------------- GEMM */
 enum { P0_GEPI_F16 = 0, P0_GEPI_F32 = 1, P0_GEPI_BIAS = 2, P0_GEPI_RESADD = 3, P0_GEPI_SWIGLU = 4 };
 enum { P0_ACT_SILU = 0, P0_ACT_GELU = 1 };

@@ -502,7 +502,7 @@ const char *enc_name(uint32_t e) { return e == P0_ENC_Q4G32A_T64 ? "q4g32a.t64" 
 p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint32_t rowB, uint32_t ldx, uint32_t M, uint32_t N,
                    uint32_t K, uint32_t kPer, uint32_t nsplit, uint32_t pro, uint32_t epi, p0_buf yb, uint32_t ldy, uint32_t ldm,
                    p0_buf stb, uint32_t stat_off, uint32_t stat_ld, p0_buf nb, uint32_t norm_off, p0_buf eb, uint32_t ev_off,
-                   uint32_t ev_ld, uint32_t src_n, uint32_t src_ld, p0_buf mxb, float cap) {
+                   uint32_t ev_ld, uint32_t src_n, uint32_t src_ld, p0_buf mxb, float cap, bool noalloc = false) {
   p0_status st;
   const uint32_t G = 32;
   if (w.enc != P0_ENC_Q4G32A_T64) return p0_fail(c, P0_EINVAL, "%s: encoding %s is not built in this library yet", op, enc_name(w.enc));
@@ -556,6 +556,24 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
   // v2 leads on the rest. P0MM_GEMV=v4 prefers v4 wherever it fits.
   V4Plan pl{};
   size_t scratch_bytes = 0;
+  if (noalloc) {
+    // the allocation-free mode: the stream-K kernel with the fixed device array as its scratch
+    if (!v4_plan(p, nsplit, c->sm_count, &pl, &scratch_bytes))
+      return p0_fail(c, P0_EINVAL, "%s: this call does not fit the stream-K kernel (geglu with k-splits, weight columns < K, "
+                     "M*K > 16384 or fewer than 16 records)", op);
+    const size_t cnt_bytes = (v4_counter_bytes(pl) + 255) / 256 * 256;
+    if (cnt_bytes > P0_NOALLOC_COUNTER_BYTES || scratch_bytes > (size_t)P0_NOALLOC_SCRATCH_BYTES - P0_NOALLOC_COUNTER_BYTES)
+      return p0_fail(c, P0_EINVAL, "%s: needs %zu bytes of counters and %zu bytes of scratch; the fixed array holds %u and %u", op,
+                     cnt_bytes, scratch_bytes, P0_NOALLOC_COUNTER_BYTES, P0_NOALLOC_SCRATCH_BYTES - P0_NOALLOC_COUNTER_BYTES);
+    uint8_t *fixed = nullptr;
+    if ((st = p0_cuda(c, v4_noalloc_scratch(&fixed), op))) return st;
+    pl.cnt = (uint32_t *)fixed;
+    pl.part = (float *)(fixed + P0_NOALLOC_COUNTER_BYTES);
+    // the counters this call uses start at zero, whatever an earlier call left behind
+    if ((st = p0_cuda(c, cudaMemsetAsync(pl.cnt, 0, cnt_bytes, c->stream), op))) return st;
+    if ((st = p0_cuda(c, launch_v4(p, pl, c->stream), op))) return st;
+    return p0_launched(c, op);
+  }
   const bool v3ok = newest >= 3 && newest != 5 && v3_fits(M, K, nsplit, N / 64, c->sm_count);
   const bool v4ok = newest >= 4 && !v3ok && v4_plan(p, nsplit, c->sm_count, &pl, &scratch_bytes) &&
                     (newest == 5 || (M >= 5 && epi != P0_EPI_GEGLU && pl.R >= 8192u));
@@ -572,6 +590,30 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
 }
 
 }  // namespace
+
+// the checks and call of gemvM (lops_spec.js:163-191), shared by p0_gemvM and p0_gemvM_noalloc
+static p0_status gemvM_call(p0_ctx *c, const p0_gemvM_args *a, uint32_t *nsplit_out, bool noalloc) {
+  if (!c || !a) return P0_EINVAL;
+  const uint32_t enc = a->w.enc;
+  if (enc != P0_ENC_Q4G32A_T64 && enc != P0_ENC_Q8G64S_T64) return p0_fail(c, P0_EINVAL, "gemvM: encoding %s", enc_name(enc));
+  if (a->pro != P0_PRO_RAW && a->pro != P0_PRO_RMS && a->pro != P0_PRO_PLEG)
+    return p0_fail(c, P0_EINVAL, "gemvM: prologue %s", a->pro == P0_PRO_SUM ? "sum" : "?");
+  const uint32_t M = a->M, K = a->K, N = a->N, G = enc == P0_ENC_Q4G32A_T64 ? 32 : 64;
+  if (M < 1 || M > 8) return p0_fail(c, P0_EINVAL, "gemvM: M %u (1..8)", M);
+  const uint32_t kPer = a->kPer ? (a->kPer < 2048 ? a->kPer : 2048) : K;
+  if (kPer == 0 || kPer % G) return p0_fail(c, P0_EINVAL, "gemvM: kPer must be a multiple of %u", G);
+  const uint32_t nsplit = (K + kPer - 1) / kPer;
+  if (a->epi != P0_EPI_STORE && nsplit > 1) return p0_fail(c, P0_EINVAL, "gemvM: %s needs one split", epi_name(a->epi));
+  if (N % 64 || N == 0) return p0_fail(c, P0_EINVAL, "gemvM: N %% 64");
+  if (a->w.off % 4) return p0_fail(c, P0_EINVAL, "gemvM: weight offset");
+  const uint32_t ldm = a->ldm ? a->ldm : N, ldy = a->ldy ? a->ldy : M * ldm;
+  p0_status st = run_gemv(c, noalloc ? "gemvM_noalloc" : "gemvM", a->w, a->x, a->x_rowB, a->x_ldx ? a->x_ldx : K, M, N, K, kPer, nsplit, a->pro, a->epi, a->y, ldy,
+                          ldm, a->stat, a->stat_off, a->stat_ld ? a->stat_ld : 2, a->norm, a->norm_off, a->ev, a->ev_off, a->ev_ld,
+                          a->src_n ? a->src_n : 1, a->src_ld, a->mx, a->cap != 0.0f ? a->cap : 30.0f, noalloc);
+  if (st == P0_OK && nsplit_out) *nsplit_out = nsplit;
+  return st;
+}
+
 
 extern "C" {
 
@@ -600,26 +642,10 @@ p0_status p0_gemv(p0_ctx *c, const p0_gemv_args *a, uint32_t *nsplit_out) {
 }
 
 // gemvM(g, a) (lops_spec.js:163-191)
-p0_status p0_gemvM(p0_ctx *c, const p0_gemvM_args *a, uint32_t *nsplit_out) {
-  if (!c || !a) return P0_EINVAL;
-  const uint32_t enc = a->w.enc;
-  if (enc != P0_ENC_Q4G32A_T64 && enc != P0_ENC_Q8G64S_T64) return p0_fail(c, P0_EINVAL, "gemvM: encoding %s", enc_name(enc));
-  if (a->pro != P0_PRO_RAW && a->pro != P0_PRO_RMS && a->pro != P0_PRO_PLEG)
-    return p0_fail(c, P0_EINVAL, "gemvM: prologue %s", a->pro == P0_PRO_SUM ? "sum" : "?");
-  const uint32_t M = a->M, K = a->K, N = a->N, G = enc == P0_ENC_Q4G32A_T64 ? 32 : 64;
-  if (M < 1 || M > 8) return p0_fail(c, P0_EINVAL, "gemvM: M %u (1..8)", M);
-  const uint32_t kPer = a->kPer ? (a->kPer < 2048 ? a->kPer : 2048) : K;
-  if (kPer == 0 || kPer % G) return p0_fail(c, P0_EINVAL, "gemvM: kPer must be a multiple of %u", G);
-  const uint32_t nsplit = (K + kPer - 1) / kPer;
-  if (a->epi != P0_EPI_STORE && nsplit > 1) return p0_fail(c, P0_EINVAL, "gemvM: %s needs one split", epi_name(a->epi));
-  if (N % 64 || N == 0) return p0_fail(c, P0_EINVAL, "gemvM: N %% 64");
-  if (a->w.off % 4) return p0_fail(c, P0_EINVAL, "gemvM: weight offset");
-  const uint32_t ldm = a->ldm ? a->ldm : N, ldy = a->ldy ? a->ldy : M * ldm;
-  p0_status st = run_gemv(c, "gemvM", a->w, a->x, a->x_rowB, a->x_ldx ? a->x_ldx : K, M, N, K, kPer, nsplit, a->pro, a->epi, a->y, ldy,
-                          ldm, a->stat, a->stat_off, a->stat_ld ? a->stat_ld : 2, a->norm, a->norm_off, a->ev, a->ev_off, a->ev_ld,
-                          a->src_n ? a->src_n : 1, a->src_ld, a->mx, a->cap != 0.0f ? a->cap : 30.0f);
-  if (st == P0_OK && nsplit_out) *nsplit_out = nsplit;
-  return st;
-}
+p0_status p0_gemvM(p0_ctx *c, const p0_gemvM_args *a, uint32_t *nsplit_out) { return gemvM_call(c, a, nsplit_out, false); }
+
+// gemvM for callers that cannot allocate device memory during a call (no counterpart in the reference; the header
+// says why and what it costs): the stream-K kernel with its scratch in a fixed device array
+p0_status p0_gemvM_noalloc(p0_ctx *c, const p0_gemvM_args *a, uint32_t *nsplit_out) { return gemvM_call(c, a, nsplit_out, true); }
 
 }  // extern "C"

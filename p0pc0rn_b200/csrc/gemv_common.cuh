@@ -158,5 +158,8 @@ bool v4_plan(const GemvParams &p, uint32_t nsplit, int sms, V4Plan *pl, size_t *
 // bytes of arrival counters the plan needs (one u32 per unit)
 size_t v4_counter_bytes(const V4Plan &pl);
 cudaError_t launch_v4(const GemvParams &p, const V4Plan &pl, cudaStream_t s);
+// the device address of the allocation-free entry point's fixed scratch (P0_NOALLOC_SCRATCH_BYTES) on the current
+// device; looked up on a device's first call
+cudaError_t v4_noalloc_scratch(uint8_t **out);
 
 }  // namespace p0gemv

@@ -16,6 +16,7 @@
 // Unlike the whole-tile-per-warp v3 kernel, no warp idles while others finish a last tile (4096 head tiles over 2368
 // warps leave v3 a 1.73 : 2 load balance), and calls with few tiles still spread over many SMs.
 #include <cstdlib>
+#include <mutex>
 
 #include "gemv_common.cuh"
 
@@ -421,7 +422,30 @@ uint32_t v4_min_records() {
   }();
   return v;
 }
+// The allocation-free entry point's scratch (p0_gemvM_noalloc): counters first, then partial sums. Static device
+// storage starts zeroed when the library's module loads; each call still clears the counters it uses.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[P0_NOALLOC_SCRATCH_BYTES];
 }  // namespace
+
+// The device address of g_noalloc_scratch on the current device. The name is only a host-side stand-in for the
+// array, so the address comes from cudaGetSymbolAddress, called once per device (with that device current) and cached.
+cudaError_t v4_noalloc_scratch(uint8_t **out) {
+  static std::mutex mu;
+  static uint8_t *addr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[dev]) {
+    void *ptr = nullptr;
+    e = cudaGetSymbolAddress((void **)&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    addr[dev] = (uint8_t *)ptr;
+  }
+  *out = addr[dev];
+  return cudaSuccess;
+}
 
 bool v4_plan(const GemvParams &p, uint32_t nsplit, int sms, V4Plan *pl, size_t *scratch_bytes) {
   const uint32_t G = p.K / 32;

@@ -51,6 +51,19 @@ def gemv(g, a):
 
 def gemvM(g, a):
     """gemvM(g, a) -> nsplit (lops_spec.js:163-191)"""
+    return _gemvM(g, a, g._lib.p0_gemvM)
+
+
+def gemvM_noalloc(g, a):
+    """gemvM(g, a) -> nsplit without any device allocation during the call (no counterpart in the reference): for
+    callers that must not allocate mid-call, e.g. a latency-bound decode loop that cannot afford the device-wide wait
+    of a workspace re-allocation, or a process whose device memory belongs to another allocator. Its scratch is a
+    fixed 16 MiB device array shared by every call on the device, so calls that overlap on the GPU race; calls that
+    need more scratch raise P0Error (include/p0mm.h has the limits)."""
+    return _gemvM(g, a, g._lib.p0_gemvM_noalloc)
+
+
+def _gemvM(g, a, entry):
     x, y = a["x"], a["y"]
     stat, norm, ev, src, mx = a.get("stat"), a.get("norm"), a.get("ev"), a.get("src"), a.get("mx")
     pro, epi = a.get("pro") or "raw", a.get("epi") or "store"
@@ -65,7 +78,7 @@ def gemvM(g, a):
         _b(ev), int((ev or {}).get("off") or 0), int((ev or {}).get("ld") or 0), int((src or {}).get("n") or 0),
         int((src or {}).get("ld") or 0), _b(mx), float(a.get("cap") or 0.0))
     ns = ctypes.c_uint32()
-    g._check(g._lib.p0_gemvM(g.ctx, ctypes.byref(args), ctypes.byref(ns)))
+    g._check(entry(g.ctx, ctypes.byref(args), ctypes.byref(ns)))
     return ns.value
 
 
