@@ -548,13 +548,14 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
   p.xc = xc;
   cudaSetDevice(c->device);
   cudaError_t e;
-  // tuning override, read on every call: P0MM_GEMV=v2 or v3 keeps the newer kernels out of the dispatch, v4 prefers v4
+  // tuning override, read on every call: P0MM_GEMV=v2 | v3 | v4 | v5 runs that kernel wherever it fits
   const char *force = getenv("P0MM_GEMV");
-  const int newest = force && !strcmp(force, "v2") ? 2 : force && !strcmp(force, "v3") ? 3 : force && !strcmp(force, "v4") ? 5 : 4;
+  const int pick = force && force[0] == 'v' && force[1] >= '2' && force[1] <= '5' && !force[2] ? force[1] - '0' : 0;
   // Measured on B200 (config-2 sweep and the config-5 chain, graph-launched): v3 leads wherever it fits (the head);
-  // v4 leads for M >= 5 on mid-sized calls (>= 8192 records, no geglu), where v2 needs two MMAs per k16 for hi / lo x;
-  // v2 leads on the rest. P0MM_GEMV=v4 prefers v4 wherever it fits.
+  // v5 on the calls with few tiles it takes (N 2048: 5.8-7.0 us against v2's 8.0-15.6; N 16384: 9.1-20.5 against
+  // 16.4-20.6); v4 next for M >= 5 on mid-sized calls (>= 8192 records, no geglu); v2 on the rest.
   V4Plan pl{};
+  V5Plan p5{};
   size_t scratch_bytes = 0;
   if (noalloc) {
     // the allocation-free mode: the stream-K kernel with the fixed device array as its scratch
@@ -574,10 +575,22 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
     if ((st = p0_cuda(c, launch_v4(p, pl, c->stream), op))) return st;
     return p0_launched(c, op);
   }
-  const bool v3ok = newest >= 3 && newest != 5 && v3_fits(M, K, nsplit, N / 64, c->sm_count);
-  const bool v4ok = newest >= 4 && !v3ok && v4_plan(p, nsplit, c->sm_count, &pl, &scratch_bytes) &&
-                    (newest == 5 || (M >= 5 && epi != P0_EPI_GEGLU && pl.R >= 8192u));
-  if (v4ok) {
+  const bool v3fit = v3_fits(M, K, nsplit, N / 64, c->sm_count);
+  const bool v5fit = v5_plan(p, nsplit, c->sm_count, &p5);
+  const bool v4fit = v4_plan(p, nsplit, c->sm_count, &pl, &scratch_bytes);
+  bool v3ok, v4ok, v5ok;
+  if (pick) {
+    v3ok = pick == 3 && v3fit;
+    v4ok = pick == 4 && v4fit;
+    v5ok = pick == 5 && v5fit;
+  } else {
+    v3ok = v3fit;
+    v5ok = !v3ok && v5fit;
+    v4ok = !v3ok && !v5ok && v4fit && M >= 5 && epi != P0_EPI_GEGLU && pl.R >= 8192u;
+  }
+  if (v5ok) {
+    e = launch_v5(p, p5, c->stream);
+  } else if (v4ok) {
     void *scratch = nullptr;
     if ((st = p0_workspace(c, v4_counter_bytes(pl), scratch_bytes, &pl.cnt, &scratch))) return st;
     pl.part = (float *)scratch;

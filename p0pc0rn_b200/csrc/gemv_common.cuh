@@ -158,6 +158,19 @@ bool v4_plan(const GemvParams &p, uint32_t nsplit, int sms, V4Plan *pl, size_t *
 // bytes of arrival counters the plan needs (one u32 per unit)
 size_t v4_counter_bytes(const V4Plan &pl);
 cudaError_t launch_v4(const GemvParams &p, const V4Plan &pl, cudaStream_t s);
+// the v5 (cluster) kernels, in gemv_v5.cu
+struct V5Plan {
+  uint32_t CS;      // CTAs per unit (thread-block cluster size, 1..8)
+  uint32_t nsplit, Gs, G, ntile;
+  uint32_t pair;    // geglu: ranks < CS/2 read the gate tile, the others the up tile
+  uint32_t nmax;    // records per CTA at most
+  uint32_t units;   // output units: tiles x k-splits (geglu: tiles)
+};
+// false when the call does not fit v5 (too many tiles for it to lead, weight columns < K, staged x or records too
+// large for shared memory); else fills the plan
+bool v5_plan(const GemvParams &p, uint32_t nsplit, int sms, V5Plan *pl);
+cudaError_t launch_v5(const GemvParams &p, const V5Plan &pl, cudaStream_t s);
+
 // the device address of the allocation-free entry point's fixed scratch (P0_NOALLOC_SCRATCH_BYTES) on the current
 // device; looked up on a device's first call
 cudaError_t v4_noalloc_scratch(uint8_t **out);

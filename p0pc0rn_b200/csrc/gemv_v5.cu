@@ -1,0 +1,329 @@
+// gemv_v5.cu -- the cluster GEMV for calls with few tiles (the decode chain's QKV / O / FFN / down projections and the
+// small config-2 calls), where the whole call is a few MB and its time is latency, not bandwidth.
+//
+// One output unit (a 64-row tile x k-split, or a geglu gate tile with its up tile) per thread-block cluster of CS CTAs.
+// CTA `rank` of the cluster takes a contiguous slice of the unit's records (geglu: ranks < CS/2 slices of the gate
+// tile, the others of the up tile). Every warp bulk-copies its share of the slice into shared memory at once (one
+// DRAM round trip for the whole call), while the CTA stages its slice of x in one pass. The warps run the v2/v3
+// arithmetic (codes as exact fp16 subnormals on mma.sync, x as fp16 hi/lo, acc += s * D + mn * sum(x) per group), sum
+// their partials in shared memory in warp order, and rank 0 of the cluster sums the CTAs' partials through distributed
+// shared memory in rank order and applies the epilogue. No global scratch, no atomics: the result does not depend on
+// timing.
+#include "gemv_common.cuh"
+
+namespace p0gemv {
+namespace {
+
+constexpr int kV5Warps = 8;
+constexpr int kV5Threads = 32 * kV5Warps;
+constexpr uint32_t kV5XUnits = 4;   // staged x: units of 8 k per thread, kept in registers across the sigma reduction
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// every CTA of the cluster has arrived (its shared-memory writes before the arrive are visible to the others)
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// a float from CTA `rank`'s shared memory at this CTA's shared address `saddr`
+__device__ __forceinline__ float ld_dsmem(uint32_t saddr, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(saddr), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+  return v;
+}
+
+// x of groups [gx, gx + n) of one slice, staged in one pass (the v4 staging): B fragments (fp16 hi / lo, permuted k
+// order) and per-(group, token) sum(x) / f, indexed by the group's position in the slice. Returns f = 2^24 / sigma.
+template <int MT>
+__device__ float stage_x_v5(const GemvParams &p, uint32_t gx, uint32_t n, uint4 *xb, float *xsum, float *red) {
+  constexpr uint32_t T = kV5Threads;
+  const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+  const uint32_t units = n * MT * 4;   // <= kV5XUnits * T (host-checked)
+  float v[kV5XUnits][8];
+  float mx = 0.0f;
+#pragma unroll
+  for (uint32_t j = 0; j < kV5XUnits; j++) {
+    const uint32_t u = t + j * T;
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[j][i] = 0.0f;
+    if (u < units) {
+      const uint32_t gg = u / (MT * 4), rem = u - gg * (MT * 4), m = rem >> 2, c = rem & 3u;
+      const uint32_t kb = (gx + gg) * 32 + c * 8;
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        v[j][i] = prologue(p, m, kb + i);
+        mx = fmaxf(mx, fabsf(v[j][i]));
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int w = 1; w < kV5Warps; w++) mx = fmaxf(mx, red[w]);
+  int e = 0;
+  if (mx > 0.0f && mx < INFINITY) frexpf(mx, &e);
+  const float sigma = ldexpf(1.0f, 14 - e), f = ldexpf(1.0f, 10 + e), finv = ldexpf(1.0f, -10 - e);
+#pragma unroll
+  for (uint32_t j = 0; j < kV5XUnits; j++) {
+    const uint32_t u = t + j * T;
+    float part = 0.0f;
+    if (u < units) {
+      float hv[8], lv[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        part += v[j][i];
+        const float vs = v[j][i] * sigma * ((i & 1) ? 0.0625f : 1.0f);
+        const float h = __half2float(__float2half_rn(vs));
+        hv[i] = h;
+        lv[i] = vs - h;
+      }
+      xb[u * 2] = make_uint4(pack_h2(hv[0], hv[4]), pack_h2(hv[1], hv[5]), pack_h2(hv[2], hv[6]), pack_h2(hv[3], hv[7]));
+      xb[u * 2 + 1] = make_uint4(pack_h2(lv[0], lv[4]), pack_h2(lv[1], lv[5]), pack_h2(lv[2], lv[6]), pack_h2(lv[3], lv[7]));
+    }
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    if (u < units && (u & 3u) == 0) xsum[u >> 2] = part * finv;
+  }
+  __syncthreads();
+  return f;
+}
+
+size_t v5_smem(uint32_t M, uint32_t nmax) {
+  return (size_t)nmax * 1280 + (size_t)nmax * M * 128 + (size_t)nmax * M * 4 + (size_t)kV5Warps * M * 64 * 4 + (size_t)M * 64 * 4 +
+         kV5Warps * 8 + 64 * 4;
+}
+
+template <int MT, bool PAIR>
+__global__ void __launch_bounds__(kV5Threads, 2) gemv_q4_v5(const __grid_constant__ GemvParams p, const __grid_constant__ V5Plan pl) {
+  constexpr bool PACK = MT <= 4;
+  extern __shared__ __align__(128) uint8_t smem8[];
+  const uint32_t CS = pl.CS, rank = CS > 1u ? cluster_rank() : 0u, unit = blockIdx.x / CS;
+  // ---- this CTA's slice: records [j0, j1) of tile `wt` (the weight tile it reads), groups gx.. of x
+  uint32_t tile, split = 0, j0, j1, wt;
+  if (PAIR) {
+    const uint32_t hr = CS / 2u, half = rank / hr, rr = rank - half * hr;
+    tile = unit;
+    j0 = rr * pl.G / hr;
+    j1 = (rr + 1u) * pl.G / hr;
+    wt = tile + half * pl.ntile;
+  } else {
+    tile = unit / pl.nsplit;
+    split = unit - tile * pl.nsplit;
+    const uint32_t u0 = split * pl.Gs, nu = min(u0 + pl.Gs, pl.G) - u0;
+    j0 = u0 + rank * nu / CS;
+    j1 = u0 + (rank + 1u) * nu / CS;
+    wt = tile;
+  }
+  const uint32_t n = j1 - j0;   // >= 1 (host-checked)
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem8);                        // [warps]
+  float *misc = reinterpret_cast<float *>(bars + kV5Warps);                    // 64 floats
+  volatile uint32_t *abort_flag = reinterpret_cast<volatile uint32_t *>(misc + 32);
+  uint8_t *recs = reinterpret_cast<uint8_t *>(misc + 64);                      // [nmax] x 1280 B (16-byte aligned)
+  uint4 *xb = reinterpret_cast<uint4 *>(recs + (size_t)pl.nmax * 1280u);     // [nmax][MT][4][2]
+  float *xsum = reinterpret_cast<float *>(xb + (size_t)pl.nmax * MT * 8);     // [nmax][MT]
+  float *red = xsum + (size_t)pl.nmax * MT;                                   // [warps][MT][64]
+  float *part = red + kV5Warps * MT * 64;                                     // [MT][64]: this CTA's slice total
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t g = lane >> 2, c = lane & 3;
+  // ---- every warp copies its share of the slice at once
+  const uint32_t wa = warp * n / kV5Warps, wb = (warp + 1u) * n / kV5Warps, wn = wb - wa;
+  if (lane == 0) {
+    tc::mbar_init(&bars[warp], 1);
+    tc::fence_mbar_init();
+  }
+  if (threadIdx.x == 0) *abort_flag = 0u;
+  __syncwarp();
+  if (lane == 0 && wn) {
+    tc::mbar_expect_tx(&bars[warp], wn * 1280u);
+    bulk_g2s(recs + (size_t)wa * 1280u, p.W + ((size_t)wt * p.wG + j0 + wa) * 1280u, wn * 1280u, &bars[warp]);
+  }
+  const float f = stage_x_v5<MT>(p, j0, n, xb, xsum, misc);   // j0 is also the slice's first group of x
+
+  // ---- the warp's records: pairs, both loaded before the math (the v3 loop)
+  const uint32_t btok = PACK ? (g & 3u) : g, bsel = PACK ? (g >> 2) : 0u;
+  const bool tok_ok = btok < MT, xs_lane = !PACK || c < 2;
+  const uint32_t rec_s = tc::smem_u32(recs), xb_s = tc::smem_u32(xb), xsum_s = tc::smem_u32(xsum);
+  const uint32_t lane_row16 = (uint32_t)lane * 16u, tail_off = 1024u + g * 4u;
+  const uint32_t xb_lane = xb_s + btok * 128u + c * 32u + bsel * 16u, xs_addr = xsum_s + 2u * c * 4u;
+  float acc[2][4][4];
+#pragma unroll
+  for (int h = 0; h < 2; h++)
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) acc[h][r][i] = 0.0f;
+  bool ok = true;
+  if (wn) {
+    const bool got = tc::mbar_wait(&bars[warp], 0, abort_flag, p.err, 0x711u, P0_SPIN_LIMIT);
+    ok = __all_sync(0xffffffffu, got);
+    for (uint32_t k = 0; ok && k < wn; k += 2) {
+      const uint32_t gA = wa + k, gB = k + 1u < wn ? gA + 1u : gA;   // positions in the slice
+      const bool two = k + 1u < wn;
+      Rec q0, q1;
+      rec_load(q0, rec_s + gA * 1280u, lane_row16, tail_off);
+      if (two) rec_load(q1, rec_s + gB * 1280u, lane_row16, tail_off);
+      uint4 bh0 = make_uint4(0, 0, 0, 0), bl0 = bh0, bh1 = bh0, bl1 = bh0;
+      float x00 = 0.0f, x01 = 0.0f, x10 = 0.0f, x11 = 0.0f;
+      if (tok_ok) {
+        bh0 = lds128(xb_lane + gA * MT * 128u);
+        if (!PACK) bl0 = lds128(xb_lane + gA * MT * 128u + 16u);
+        bh1 = lds128(xb_lane + gB * MT * 128u);
+        if (!PACK) bl1 = lds128(xb_lane + gB * MT * 128u + 16u);
+      }
+      if (xs_lane) {
+        if (2 * c < MT) { x00 = __uint_as_float(lds32(xs_addr + gA * MT * 4u)); x10 = __uint_as_float(lds32(xs_addr + gB * MT * 4u)); }
+        if (2 * c + 1 < MT) { x01 = __uint_as_float(lds32(xs_addr + gA * MT * 4u + 4u)); x11 = __uint_as_float(lds32(xs_addr + gB * MT * 4u + 4u)); }
+      }
+      rec_math<PACK>(acc[0], q0, bh0, bl0, x00, x01);
+      if (two) rec_math<PACK>(acc[1], q1, bh1, bl1, x10, x11);
+    }
+  }
+  // ---- the warp's totals (x f; PACK: hi + lo columns) -> red[warp][m][row]
+  const bool holder = !PACK || c < 2u;
+#pragma unroll
+  for (int r = 0; r < 4; r++)
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      float v = (acc[0][r][i] + acc[1][r][i]) * f;
+      if (PACK) v += __shfl_xor_sync(0xffffffffu, v, 2);
+      const uint32_t row = 16u * r + g + (i >= 2 ? 8u : 0u), m = 2u * c + (i & 1);
+      if (holder && m < MT) red[(warp * MT + m) * 64u + row] = v;
+    }
+  __syncthreads();
+  // the CTA's slice total, summed in warp order
+  for (uint32_t idx = threadIdx.x; idx < MT * 64u; idx += kV5Threads) {
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kV5Warps; w++) s += red[w * MT * 64u + idx];
+    part[idx] = s;
+  }
+  if (CS > 1u) cluster_sync();
+  else __syncthreads();
+  // ---- rank 0: the unit's total (the ranks' parts in rank order; geglu: gate ranks, then up ranks) and the epilogue;
+  // warp m takes token m, lane l rows l and l + 32
+  if (rank == 0u && warp < MT && ok && !*abort_flag) {
+    const uint32_t m = warp, part_s = tc::smem_u32(part);
+    float t[2], u2[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const uint32_t idx = m * 64u + lane + 32u * h;
+      if (PAIR) {
+        const uint32_t hr = CS / 2u;
+        float a = part[idx], b = 0.0f;
+        for (uint32_t r = 1; r < hr; r++) a += ld_dsmem(part_s + idx * 4u, r);
+        for (uint32_t r = hr; r < CS; r++) b += ld_dsmem(part_s + idx * 4u, r);
+        t[h] = a;
+        u2[h] = b;
+      } else {
+        float a = part[idx];
+        for (uint32_t r = 1; r < CS; r++) a += ld_dsmem(part_s + idx * 4u, r);
+        t[h] = a;
+      }
+    }
+    const uint32_t R0 = tile * 64u;
+    if (PAIR) {
+#pragma unroll
+      for (int h = 0; h < 2; h++) p.Y[(size_t)m * p.ldm + R0 + lane + 32u * h] = __fmul_rn(gelu_l(t[h]), u2[h]);
+    } else if (p.epi == P0_EPI_SOFTCAP) {
+      float bv = -INFINITY;
+      uint32_t bi = 0xffffffffu;
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const float v = __fmul_rn(p.cap, tanhf(fminf(15.0f, fmaxf(-15.0f, __fdiv_rn(t[h], p.cap)))));
+        p.Y[(size_t)m * p.ldm + R0 + lane + 32u * h] = v;
+        if (v > bv) { bv = v; bi = lane + 32u * h; }   // h = 0 first: ties keep the lower row
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      if (lane == 0) {
+        const size_t o = ((size_t)m * p.ntile + tile) * 2;
+        p.MX[o] = bv;
+        p.MX[o + 1] = __uint_as_float(R0 + bi);
+      }
+    } else {
+#pragma unroll
+      for (int h = 0; h < 2; h++) p.Y[(size_t)split * p.ldy + (size_t)m * p.ldm + R0 + lane + 32u * h] = t[h];
+    }
+  }
+  // the other CTAs' shared memory stays in place until rank 0 has read it
+  if (CS > 1u) cluster_sync();
+  // a copy whose wait gave up lands before the CTA exits (bounded)
+  if (!ok && lane == 0 && wn) {
+    volatile uint32_t never = 0;
+    tc::mbar_wait(&bars[warp], 0, &never, p.err, 0x712u, P0_SPIN_LIMIT);
+  }
+}
+
+typedef void (*V5Kernel)(const GemvParams, const V5Plan);
+template <int MT>
+V5Kernel v5_kernel_m(bool pair) { return pair ? gemv_q4_v5<MT, true> : gemv_q4_v5<MT, false>; }
+V5Kernel v5_kernel_for(uint32_t M, bool pair) {
+  switch (M) {
+    case 1: return v5_kernel_m<1>(pair);
+    case 2: return v5_kernel_m<2>(pair);
+    case 3: return v5_kernel_m<3>(pair);
+    case 4: return v5_kernel_m<4>(pair);
+    case 5: return v5_kernel_m<5>(pair);
+    case 6: return v5_kernel_m<6>(pair);
+    case 7: return v5_kernel_m<7>(pair);
+    default: return v5_kernel_m<8>(pair);
+  }
+}
+}  // namespace
+
+bool v5_plan(const GemvParams &p, uint32_t nsplit, int sms, V5Plan *pl) {
+  const uint32_t G = p.K / 32;
+  const bool pair = p.epi == P0_EPI_GEGLU;
+  if (G == 0 || p.wG < G || (pair && nsplit != 1)) return false;
+  const uint32_t ntile = p.N / 64, Gs = p.kPer / 32 < G ? p.kPer / 32 : G;
+  const uint64_t units = pair ? ntile : (uint64_t)ntile * nsplit;
+  const uint32_t nu = pair ? G : Gs;   // records per unit (per half for geglu)
+  // the smallest cluster that gives every SM a CTA, within the staging and shared-memory limits
+  uint32_t best = 0;
+  for (uint32_t CS = pair ? 2u : 1u; CS <= 8u; CS *= 2u) {
+    const uint32_t parts = pair ? CS / 2u : CS;
+    if (parts > nu) break;
+    const uint32_t nmax = (nu + parts - 1) / parts;
+    if (nmax * p.M * 4 > kV5XUnits * kV5Threads || v5_smem(p.M, nmax) > 200u * 1024u) continue;
+    best = CS;
+    if (units * CS >= (uint64_t)sms) break;
+  }
+  if (!best || units * best > (uint64_t)sms * 8) return false;   // many tiles: the streaming kernels take them
+  const uint32_t parts = pair ? best / 2u : best;
+  pl->CS = best; pl->nsplit = nsplit; pl->Gs = Gs; pl->G = G; pl->ntile = ntile; pl->pair = pair;
+  pl->nmax = (nu + parts - 1) / parts;
+  pl->units = (uint32_t)units;
+  return true;
+}
+
+cudaError_t launch_v5(const GemvParams &p, const V5Plan &pl, cudaStream_t s) {
+  V5Kernel k = v5_kernel_for(p.M, pl.pair != 0);
+  const size_t smem = v5_smem(p.M, pl.nmax);
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.units * pl.CS);
+  cfg.blockDim = dim3(kV5Threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = pl.CS;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, p, pl);
+}
+
+}  // namespace p0gemv
