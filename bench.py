@@ -236,6 +236,8 @@ def run_ours(args, ws, rank, local):
     g.set_stream(stream.cuda_stream)
     sw = Sweep(g, torch, ws, rank)
     torch.cuda.synchronize()
+    # the weights are packed and synchronised: GEMVs may fetch them while the call ahead finishes (p0_set_overlap)
+    g.set_overlap(True)
     # one gather buffer: every call's outputs of this rank, concatenated; one all-gather per step
     gather_src = torch.empty(sw.out_floats, dtype=torch.float32, device="cuda")
     gather_dst = torch.empty(sw.out_floats * ws, dtype=torch.float32, device="cuda")

@@ -47,6 +47,14 @@ p0_status p0_destroy(p0_ctx *ctx);
 /* run subsequent work on an external cudaStream_t (NULL = the context's own stream; pass cudaStreamLegacy for CUDA's
  * legacy default stream, whose handle 0 would otherwise mean "own stream") */
 p0_status p0_set_stream(p0_ctx *ctx, void *cuda_stream);
+/* Consecutive GEMV calls on the context's stream always overlap their launch with the call ahead (programmatic
+ * dependent launch: a call waits for the work ahead before it reads x or writes anything). With P0_OVERLAP_WEIGHTS set
+ * a call also starts fetching its weights before the work ahead has finished; the caller then guarantees that no work
+ * still in flight on the stream writes a weight buffer a later GEMV reads (weights written once, then the stream
+ * synchronised, as a loaded model's are). No counterpart in the reference, whose WebGPU queue runs dispatches in
+ * order. Default: 0. */
+enum { P0_OVERLAP_WEIGHTS = 1 };
+p0_status p0_set_overlap(p0_ctx *ctx, uint32_t flags);
 /* the message of the last failed call, in the reference's wording (e.g. "gemv: N % 64") */
 p0_status p0_last_error(p0_ctx *ctx, char *msg, size_t cap);
 /* byte accounting (gpu.js:28, 81-96) and dispatch counter (Runner, gpu.js:177-179) */

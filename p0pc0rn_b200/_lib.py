@@ -19,10 +19,11 @@ GEPI = {"f16": 0, "f32": 1, "bias": 2, "resadd": 3, "swiglu": 4}
 ACT = {"silu": 0, "gelu": 1}
 
 # every symbol include/p0mm.h declares
-EXPORTS = ["p0_init", "p0_destroy", "p0_set_stream", "p0_last_error", "p0_stats", "p0_buffer", "p0_wrap", "p0_upload", "p0_read",
+EXPORTS = ["p0_init", "p0_destroy", "p0_set_stream", "p0_set_overlap", "p0_last_error", "p0_stats", "p0_buffer", "p0_wrap", "p0_upload", "p0_read",
            "p0_free", "p0_done", "p0_device_ptr", "p0_gemv", "p0_gemvM", "p0_gemvM_noalloc", "p0_gemm", "p0_pack_q4",
            "p0_dequant_f16", "p0_version"]
 P0_NOALLOC_SCRATCH_BYTES = 16 << 20   # include/p0mm.h
+P0_OVERLAP_WEIGHTS = 1
 P0_NOALLOC_COUNTER_BYTES = 64 << 10
 
 
@@ -74,6 +75,7 @@ def load():
     L.p0_init.argtypes = [ctypes.c_int, ctypes.POINTER(vp)]
     L.p0_destroy.argtypes = [vp]
     L.p0_set_stream.argtypes = [vp, vp]
+    L.p0_set_overlap.argtypes = [vp, ctypes.c_uint32]
     L.p0_last_error.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t]
     L.p0_stats.argtypes = [vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]
     L.p0_buffer.argtypes = [vp, ctypes.c_size_t, ctypes.c_char_p, ctypes.POINTER(p0_buf)]

@@ -79,6 +79,13 @@ p0_status p0_set_stream(p0_ctx *c, void *s) {
   return P0_OK;
 }
 
+p0_status p0_set_overlap(p0_ctx *c, uint32_t flags) {
+  if (!c) return P0_EINVAL;
+  if (flags & ~(uint32_t)P0_OVERLAP_WEIGHTS) return p0_fail(c, P0_EINVAL, "set_overlap: unknown flags 0x%x", flags);
+  c->overlap = (flags & P0_OVERLAP_WEIGHTS) != 0;
+  return P0_OK;
+}
+
 p0_status p0_last_error(p0_ctx *c, char *msg, size_t cap) {
   if (!c || !msg || !cap) return P0_EINVAL;
   snprintf(msg, cap, "%s", c->last_error.c_str());

@@ -55,6 +55,8 @@ __global__ void __launch_bounds__(kThreads) gemv_q4_v1(const GemvParams p) {
     for (int r = 0; r < 2; r++)
 #pragma unroll
       for (int m = 0; m < MT; m++) acc[a][r][m] = 0.0f;
+  pdl_wait();
+  pdl_trigger();
 
   for (uint32_t kc = k0; kc < k1; kc += XC) {
     const uint32_t kc1 = min(k1, kc + XC), len = kc1 - kc, ngr = len / 32;
@@ -254,6 +256,8 @@ __global__ void __launch_bounds__(kThreads) gemv_q4_v2(const GemvParams p, const
   uint32_t G = 0;
   const size_t pair_off = (size_t)(p.N / 64u) * p.wG * 1280u;   // geglu: the up rows' tiles follow the gate rows' tiles
   const bool tok_ok = (uint32_t)g < MT;                          // B column n = g is a real token
+  pdl_wait();
+  pdl_trigger();
   for (uint32_t item = blockIdx.x; item < plan.nitems; item += gridDim.x) {
     const uint32_t split = item / plan.items_per_split, it = item - split * plan.items_per_split;
     const uint32_t k0 = split * p.kPer, k1 = min(p.K, k0 + p.kPer);
@@ -459,8 +463,7 @@ cudaError_t launch_v2(const GemvParams &p, uint32_t nsplit, int sms, cudaStream_
   pl.items_per_split = nrb / (bRW * pl.units_per_item);
   pl.nitems = pl.items_per_split * nsplit;
   const uint32_t grid = bslots < pl.nitems ? bslots : pl.nitems;
-  v2_kernel_for(p.M, pair, bRW)<<<grid, kThreads, smem, s>>>(p, pl);
-  return cudaGetLastError();
+  return launch_pdl(v2_kernel_for(p.M, pair, bRW), dim3(grid), dim3(kThreads), smem, s, 1, p, pl);
 }
 
 template <int MT>
@@ -468,13 +471,12 @@ cudaError_t launch_mt(const GemvParams &p, dim3 grid, size_t smem, cudaStream_t 
   if (p.epi == P0_EPI_GEGLU) {
     auto k = gemv_q4_v1<MT, true>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k<<<grid, kThreads, smem, s>>>(p);
+    return launch_pdl(k, grid, dim3(kThreads), smem, s, 1, p);
   } else {
     auto k = gemv_q4_v1<MT, false>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k<<<grid, kThreads, smem, s>>>(p);
+    return launch_pdl(k, grid, dim3(kThreads), smem, s, 1, p);
   }
-  return cudaGetLastError();
 }
 
 cudaError_t launch_gemv(const GemvParams &p, uint32_t nsplit, cudaStream_t s) {
@@ -540,7 +542,7 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
   p.NW = (const float *)rn.base; p.EV = (const float *)re.base; p.ST = (const float *)rs.base; p.MX = (float *)rm.base;
   p.M = M; p.N = N; p.K = K; p.wG = wG; p.kPer = kPer; p.ldy = ldy; p.ldm = ldm; p.ldx = ldx; p.rowB = rowB;
   p.nOff = norm_off; p.statOff = stat_off; p.statLd = stat_ld; p.evOff = ev_off; p.evLd = ev_ld; p.ldp = src_ld; p.nsrc = src_n;
-  p.ntile = NT; p.cap = cap; p.pro = (int)pro; p.epi = (int)epi; p.err = c->d_err;
+  p.ntile = NT; p.cap = cap; p.pro = (int)pro; p.epi = (int)epi; p.err = c->d_err; p.overlap = c->overlap ? 1 : 0;
   // staged x per chunk: <= 32 KB of x rows, whole groups
   uint32_t xc = (8192u / M) / 32u * 32u;
   uint32_t span = kPer < K ? kPer : K;

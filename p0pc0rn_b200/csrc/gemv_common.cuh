@@ -24,8 +24,41 @@ struct GemvParams {
   uint32_t M, N, K, wG, kPer, ldy, ldm, ldx, rowB, nOff, statOff, statLd, evOff, evLd, ldp, nsrc, ntile, xc;
   float cap;
   int pro, epi;
+  int overlap;       // the weights are not written by work ahead on the stream: copies may start before pdl_wait()
   uint32_t *err;
 };
+
+// Programmatic dependent launch. Every GEMV is launched so that it may start while the kernel ahead of it on the
+// stream is still running; it calls pdl_wait() before it touches anything an earlier kernel may write (x, the norm /
+// stat / pleg vectors, its outputs, the workspace), and pdl_trigger() as soon as its own loads are under way, so that
+// the next call can start too. Without such a launch both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// a kernel launch with the programmatic-dependent-launch attribute (and a cluster shape when cluster > 1)
+template <typename Kern, typename... Args>
+cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t s, uint32_t cluster, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[2];
+  unsigned n = 0;
+  at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[n].val.programmaticStreamSerializationAllowed = 1;
+  n++;
+  if (cluster > 1) {
+    at[n].id = cudaLaunchAttributeClusterDimension;
+    at[n].val.clusterDim.x = cluster;
+    at[n].val.clusterDim.y = 1;
+    at[n].val.clusterDim.z = 1;
+    n++;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
 
 __device__ __forceinline__ uint4 ldg_stream(const void *p) {
   uint4 v;
@@ -110,7 +143,8 @@ __device__ __forceinline__ void rec_load(Rec &q, uint32_t rec, uint32_t lane_row
 }
 // the code MMAs and acc += s * D + mn * sum(x) for the 4 row-blocks (xs0 / xs1: this lane's x sums, 0 where they do
 // not apply)
-template <bool PACK>
+// (MT == 1: the odd D columns, tokens 1 and 3 in the packed layout, are empty for every lane; their updates are skipped)
+template <int MT, bool PACK>
 __device__ __forceinline__ void rec_math(float (&acc)[4][4], const Rec &q, const uint4 bh, const uint4 bl, float xs0, float xs1) {
 #pragma unroll
   for (int r = 0; r < 4; r++) {
@@ -128,9 +162,11 @@ __device__ __forceinline__ void rec_math(float (&acc)[4][4], const Rec &q, const
     const __half2 h0 = *reinterpret_cast<const __half2 *>(&q.t[r][0]), h1 = *reinterpret_cast<const __half2 *>(&q.t[r][1]);
     const float s0 = __low2float(h0), m0 = __high2float(h0), s1 = __low2float(h1), m1 = __high2float(h1);
     acc[r][0] = fmaf(s0, d[0], fmaf(m0, xs0, acc[r][0]));
-    acc[r][1] = fmaf(s0, d[1], fmaf(m0, xs1, acc[r][1]));
     acc[r][2] = fmaf(s1, d[2], fmaf(m1, xs0, acc[r][2]));
-    acc[r][3] = fmaf(s1, d[3], fmaf(m1, xs1, acc[r][3]));
+    if (MT > 1) {
+      acc[r][1] = fmaf(s0, d[1], fmaf(m0, xs1, acc[r][1]));
+      acc[r][3] = fmaf(s1, d[3], fmaf(m1, xs1, acc[r][3]));
+    }
   }
 }
 

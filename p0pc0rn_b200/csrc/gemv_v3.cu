@@ -120,9 +120,12 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
     issued++;
     if (++ni_s == spt) { ni_s = 0; ni_t++; ni_src += ustride_bytes; }
   };
-  // the first copies fly while x is staged
+  // the first copies fly while x is staged (and, when the weights are static, while the call ahead finishes)
+  if (!p.overlap) pdl_wait();
   if (lane == 0)
     for (uint32_t j = 0; j < nslot && j < nstage; j++) issue_next(j);
+  pdl_trigger();
+  if (p.overlap) pdl_wait();
   const float f = stage_x_v3<MT>(p, G, xb, xsum, scratch);
 
   const uint32_t btok = PACK ? (g & 3u) : g, bsel = PACK ? (g >> 2) : 0u;   // B column of this lane
@@ -178,11 +181,11 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
       }
       if (++cs == nslot) { cs = 0; cph ^= 1u; }
       if (PAIR) {
-        rec_math<PACK>(acc[0][0], q0, bh0, bl0, x00, x01);
-        rec_math<PACK>(acc[1][NP - 1], q1, bh0, bl0, x00, x01);
+        rec_math<MT, PACK>(acc[0][0], q0, bh0, bl0, x00, x01);
+        rec_math<MT, PACK>(acc[1][NP - 1], q1, bh0, bl0, x00, x01);
       } else {
-        rec_math<PACK>(acc[0][0], q0, bh0, bl0, x00, x01);
-        if (two) rec_math<PACK>(acc[1][0], q1, bh1, bl1, x10, x11);
+        rec_math<MT, PACK>(acc[0][0], q0, bh0, bl0, x00, x01);
+        if (two) rec_math<MT, PACK>(acc[1][0], q1, bh1, bl1, x10, x11);
       }
     }
     if (!ok) break;
@@ -289,8 +292,7 @@ cudaError_t launch_v3(const GemvParams &p, int sms, cudaStream_t s) {
   const uint32_t ntile = p.N / 64, need = (ntile + kV3Warps - 1) / kV3Warps;
   uint32_t gx = (uint32_t)sms;
   if (gx > need) gx = need;
-  k<<<gx, kV3Threads, smem, s>>>(p, gx, nslot);
-  return cudaGetLastError();
+  return launch_pdl(k, dim3(gx), dim3(kV3Threads), smem, s, 1, p, gx, nslot);
 }
 
 

@@ -273,8 +273,11 @@ __global__ void __launch_bounds__(kV4Threads, 1) gemv_q4_v4(const __grid_constan
     }
     issued++;
   };
+  if (!p.overlap) pdl_wait();
   if (lane == 0)
     for (uint32_t k = 0; k < nslot && i_rec < r1; k++) issue_next(k);   // these fly while x is staged
+  pdl_trigger();
+  if (p.overlap) pdl_wait();
   const float f = stage_x_v4<MT>(p, G, xb, xsum, red);
 
   const uint32_t btok = PACK ? (g & 3u) : g, bsel = PACK ? (g >> 2) : 0u;   // B column of this lane
@@ -354,8 +357,8 @@ __global__ void __launch_bounds__(kV4Threads, 1) gemv_q4_v4(const __grid_constan
         issue_next(cs);
       }
       if (++cs == nslot) { cs = 0; cph ^= 1u; }
-      rec_math<PACK>(acc[0], q0, bh0, bl0, x00, x01);
-      if (two) rec_math<PACK>(acc[1], q1, bh1, bl1, x10, x11);
+      rec_math<MT, PACK>(acc[0], q0, bh0, bl0, x00, x01);
+      if (two) rec_math<MT, PACK>(acc[1], q1, bh1, bl1, x10, x11);
     }
     if (!ok) break;
     rec = e;
@@ -483,8 +486,7 @@ cudaError_t launch_v4(const GemvParams &p, const V4Plan &pl, cudaStream_t s) {
   V4Kernel k = v4_kernel_for(p.M, pl.Gt != pl.G);
   const size_t smem = v4_smem(p.M, pl.G, pl.nslot);
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  k<<<pl.NW / kV4Warps, kV4Threads, smem, s>>>(p, pl);
-  return cudaGetLastError();
+  return launch_pdl(k, dim3(pl.NW / kV4Warps), dim3(kV4Threads), smem, s, 1, p, pl);
 }
 
 }  // namespace p0gemv

@@ -140,10 +140,13 @@ __global__ void __launch_bounds__(kV5Threads, 2) gemv_q4_v5(const __grid_constan
   }
   if (threadIdx.x == 0) *abort_flag = 0u;
   __syncwarp();
+  if (!p.overlap) pdl_wait();
   if (lane == 0 && wn) {
     tc::mbar_expect_tx(&bars[warp], wn * 1280u);
     bulk_g2s(recs + (size_t)wa * 1280u, p.W + ((size_t)wt * p.wG + j0 + wa) * 1280u, wn * 1280u, &bars[warp]);
   }
+  pdl_trigger();
+  if (p.overlap) pdl_wait();
   const float f = stage_x_v5<MT>(p, j0, n, xb, xsum, misc);   // j0 is also the slice's first group of x
 
   // ---- the warp's records: pairs, both loaded before the math (the v3 loop)
@@ -181,8 +184,8 @@ __global__ void __launch_bounds__(kV5Threads, 2) gemv_q4_v5(const __grid_constan
         if (2 * c < MT) { x00 = __uint_as_float(lds32(xs_addr + gA * MT * 4u)); x10 = __uint_as_float(lds32(xs_addr + gB * MT * 4u)); }
         if (2 * c + 1 < MT) { x01 = __uint_as_float(lds32(xs_addr + gA * MT * 4u + 4u)); x11 = __uint_as_float(lds32(xs_addr + gB * MT * 4u + 4u)); }
       }
-      rec_math<PACK>(acc[0], q0, bh0, bl0, x00, x01);
-      if (two) rec_math<PACK>(acc[1], q1, bh1, bl1, x10, x11);
+      rec_math<MT, PACK>(acc[0], q0, bh0, bl0, x00, x01);
+      if (two) rec_math<MT, PACK>(acc[1], q1, bh1, bl1, x10, x11);
     }
   }
   // ---- the warp's totals (x f; PACK: hi + lo columns) -> red[warp][m][row]
@@ -311,19 +314,7 @@ cudaError_t launch_v5(const GemvParams &p, const V5Plan &pl, cudaStream_t s) {
   V5Kernel k = v5_kernel_for(p.M, pl.pair != 0);
   const size_t smem = v5_smem(p.M, pl.nmax);
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.units * pl.CS);
-  cfg.blockDim = dim3(kV5Threads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = pl.CS;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k, p, pl);
+  return launch_pdl(k, dim3(pl.units * pl.CS), dim3(kV5Threads), smem, s, pl.CS, p, pl);
 }
 
 }  // namespace p0gemv

@@ -33,6 +33,7 @@ struct p0_ctx {
   // or shrinks while the workspace lives, so one call's scratch never lands on another call's counters.
   void *ws = nullptr;
   size_t ws_bytes = 0, ws_cnt_bytes = 0;
+  bool overlap = false;          // p0_set_overlap: weights are static, GEMVs may fetch them before the call ahead ends
   std::mutex mu;
 };
 

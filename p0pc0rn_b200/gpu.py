@@ -75,6 +75,11 @@ class Gpu:
         """run subsequent work on an external cudaStream_t (an int address; 0 = the context's own stream)"""
         self._check(self._lib.p0_set_stream(self.ctx, ctypes.c_void_p(int(stream_ptr) or None)))
 
+    def set_overlap(self, weights_static=True):
+        """let GEMV calls fetch their weights before the call ahead on the stream has finished (p0_set_overlap): the
+        caller guarantees that no work in flight writes a weight buffer (weights written once, then synchronised)"""
+        self._check(self._lib.p0_set_overlap(self.ctx, 1 if weights_static else 0))
+
     @property
     def stats(self):
         a, p, d = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
