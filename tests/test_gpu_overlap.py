@@ -39,11 +39,11 @@ def test_dependent_chain(g, overlap):
             bufs.append(yb)
             cur = yb
         # overwrite the first link's input with a call that reads the last output (a write after an earlier read)
-        M, N, K = 1, 2048, 2048
-        bo, _ = ref.pack_q4(ref.randn(N * K, 620, 0.02), N, K)
+        No, Ko = 2048, 2048
+        bo, _ = ref.pack_q4(ref.randn(No * Ko, 620, 0.02), No, Ko)
         wbo = g.upload(bo)
         g.done()
-        p0.gemv(g, {"w": wview(wbo, N, K), "x": {"buf": bufs[-1]}, "N": N, "K": K, "y": {"buf": bufs[0]}})
+        p0.gemv(g, {"w": wview(wbo, No, Ko), "x": {"buf": bufs[-1]}, "N": No, "K": Ko, "y": {"buf": bufs[0]}})
         outs = [g.read(bb, 0, None, np.float32) for bb in bufs]
         xin = x0
         for (M, N, K), (b, _), out in zip(LINKS, ws, outs[1:]):
@@ -51,6 +51,6 @@ def test_dependent_chain(g, overlap):
             want = ref.gemv(b, X, N, K)[0] if M == 1 else ref.gemvM(b, X, M, N, K)[0]
             assert_close(out[:M * N], want)
             xin = out
-        assert_close(outs[0][:N], ref.gemv(bo, outs[-1][:K], N, K)[0])
+        assert_close(outs[0][:No], ref.gemv(bo, outs[-1][:Ko], No, Ko)[0])
     finally:
         g.set_overlap(False)
