@@ -9,6 +9,8 @@
 // their partials in shared memory in warp order, and rank 0 of the cluster sums the CTAs' partials through distributed
 // shared memory in rank order and applies the epilogue. No global scratch, no atomics: the result does not depend on
 // timing.
+#include <cstdlib>
+
 #include "gemv_common.cuh"
 
 namespace p0gemv {
@@ -27,13 +29,11 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// a float from CTA `rank`'s shared memory at this CTA's shared address `saddr`
-__device__ __forceinline__ float ld_dsmem(uint32_t saddr, uint32_t rank) {
+// store a float into CTA `rank`'s shared memory at this CTA's shared address `saddr` (the layouts are the same)
+__device__ __forceinline__ void st_dsmem(uint32_t saddr, uint32_t rank, float v) {
   uint32_t a;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(saddr), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
-  return v;
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
 }
 
 // x of groups [gx, gx + n) of one slice, staged in one pass (the v4 staging): B fragments (fp16 hi / lo, permuted k
@@ -96,7 +96,7 @@ __device__ float stage_x_v5(const GemvParams &p, uint32_t gx, uint32_t n, uint4 
 }
 
 size_t v5_smem(uint32_t M, uint32_t nmax) {
-  return (size_t)nmax * 1280 + (size_t)nmax * M * 128 + (size_t)nmax * M * 4 + (size_t)kV5Warps * M * 64 * 4 + (size_t)M * 64 * 4 +
+  return (size_t)nmax * 1280 + (size_t)nmax * M * 128 + (size_t)nmax * M * 4 + (size_t)kV5Warps * M * 64 * 4 + (size_t)8 * M * 64 * 4 +
          kV5Warps * 8 + 64 * 4;
 }
 
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kV5Threads, 2) gemv_q4_v5(const __grid_constan
   uint4 *xb = reinterpret_cast<uint4 *>(recs + (size_t)pl.nmax * 1280u);     // [nmax][MT][4][2]
   float *xsum = reinterpret_cast<float *>(xb + (size_t)pl.nmax * MT * 8);     // [nmax][MT]
   float *red = xsum + (size_t)pl.nmax * MT;                                   // [warps][MT][64]
-  float *part = red + kV5Warps * MT * 64;                                     // [MT][64]: this CTA's slice total
+  float *gath = red + kV5Warps * MT * 64;   // [rank][MT][64]: in rank 0, every CTA's slice total
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t g = lane >> 2, c = lane & 3;
   // ---- every warp copies its share of the slice at once
@@ -200,35 +200,32 @@ __global__ void __launch_bounds__(kV5Threads, 2) gemv_q4_v5(const __grid_constan
       if (holder && m < MT) red[(warp * MT + m) * 64u + row] = v;
     }
   __syncthreads();
-  // the CTA's slice total, summed in warp order
+  // the CTA's slice total, summed in warp order, pushed into rank 0's gath[rank] (remote stores, no round trips)
+  const uint32_t gath_s = tc::smem_u32(gath) + rank * (MT * 64u) * 4u;
   for (uint32_t idx = threadIdx.x; idx < MT * 64u; idx += kV5Threads) {
-    float s = 0.0f;
+    float sum = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kV5Warps; w++) s += red[w * MT * 64u + idx];
-    part[idx] = s;
+    for (int w = 0; w < kV5Warps; w++) sum += red[w * MT * 64u + idx];
+    if (CS > 1u) st_dsmem(gath_s + idx * 4u, 0u, sum);
+    else gath[idx] = sum;
   }
-  if (CS > 1u) cluster_sync();
+  if (CS > 1u) cluster_sync();   // the release / acquire pair makes every rank's stores visible in rank 0
   else __syncthreads();
   // ---- rank 0: the unit's total (the ranks' parts in rank order; geglu: gate ranks, then up ranks) and the epilogue;
   // warp m takes token m, lane l rows l and l + 32
   if (rank == 0u && warp < MT && ok && !*abort_flag) {
-    const uint32_t m = warp, part_s = tc::smem_u32(part);
+    const uint32_t m = warp;
     float t[2], u2[2] = {0.0f, 0.0f};
 #pragma unroll
     for (int h = 0; h < 2; h++) {
       const uint32_t idx = m * 64u + lane + 32u * h;
-      if (PAIR) {
-        const uint32_t hr = CS / 2u;
-        float a = part[idx], b = 0.0f;
-        for (uint32_t r = 1; r < hr; r++) a += ld_dsmem(part_s + idx * 4u, r);
-        for (uint32_t r = hr; r < CS; r++) b += ld_dsmem(part_s + idx * 4u, r);
-        t[h] = a;
-        u2[h] = b;
-      } else {
-        float a = part[idx];
-        for (uint32_t r = 1; r < CS; r++) a += ld_dsmem(part_s + idx * 4u, r);
-        t[h] = a;
-      }
+      const uint32_t hr = PAIR ? CS / 2u : CS;
+      float a = 0.0f, b = 0.0f;
+      for (uint32_t r = 0; r < hr; r++) a += gath[r * MT * 64u + idx];
+      if (PAIR)
+        for (uint32_t r = hr; r < CS; r++) b += gath[r * MT * 64u + idx];
+      t[h] = a;
+      u2[h] = b;
     }
     const uint32_t R0 = tile * 64u;
     if (PAIR) {
@@ -259,8 +256,6 @@ __global__ void __launch_bounds__(kV5Threads, 2) gemv_q4_v5(const __grid_constan
       for (int h = 0; h < 2; h++) p.Y[(size_t)split * p.ldy + (size_t)m * p.ldm + R0 + lane + 32u * h] = t[h];
     }
   }
-  // the other CTAs' shared memory stays in place until rank 0 has read it
-  if (CS > 1u) cluster_sync();
   // a copy whose wait gave up lands before the CTA exits (bounded)
   if (!ok && lane == 0 && wn) {
     volatile uint32_t never = 0;
@@ -293,6 +288,10 @@ bool v5_plan(const GemvParams &p, uint32_t nsplit, int sms, V5Plan *pl) {
   const uint64_t units = pair ? ntile : (uint64_t)ntile * nsplit;
   const uint32_t nu = pair ? G : Gs;   // records per unit (per half for geglu)
   // the smallest cluster that gives every SM a CTA, within the staging and shared-memory limits
+  // (P0MM_V5_CTAS, a tuning override, sets the CTA count to reach instead of the SM count)
+  const char *tv = getenv("P0MM_V5_CTAS");
+  const long tn = tv ? strtol(tv, nullptr, 10) : 0;
+  const uint64_t target = tn > 0 && tn < 100000 ? (uint64_t)tn : (uint64_t)sms;
   uint32_t best = 0;
   for (uint32_t CS = pair ? 2u : 1u; CS <= 8u; CS *= 2u) {
     const uint32_t parts = pair ? CS / 2u : CS;
@@ -300,7 +299,7 @@ bool v5_plan(const GemvParams &p, uint32_t nsplit, int sms, V5Plan *pl) {
     const uint32_t nmax = (nu + parts - 1) / parts;
     if (nmax * p.M * 4 > kV5XUnits * kV5Threads || v5_smem(p.M, nmax) > 200u * 1024u) continue;
     best = CS;
-    if (units * CS >= (uint64_t)sms) break;
+    if (units * CS >= target) break;
   }
   if (!best || units * best > (uint64_t)sms * 8) return false;   // many tiles: the streaming kernels take them
   const uint32_t parts = pair ? best / 2u : best;
