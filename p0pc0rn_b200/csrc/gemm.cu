@@ -17,6 +17,7 @@
 //                coalesced vector stores.
 // Orientation: D = Wdq . X^T, so TMEM lane = output column n and TMEM column = token m.
 #include <cuda.h>
+#include <cstdlib>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
@@ -27,15 +28,26 @@ namespace {
 
 constexpr int kBW = 128;        // weight rows per CTA (TMEM lanes, MMA M)
 constexpr int kBK = 64;         // k per stage
-constexpr int kStages = 5;
-constexpr int kDqWarps = 16;    // warps 2..17: (lane quarter) x (32-k half of a stage) x (stage parity)
+// Two shapes of the kernel, one source. Cfg1: 16 dequantiser warps (two stage parities), 5 stages, tiles of up to 256
+// tokens, one CTA per SM, 512 TMEM columns. Cfg2: 8 dequantiser warps, 4 stages, tiles of up to 128 tokens, two CTAs
+// per SM with 256 TMEM columns each, so that one CTA's epilogue runs while the other's main loop keeps the tensor
+// cores busy.
+template <int DQW, int STAGES, uint32_t MAXBT, int MINB>
+struct GemmCfg {
+  static constexpr int kDqWarps = DQW;                 // warps 2 .. 2+DQW-1: (lane quarter) x (32-k half) x (parity)
+  static constexpr int kPar = DQW / 8;                 // stage parities the dequantisers alternate over
+  static constexpr int kStages = STAGES;
+  static constexpr int kMinBlocks = MINB;
+  static constexpr int kThreads = 32 * (2 + DQW);
+  static constexpr uint32_t kMaxBT = MAXBT;
+  static constexpr uint32_t kAcol = MAXBT;             // first TMEM column of the weight (A) stages; D holds [0, BT)
+  static constexpr uint32_t kTmemCols = MAXBT + 32u * STAGES <= 256u ? 256u : 512u;
+  static constexpr size_t kXStage = (size_t)MAXBT * kBK * 2;   // X slot (1024-aligned); the ring is also the staging
+  static constexpr size_t kRingBytes = (size_t)STAGES * kXStage;
+};
+using Cfg1 = GemmCfg<16, 5, 256, 1>;
+using Cfg2 = GemmCfg<8, 4, 128, 2>;
 constexpr int kDqPerStage = 8;  // dequant warps that fill one stage
-constexpr int kThreads = 32 * (2 + kDqWarps);
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAcol = 256; // first TMEM column of the weight (A) stages; the accumulator holds columns [0, BT)
-constexpr uint32_t kMaxBT = 256;
-constexpr size_t kXStage = (size_t)kMaxBT * kBK * 2;                // 32 KB X slot (1024-aligned)
-constexpr size_t kRingBytes = (size_t)kStages * kXStage;              // 160 KB; also the epilogue staging area
 constexpr uint32_t kWStage = 2u * 2u * 1280u;                        // weights of a stage: 2 row tiles x 2 groups
 
 struct GemmParams {
@@ -151,7 +163,12 @@ __device__ __forceinline__ void cta_tiles(const GemmParams &p, uint32_t nB, uint
   t1 = t1 < nt ? t1 : nt - 1;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) gemm_q4_tc(const __grid_constant__ CUtensorMap tmx, const GemmParams p) {
+template <class C>
+__global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const __grid_constant__ CUtensorMap tmx, const GemmParams p) {
+  constexpr int kStages = C::kStages, kDqWarps = C::kDqWarps;
+  constexpr uint32_t kAcol = C::kAcol, kTmemCols = C::kTmemCols;
+  constexpr size_t kXStage = C::kXStage, kRingBytes = C::kRingBytes;
+  static_assert((size_t)C::kMaxBT * 128 * 4 <= C::kRingBytes, "the epilogue stages [BT][128] f32 in the X ring");
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base by pointer arithmetic on the shared array (keeps shared-space loads and stores)
   uint8_t *smem = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -268,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4_tc(const __grid_constant_
       tail_off = 4096u + (h * 128u + nl) * 4u;
     }
     bool ok = true;
-    for (uint32_t s = par; s < nk; s += 2) {   // this warp fills every other stage
+    for (uint32_t s = par; s < nk; s += C::kPar) {   // this warp fills every kPar-th stage
       const uint32_t slot = s % kStages, ph = (s / kStages) & 1u;
       const bool got = tc::mbar_wait(&full[slot], ph, abort_flag, p.err, 0x301u, P0_SPIN_LIMIT);
       if (!__all_sync(0xffffffffu, got)) { ok = false; break; }   // warp-uniform: tcgen05.st is .sync.aligned
@@ -309,7 +326,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q4_tc(const __grid_constant_
         gB = p.BV[p.bvOff + o];
         uB = p.BV[p.bvOff + p.bvUp + o];
       }
-      const uint32_t e = d >> 2, cpw = BT / 4;   // 16 warps: quarter q of the lanes, columns [e*BT/4, (e+1)*BT/4)
+      // warp: quarter q of the lanes, columns [e*cpw, (e+1)*cpw) of BT / (warps / 4)
+      const uint32_t e = d >> 2, cpw = BT / (kDqWarps / 4);
       for (uint32_t c0 = e * cpw; c0 < (e + 1) * cpw; c0 += 16) {
         uint32_t r[16];
         tc::tmem_ld16(tq + c0, r);
@@ -461,7 +479,11 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   if (bias && (st = p0_range(c, a->bv, 0, ((uint64_t)a->bv_off + (swi ? a->bv_up + N / 2 : N)) * 4, op, "BV", &rb))) return st;
   if (swi && (a->wr0 + N / 2 > a->w.rows || a->wr1 + N / 2 > a->w.rows)) return p0_fail(c, P0_EINVAL, "gemm: swiglu rows beyond the weight");
 
-  const uint32_t BT = M <= 64 ? 64u : M <= 128 ? 128u : 256u;
+  // Cfg1 everywhere: measured on B200 (configs 3 and 4), Cfg2's overlapped epilogue does not pay for halving the tokens
+  // each dequantised stage feeds (804-899 against 937-1067 TFLOP/s). P0MM_GEMM=2 selects Cfg2 (tuning and tests).
+  const char *gv = getenv("P0MM_GEMM");
+  const bool cfg2 = gv && gv[0] == '2';
+  const uint32_t BT = M <= 64 ? 64u : (M <= 128 || cfg2) ? 128u : 256u;
   auto enc_fn = tensor_map_encoder();
   if (!enc_fn) return p0_fail(c, P0_EDEVICE, "gemm: cuTensorMapEncodeTiled is unavailable");
   CUtensorMap tm;
@@ -483,11 +505,18 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   p.BT = BT; p.nk = (K + kBK - 1) / kBK; p.err = c->d_err;
   // bulk-copy weight path: every CTA's 128 lanes read two whole 64-row tiles
   p.wtma = swi ? (a->wr0 % 64 == 0 && a->wr1 % 64 == 0 && (N / 2) % 64 == 0) : (a->wr0 % 64 == 0);
-  const size_t smem = kRingBytes + (size_t)kStages * kWStage + 1024 + 256;
   cudaSetDevice(c->device);
-  cudaFuncSetAttribute(gemm_q4_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
-  gemm_q4_tc<<<grid, kThreads, smem, c->stream>>>(tm, p);
+  if (cfg2) {
+    const size_t smem = Cfg2::kRingBytes + (size_t)Cfg2::kStages * kWStage + 1024 + 256;
+    cudaFuncSetAttribute(gemm_q4_tc<Cfg2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
+    gemm_q4_tc<Cfg2><<<grid, Cfg2::kThreads, smem, c->stream>>>(tm, p);
+  } else {
+    const size_t smem = Cfg1::kRingBytes + (size_t)Cfg1::kStages * kWStage + 1024 + 256;
+    cudaFuncSetAttribute(gemm_q4_tc<Cfg1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
+    gemm_q4_tc<Cfg1><<<grid, Cfg1::kThreads, smem, c->stream>>>(tm, p);
+  }
   if ((st = p0_launched(c, "gemm"))) return st;
   if (flops) *flops = 2.0 * M * N * K;
   (void)gepi_name;
