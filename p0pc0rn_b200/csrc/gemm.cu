@@ -47,6 +47,7 @@ struct GemmCfg {
 };
 using Cfg1 = GemmCfg<16, 5, 256, 1>;
 using Cfg2 = GemmCfg<8, 4, 128, 2>;
+using Cfg3 = GemmCfg<16, 6, 256, 1>;   // Cfg1 with a sixth stage (223 KB of shared memory, 448 TMEM columns)
 constexpr int kDqPerStage = 8;  // dequant warps that fill one stage
 constexpr uint32_t kWStage = 2u * 2u * 1280u;                        // weights of a stage: 2 row tiles x 2 groups
 
@@ -126,14 +127,21 @@ __device__ __forceinline__ uint32_t ldg_w32(const void *p) {
 }
 
 // activations in the reference's source order (no contraction)
+// tanh on the SFU (tanh.approx.f32): its error is far below an fp16 ulp of the GELU results the epilogue stores, and
+// it takes one instruction where tanhf takes a sequence; the epilogue's GELU is the MLP-up GEMM's largest extra cost
+__device__ __forceinline__ float tanh_sfu(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float gelu_g(float g) {   // gemm.js:204
   float u = __fmul_rn(0.7978845608f, __fadd_rn(g, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, g), g), g)));
   u = fminf(15.0f, fmaxf(-15.0f, u));
-  return __fmul_rn(__fmul_rn(g, 0.5f), __fadd_rn(1.0f, tanhf(u)));
+  return __fmul_rn(__fmul_rn(g, 0.5f), __fadd_rn(1.0f, tanh_sfu(u)));
 }
 __device__ __forceinline__ float gelu_m(float x) {   // ops/misc.js:116
   float u = __fmul_rn(0.7978845608f, __fadd_rn(x, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x)));
-  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(fminf(15.0f, fmaxf(-15.0f, u)))));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanh_sfu(fminf(15.0f, fmaxf(-15.0f, u)))));
 }
 __device__ __forceinline__ float silu_g(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
 
@@ -482,7 +490,7 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   // Cfg1 everywhere: measured on B200 (configs 3 and 4), Cfg2's overlapped epilogue does not pay for halving the tokens
   // each dequantised stage feeds (804-899 against 937-1067 TFLOP/s). P0MM_GEMM=2 selects Cfg2 (tuning and tests).
   const char *gv = getenv("P0MM_GEMM");
-  const bool cfg2 = gv && gv[0] == '2';
+  const bool cfg2 = gv && gv[0] == '2', cfg3 = gv && gv[0] == '3';
   const uint32_t BT = M <= 64 ? 64u : (M <= 128 || cfg2) ? 128u : 256u;
   auto enc_fn = tensor_map_encoder();
   if (!enc_fn) return p0_fail(c, P0_EDEVICE, "gemm: cuTensorMapEncodeTiled is unavailable");
@@ -506,7 +514,12 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   // bulk-copy weight path: every CTA's 128 lanes read two whole 64-row tiles
   p.wtma = swi ? (a->wr0 % 64 == 0 && a->wr1 % 64 == 0 && (N / 2) % 64 == 0) : (a->wr0 % 64 == 0);
   cudaSetDevice(c->device);
-  if (cfg2) {
+  if (cfg3) {
+    const size_t smem = Cfg3::kRingBytes + (size_t)Cfg3::kStages * kWStage + 1024 + 256;
+    cudaFuncSetAttribute(gemm_q4_tc<Cfg3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
+    gemm_q4_tc<Cfg3><<<grid, Cfg3::kThreads, smem, c->stream>>>(tm, p);
+  } else if (cfg2) {
     const size_t smem = Cfg2::kRingBytes + (size_t)Cfg2::kStages * kWStage + 1024 + 256;
     cudaFuncSetAttribute(gemm_q4_tc<Cfg2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
