@@ -31,8 +31,8 @@ K = 2048
 MS = (1, 2, 4, 8)
 NS = (2048, 16384, 262144)
 HEAD_N = 262144
-# DRAM bytes (read + write) of one head GEMV launch (N = 262144, K = 2048) from ncu captures at M = 1 and M = 8
-HEAD_TRAFFIC = 343.45e6
+# DRAM bytes (read + write) of one head GEMV launch (N = 262144, K = 2048, M = 1) from an ncu capture
+HEAD_TRAFFIC = 340.45e6
 
 
 def gemv_bytes(M, N, K, head):
@@ -354,8 +354,8 @@ def run_ours(args, ws, rank, local):
                                  "events between graph launches time the head"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "traffic": HEAD_TRAFFIC if ws == 1 else None,
-                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per head launch, one ncu capture each at "
-                                         "M=1 (342.4 MB) and M=8 (344.5 MB), mean; algorithmic 336.6 / 344.5 MB", "kernel": "gemv head (rms+softcap) N=%d/rank K=%d, M=1/2/4/8" % (HEAD_N // ws, K),
+                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one head launch at M=1 from an ncu "
+                                         "capture (335.7 + 4.7 MB); algorithmic 336.6 MB", "kernel": "gemv head (rms+softcap) N=%d/rank K=%d, M=1/2/4/8" % (HEAD_N // ws, K),
                          "per_M_us": {str(k): round(v * 1e3, 2) for k, v in sorted(per_m.items())}, "peak_source": src},
             "e2e": e2e, "gpu_launches": len(sw.calls) * args.steps, "clocks": clocks, "gemm": gemm,
             "calls_us": calls_us, "decode": decode,
