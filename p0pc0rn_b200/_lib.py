@@ -20,7 +20,7 @@ ACT = {"silu": 0, "gelu": 1}
 
 # every symbol include/p0mm.h declares
 EXPORTS = ["p0_init", "p0_destroy", "p0_set_stream", "p0_set_overlap", "p0_last_error", "p0_stats", "p0_buffer", "p0_wrap", "p0_upload", "p0_read",
-           "p0_free", "p0_done", "p0_device_ptr", "p0_gemv", "p0_gemvM", "p0_gemvM_noalloc", "p0_gemm", "p0_pack_q4",
+           "p0_free", "p0_done", "p0_device_ptr", "p0_gemv", "p0_gemvM", "p0_gemvM_noalloc", "p0_gemm", "p0_pack_q4", "p0_pack_q8",
            "p0_dequant_f16", "p0_version"]
 P0_NOALLOC_SCRATCH_BYTES = 16 << 20   # include/p0mm.h
 P0_OVERLAP_WEIGHTS = 1
@@ -90,6 +90,7 @@ def load():
     L.p0_gemvM_noalloc.argtypes = [vp, ctypes.POINTER(p0_gemvM_args), ctypes.POINTER(ctypes.c_uint32)]
     L.p0_gemm.argtypes = [vp, ctypes.POINTER(p0_gemm_args), ctypes.POINTER(ctypes.c_double)]
     L.p0_pack_q4.argtypes = [vp, p0_buf, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, p0_buf, ctypes.c_uint64]
+    L.p0_pack_q8.argtypes = [vp, p0_buf, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, p0_buf, ctypes.c_uint64]
     L.p0_dequant_f16.argtypes = [vp, ctypes.POINTER(p0_wview), p0_buf]
     L.p0_version.restype = ctypes.c_char_p
     for name in EXPORTS:

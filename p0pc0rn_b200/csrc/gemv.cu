@@ -506,17 +506,18 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
                    p0_buf stb, uint32_t stat_off, uint32_t stat_ld, p0_buf nb, uint32_t norm_off, p0_buf eb, uint32_t ev_off,
                    uint32_t ev_ld, uint32_t src_n, uint32_t src_ld, p0_buf mxb, float cap, bool noalloc = false) {
   p0_status st;
-  const uint32_t G = 32;
-  if (w.enc != P0_ENC_Q4G32A_T64) return p0_fail(c, P0_EINVAL, "%s: encoding %s is not built in this library yet", op, enc_name(w.enc));
+  const bool q8 = w.enc == P0_ENC_Q8G64S_T64;
+  const uint32_t G = q8 ? 64u : 32u, RB = q8 ? 4224u : 1280u;   // k per record, bytes per record
+  if (w.enc != P0_ENC_Q4G32A_T64 && !q8) return p0_fail(c, P0_EINVAL, "%s: encoding %s is not built in this library yet", op, enc_name(w.enc));
   if (K % G) return p0_fail(c, P0_EINVAL, "%s: K must be a multiple of %u", op, G);
   if (w.cols % G || w.cols < K) return p0_fail(c, P0_EINVAL, "%s: weight cols %u do not cover K %u", op, w.cols, K);
   if (pro > P0_PRO_PLEG || epi > P0_EPI_SOFTCAP) return p0_fail(c, P0_EINVAL, "%s: prologue/epilogue code", op);
   const uint32_t wG = w.cols / G, NT = N / 64, ntw = epi == P0_EPI_GEGLU ? 2 * NT : NT;
   // bind and bounds-check every view, as WebGPU validates bindings
   P0Range rw, rx, ry, rn, re, rs, rm;
-  // the records the call reads: every tile's first K/32 groups, tiles wG records apart (a view may start at a later
+  // the records the call reads: every tile's first K/G groups, tiles wG records apart (a view may start at a later
   // group of tile 0, as a k-slice of a wider weight does)
-  uint64_t wneed = ((uint64_t)(ntw - 1) * wG + K / G) * 1280u;
+  uint64_t wneed = ((uint64_t)(ntw - 1) * wG + K / G) * RB;
   if (w.bytes && wneed > w.bytes) return p0_fail(c, P0_EINVAL, "%s: weight view of %llu bytes holds fewer than %u tiles", op, (unsigned long long)w.bytes, ntw);
   if ((st = p0_range(c, w.buf, w.off, wneed, op, "W", &rw))) return st;
   if ((uintptr_t)rw.base % 16) return p0_fail(c, P0_EALIGN, "%s: weight offset (16-byte aligned records needed)", op);
@@ -543,6 +544,7 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
   p.M = M; p.N = N; p.K = K; p.wG = wG; p.kPer = kPer; p.ldy = ldy; p.ldm = ldm; p.ldx = ldx; p.rowB = rowB;
   p.nOff = norm_off; p.statOff = stat_off; p.statLd = stat_ld; p.evOff = ev_off; p.evLd = ev_ld; p.ldp = src_ld; p.nsrc = src_n;
   p.ntile = NT; p.cap = cap; p.pro = (int)pro; p.epi = (int)epi; p.err = c->d_err; p.overlap = c->overlap ? 1 : 0;
+  p.q8 = q8 ? 1 : 0;
   // staged x per chunk: <= 32 KB of x rows, whole groups
   uint32_t xc = (8192u / M) / 32u * 32u;
   uint32_t span = kPer < K ? kPer : K;
@@ -559,6 +561,14 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
   V4Plan pl{};
   V5Plan p5{};
   size_t scratch_bytes = 0;
+  if (q8) {
+    // q8g64s.t64 weights run on the cluster kernel only
+    if (noalloc) return p0_fail(c, P0_EINVAL, "%s: q8g64s.t64 weights are not built for the allocation-free entry point", op);
+    if (!v5_plan(p, nsplit, c->sm_count, &p5))
+      return p0_fail(c, P0_EINVAL, "%s: q8g64s.t64 with M %u x K %u (split %u) is not built in this library yet", op, M, K, kPer);
+    if ((st = p0_cuda(c, launch_v5(p, p5, c->stream), op))) return st;
+    return p0_launched(c, op);
+  }
   if (noalloc) {
     // the allocation-free mode: the stream-K kernel with the fixed device array as its scratch
     if (!v4_plan(p, nsplit, c->sm_count, &pl, &scratch_bytes))

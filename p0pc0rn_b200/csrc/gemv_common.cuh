@@ -25,6 +25,7 @@ struct GemvParams {
   float cap;
   int pro, epi;
   int overlap;       // the weights are not written by work ahead on the stream: copies may start before pdl_wait()
+  int q8;            // q8g64s.t64 weights (4224-byte records of 64 k; only the v5 kernels take them)
   uint32_t *err;
 };
 
@@ -170,6 +171,65 @@ __device__ __forceinline__ void rec_math(float (&acc)[4][4], const Rec &q, const
   }
 }
 
+
+// ---------------------------------------------------------------- q8g64s.t64 records (v5)
+// A q8 record (64 rows x 64 k): int8 codes at r*64 + k, fp16 scales at 4096 + 2r; the weight is q*s (kcheck.js:40-53).
+// Code word c (bytes 4c..4c+3) of a row's 16-k chunk j feeds the m16n8k16 A fragment: its first two codes are MMA-k
+// 2c, 2c+1 and its last two MMA-k 2c+8, 2c+9, so x is staged in that order. Codes become exact fp16 by an xor with
+// 0x80, a byte permute against 0x64 ((1024 + q + 128) in fp16) and an fp16 subtract of 1152.
+struct Rec8 {
+  uint32_t w[4][4][2];   // [row block][chunk][rows g, g+8]
+  uint32_t s[4];         // [row block]: fp16 scales of rows g (low half) and g + 8 (high half)
+};
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void rec8_load(Rec8 &q, uint32_t rec, uint32_t lane) {
+  const uint32_t g = lane >> 2, rl = (lane & 7u) + 8u * ((lane >> 3) & 1u), jl = lane >> 4;
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+#pragma unroll
+    for (int jp = 0; jp < 2; jp++)
+      ldsm_x4(rec + (16u * r + rl) * 64u + 16u * (2u * jp + jl), q.w[r][2 * jp][0], q.w[r][2 * jp][1], q.w[r][2 * jp + 1][0],
+              q.w[r][2 * jp + 1][1]);
+    q.s[r] = lds16(rec + 4096u + 2u * (16u * r + g)) | (lds16(rec + 4096u + 2u * (16u * r + g + 8u)) << 16);
+  }
+}
+__device__ __forceinline__ uint32_t q8_pair(uint32_t u, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(u), "r"(0x64646464u), "r"(sel));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(d), "r"(0x64806480u));
+  return d;
+}
+// acc[r] += s_row * sum_k q x over the record; b[j] = this lane's staged x of chunk j (hi in .x/.y, lo in .z/.w)
+template <int MT, bool PACK>
+__device__ __forceinline__ void rec8_math(float (&acc)[4][4], const Rec8 &q, const uint4 (&b)[4], uint32_t bsel) {
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const uint32_t u0 = q.w[r][j][0] ^ 0x80808080u, u1 = q.w[r][j][1] ^ 0x80808080u;
+      const uint32_t A[4] = {q8_pair(u0, 0x4140u), q8_pair(u1, 0x4140u), q8_pair(u0, 0x4342u), q8_pair(u1, 0x4342u)};
+      if (PACK) {
+        mma16816(d, A, bsel ? b[j].z : b[j].x, bsel ? b[j].w : b[j].y);
+      } else {
+        mma16816(d, A, b[j].x, b[j].y);
+        mma16816(d, A, b[j].z, b[j].w);
+      }
+    }
+    const __half2 sh = *reinterpret_cast<const __half2 *>(&q.s[r]);
+    const float s0 = __low2float(sh), s1 = __high2float(sh);
+    acc[r][0] = fmaf(s0, d[0], acc[r][0]);
+    acc[r][2] = fmaf(s1, d[2], acc[r][2]);
+    if (MT > 1) {
+      acc[r][1] = fmaf(s0, d[1], acc[r][1]);
+      acc[r][3] = fmaf(s1, d[3], acc[r][3]);
+    }
+  }
+}
 
 // the v3 (bulk-copy fed, whole tiles per warp) kernels, in gemv_v3.cu
 bool v3_fits(uint32_t M, uint32_t K, uint32_t nsplit, uint32_t ntile, int sms);

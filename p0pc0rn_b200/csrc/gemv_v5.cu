@@ -95,14 +95,79 @@ __device__ float stage_x_v5(const GemvParams &p, uint32_t gx, uint32_t n, uint4 
   return f;
 }
 
-size_t v5_smem(uint32_t M, uint32_t nmax) {
-  return (size_t)nmax * 1280 + (size_t)nmax * M * 128 + (size_t)nmax * M * 4 + (size_t)kV5Warps * M * 64 * 4 + (size_t)8 * M * 64 * 4 +
-         kV5Warps * 8 + 64 * 4;
+// q8 slices: x of groups [gx, gx + n) (64 k each) as fp16 hi / lo in the order of the q8 A fragments (see Rec8):
+// entry ((group * MT + token) * 4 + chunk) * 4 + c = {hi(k0, k1), hi(k2, k3), lo(k0, k1), lo(k2, k3)} for k = 16 chunk
+// + 4c + 0..3. The codes are integers, so f = 1 / sigma.
+template <int MT>
+__device__ float stage_x_v5q8(const GemvParams &p, uint32_t gx, uint32_t n, uint4 *xb8, float *red) {
+  constexpr uint32_t T = kV5Threads;
+  const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+  const uint32_t units = n * MT * 8;   // units of 8 consecutive k; <= kV5XUnits * T (host-checked)
+  float v[kV5XUnits][8];
+  float mx = 0.0f;
+#pragma unroll
+  for (uint32_t j = 0; j < kV5XUnits; j++) {
+    const uint32_t u = t + j * T;
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[j][i] = 0.0f;
+    if (u < units) {
+      const uint32_t gg = u / (MT * 8), rem = u - gg * (MT * 8), m = rem >> 3, cp = rem & 7u;
+      const uint32_t kb = (gx + gg) * 64 + cp * 8;
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        v[j][i] = prologue(p, m, kb + i);
+        mx = fmaxf(mx, fabsf(v[j][i]));
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int w = 1; w < kV5Warps; w++) mx = fmaxf(mx, red[w]);
+  int e = 0;
+  if (mx > 0.0f && mx < INFINITY) frexpf(mx, &e);
+  const float sigma = ldexpf(1.0f, 14 - e), f = ldexpf(1.0f, e - 14);
+#pragma unroll
+  for (uint32_t j = 0; j < kV5XUnits; j++) {
+    const uint32_t u = t + j * T;
+    if (u < units) {
+      const uint32_t gg = u / (MT * 8), rem = u - gg * (MT * 8), m = rem >> 3, cp = rem & 7u;
+#pragma unroll
+      for (int hc = 0; hc < 2; hc++) {
+        float hv[4], lv[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float vs = v[j][4 * hc + i] * sigma;   // exact power of two
+          const float h = __half2float(__float2half_rn(vs));
+          hv[i] = h;
+          lv[i] = vs - h;
+        }
+        const uint32_t c = 2u * (cp & 1u) + hc;
+        xb8[((gg * MT + m) * 4 + (cp >> 1)) * 4 + c] =
+            make_uint4(pack_h2(hv[0], hv[1]), pack_h2(hv[2], hv[3]), pack_h2(lv[0], lv[1]), pack_h2(lv[2], lv[3]));
+      }
+    }
+  }
+  __syncthreads();
+  return f;
 }
 
-template <int MT, bool PAIR>
+// record bytes and x staging bytes per (group, token) of each encoding
+__host__ __device__ constexpr uint32_t v5_rec_bytes(bool q8) { return q8 ? 4224u : 1280u; }
+__host__ __device__ constexpr uint32_t v5_xb_bytes(bool q8) { return q8 ? 256u : 128u; }
+
+size_t v5_smem(uint32_t M, uint32_t nmax, bool q8) {
+  return (size_t)nmax * v5_rec_bytes(q8) + (size_t)nmax * M * v5_xb_bytes(q8) + (size_t)nmax * M * 4 + (size_t)kV5Warps * M * 64 * 4 +
+         (size_t)8 * M * 64 * 4 + kV5Warps * 8 + 64 * 4;
+}
+
+template <int MT, bool PAIR, bool Q8>
 __global__ void __launch_bounds__(kV5Threads, 2) gemv_q4_v5(const __grid_constant__ GemvParams p, const __grid_constant__ V5Plan pl) {
   constexpr bool PACK = MT <= 4;
+  constexpr uint32_t RB = v5_rec_bytes(Q8), XB = v5_xb_bytes(Q8);
   extern __shared__ __align__(128) uint8_t smem8[];
   const uint32_t CS = pl.CS, rank = CS > 1u ? cluster_rank() : 0u, unit = blockIdx.x / CS;
   // ---- this CTA's slice: records [j0, j1) of tile `wt` (the weight tile it reads), groups gx.. of x
@@ -125,9 +190,9 @@ __global__ void __launch_bounds__(kV5Threads, 2) gemv_q4_v5(const __grid_constan
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem8);                        // [warps]
   float *misc = reinterpret_cast<float *>(bars + kV5Warps);                    // 64 floats
   volatile uint32_t *abort_flag = reinterpret_cast<volatile uint32_t *>(misc + 32);
-  uint8_t *recs = reinterpret_cast<uint8_t *>(misc + 64);                      // [nmax] x 1280 B (16-byte aligned)
-  uint4 *xb = reinterpret_cast<uint4 *>(recs + (size_t)pl.nmax * 1280u);     // [nmax][MT][4][2]
-  float *xsum = reinterpret_cast<float *>(xb + (size_t)pl.nmax * MT * 8);     // [nmax][MT]
+  uint8_t *recs = reinterpret_cast<uint8_t *>(misc + 64);                      // [nmax] x RB (16-byte aligned)
+  uint4 *xb = reinterpret_cast<uint4 *>(recs + (size_t)pl.nmax * RB);         // [nmax][MT] x XB
+  float *xsum = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(xb) + (size_t)pl.nmax * MT * XB);   // [nmax][MT] (q4)
   float *red = xsum + (size_t)pl.nmax * MT;                                   // [warps][MT][64]
   float *gath = red + kV5Warps * MT * 64;   // [rank][MT][64]: in rank 0, every CTA's slice total
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -142,12 +207,13 @@ __global__ void __launch_bounds__(kV5Threads, 2) gemv_q4_v5(const __grid_constan
   __syncwarp();
   if (!p.overlap) pdl_wait();
   if (lane == 0 && wn) {
-    tc::mbar_expect_tx(&bars[warp], wn * 1280u);
-    bulk_g2s(recs + (size_t)wa * 1280u, p.W + ((size_t)wt * p.wG + j0 + wa) * 1280u, wn * 1280u, &bars[warp]);
+    tc::mbar_expect_tx(&bars[warp], wn * RB);
+    bulk_g2s(recs + (size_t)wa * RB, p.W + ((size_t)wt * p.wG + j0 + wa) * RB, wn * RB, &bars[warp]);
   }
   pdl_trigger();
   if (p.overlap) pdl_wait();
-  const float f = stage_x_v5<MT>(p, j0, n, xb, xsum, misc);   // j0 is also the slice's first group of x
+  // j0 is also the slice's first group of x
+  const float f = Q8 ? stage_x_v5q8<MT>(p, j0, n, xb, misc) : stage_x_v5<MT>(p, j0, n, xb, xsum, misc);
 
   // ---- the warp's records: pairs, both loaded before the math (the v3 loop)
   const uint32_t btok = PACK ? (g & 3u) : g, bsel = PACK ? (g >> 2) : 0u;
@@ -166,7 +232,21 @@ __global__ void __launch_bounds__(kV5Threads, 2) gemv_q4_v5(const __grid_constan
   if (wn) {
     const bool got = tc::mbar_wait(&bars[warp], 0, abort_flag, p.err, 0x711u, P0_SPIN_LIMIT);
     ok = __all_sync(0xffffffffu, got);
-    for (uint32_t k = 0; ok && k < wn; k += 2) {
+    if (Q8) {
+      // one 4224-byte record at a time (its 32 code words per lane fill the registers a second record would take)
+      const uint32_t xb8_s = tc::smem_u32(xb);
+      for (uint32_t k = 0; ok && k < wn; k++) {
+        const uint32_t gA = wa + k;
+        Rec8 q;
+        rec8_load(q, rec_s + gA * RB, (uint32_t)lane);
+        uint4 b[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          b[j] = tok_ok ? lds128(xb8_s + (((gA * MT + btok) * 4u + (uint32_t)j) * 4u + c) * 16u) : make_uint4(0, 0, 0, 0);
+        rec8_math<MT, PACK>(acc[0], q, b, bsel);
+      }
+    }
+    for (uint32_t k = 0; !Q8 && ok && k < wn; k += 2) {
       const uint32_t gA = wa + k, gB = k + 1u < wn ? gA + 1u : gA;   // positions in the slice
       const bool two = k + 1u < wn;
       Rec q0, q1;
@@ -265,26 +345,30 @@ __global__ void __launch_bounds__(kV5Threads, 2) gemv_q4_v5(const __grid_constan
 
 typedef void (*V5Kernel)(const GemvParams, const V5Plan);
 template <int MT>
-V5Kernel v5_kernel_m(bool pair) { return pair ? gemv_q4_v5<MT, true> : gemv_q4_v5<MT, false>; }
-V5Kernel v5_kernel_for(uint32_t M, bool pair) {
+V5Kernel v5_kernel_m(bool pair, bool q8) {
+  return q8 ? (pair ? gemv_q4_v5<MT, true, true> : gemv_q4_v5<MT, false, true>)
+            : (pair ? gemv_q4_v5<MT, true, false> : gemv_q4_v5<MT, false, false>);
+}
+V5Kernel v5_kernel_for(uint32_t M, bool pair, bool q8) {
   switch (M) {
-    case 1: return v5_kernel_m<1>(pair);
-    case 2: return v5_kernel_m<2>(pair);
-    case 3: return v5_kernel_m<3>(pair);
-    case 4: return v5_kernel_m<4>(pair);
-    case 5: return v5_kernel_m<5>(pair);
-    case 6: return v5_kernel_m<6>(pair);
-    case 7: return v5_kernel_m<7>(pair);
-    default: return v5_kernel_m<8>(pair);
+    case 1: return v5_kernel_m<1>(pair, q8);
+    case 2: return v5_kernel_m<2>(pair, q8);
+    case 3: return v5_kernel_m<3>(pair, q8);
+    case 4: return v5_kernel_m<4>(pair, q8);
+    case 5: return v5_kernel_m<5>(pair, q8);
+    case 6: return v5_kernel_m<6>(pair, q8);
+    case 7: return v5_kernel_m<7>(pair, q8);
+    default: return v5_kernel_m<8>(pair, q8);
   }
 }
 }  // namespace
 
 bool v5_plan(const GemvParams &p, uint32_t nsplit, int sms, V5Plan *pl) {
-  const uint32_t G = p.K / 32;
+  const bool q8 = p.q8 != 0;
+  const uint32_t GK = q8 ? 64u : 32u, G = p.K / GK;
   const bool pair = p.epi == P0_EPI_GEGLU;
   if (G == 0 || p.wG < G || (pair && nsplit != 1)) return false;
-  const uint32_t ntile = p.N / 64, Gs = p.kPer / 32 < G ? p.kPer / 32 : G;
+  const uint32_t ntile = p.N / 64, Gs = p.kPer / GK < G ? p.kPer / GK : G;
   const uint64_t units = pair ? ntile : (uint64_t)ntile * nsplit;
   const uint32_t nu = pair ? G : Gs;   // records per unit (per half for geglu)
   // the smallest cluster that reaches a CTA count, within the staging and shared-memory limits: one CTA per SM for
@@ -299,11 +383,12 @@ bool v5_plan(const GemvParams &p, uint32_t nsplit, int sms, V5Plan *pl) {
     const uint32_t parts = pair ? CS / 2u : CS;
     if (parts > nu) break;
     const uint32_t nmax = (nu + parts - 1) / parts;
-    if (nmax * p.M * 4 > kV5XUnits * kV5Threads || v5_smem(p.M, nmax) > 200u * 1024u) continue;
+    if (nmax * p.M * (q8 ? 8u : 4u) > kV5XUnits * kV5Threads || v5_smem(p.M, nmax, q8) > 200u * 1024u) continue;
     best = CS;
     if (units * CS >= target) break;
   }
-  if (!best || units * best > (uint64_t)sms * 8) return false;   // many tiles: the streaming kernels take them
+  // many tiles: the streaming kernels take q4 calls; q8 calls have only this kernel, in as many waves as they need
+  if (!best || (!q8 && units * best > (uint64_t)sms * 8)) return false;
   const uint32_t parts = pair ? best / 2u : best;
   pl->CS = best; pl->nsplit = nsplit; pl->Gs = Gs; pl->G = G; pl->ntile = ntile; pl->pair = pair;
   pl->nmax = (nu + parts - 1) / parts;
@@ -312,8 +397,8 @@ bool v5_plan(const GemvParams &p, uint32_t nsplit, int sms, V5Plan *pl) {
 }
 
 cudaError_t launch_v5(const GemvParams &p, const V5Plan &pl, cudaStream_t s) {
-  V5Kernel k = v5_kernel_for(p.M, pl.pair != 0);
-  const size_t smem = v5_smem(p.M, pl.nmax);
+  V5Kernel k = v5_kernel_for(p.M, pl.pair != 0, p.q8 != 0);
+  const size_t smem = v5_smem(p.M, pl.nmax, p.q8 != 0);
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   return launch_pdl(k, dim3(pl.units * pl.CS), dim3(kV5Threads), smem, s, pl.CS, p, pl);
 }
