@@ -49,7 +49,10 @@ using Cfg1 = GemmCfg<16, 5, 256, 1>;
 using Cfg2 = GemmCfg<8, 4, 128, 2>;
 using Cfg3 = GemmCfg<16, 6, 256, 1>;   // Cfg1 with a sixth stage (223 KB of shared memory, 448 TMEM columns)
 constexpr int kDqPerStage = 8;  // dequant warps that fill one stage
-constexpr uint32_t kWStage = 2u * 2u * 1280u;                        // weights of a stage: 2 row tiles x 2 groups
+// weights of a stage: q4 2 row tiles x 2 groups of 1280 B; q8 2 row tiles x 1 group of 4224 B (= the gathered layout's
+// 128 rows x 2 halves x 32 code bytes + 128 scales x 2 B + 256 B)
+template <bool Q8> __host__ __device__ constexpr uint32_t w_stage() { return Q8 ? 2u * 4224u : 2u * 2u * 1280u; }
+constexpr uint32_t kWStage = w_stage<false>();
 
 struct GemmParams {
   const uint8_t *W;   // weight view base
@@ -115,6 +118,30 @@ __device__ __forceinline__ void deq_row16(const uint4 c, uint32_t sm, uint32_t (
   }
 }
 
+// q8 (gemm.js:150-160: f16(f32(q) * s)): 32 codes of one row (byte i = k i) -> 16 fp16 pairs. A code becomes exact fp16
+// by an xor with 0x80, a byte permute against 0x64 ((1024 + q + 128) in fp16) and a subtract of 1152; q * s is exact
+// in f32 (8 x 11 significant bits), so one fp16 multiply rounds it exactly as the reference's conversion does.
+__device__ __forceinline__ uint32_t q8_pair_f16(uint32_t u, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(u), "r"(0x64646464u), "r"(sel));
+  return hsub2_u32(d, 0x64806480u);
+}
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ void deq_row16_q8(const uint4 c0, const uint4 c1, uint32_t sbits, uint32_t (&r)[16]) {
+  const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  const uint32_t s2 = (sbits & 0xffffu) * 0x10001u;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const uint32_t u = w[i] ^ 0x80808080u;
+    r[2 * i] = hmul2_u32(q8_pair_f16(u, 0x4140u), s2);
+    r[2 * i + 1] = hmul2_u32(q8_pair_f16(u, 0x4342u), s2);
+  }
+}
+
 __device__ __forceinline__ uint4 ldg_w(const void *p) {
   uint4 v;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
@@ -171,9 +198,10 @@ __device__ __forceinline__ void cta_tiles(const GemmParams &p, uint32_t nB, uint
   t1 = t1 < nt ? t1 : nt - 1;
 }
 
-template <class C>
+template <class C, bool Q8>
 __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const __grid_constant__ CUtensorMap tmx, const GemmParams p) {
   constexpr int kStages = C::kStages, kDqWarps = C::kDqWarps;
+  constexpr uint32_t kWStage = w_stage<Q8>();
   constexpr uint32_t kAcol = C::kAcol, kTmemCols = C::kTmemCols;
   constexpr size_t kXStage = C::kXStage, kRingBytes = C::kRingBytes;
   static_assert((size_t)C::kMaxBT * 128 * 4 <= C::kRingBytes, "the epilogue stages [BT][128] f32 in the X ring");
@@ -192,7 +220,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t BT = p.BT, nk = p.nk, nB = blockIdx.x * kBW, m0 = blockIdx.y * BT;
   const uint32_t xbytes = BT * kBK * 2;
-  const uint32_t g0 = p.wk0 / 32u;
+  const uint32_t g0 = p.wk0 / (Q8 ? 64u : 32u);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; s++) {
@@ -226,12 +254,36 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
       if (!__shfl_sync(0xffffffffu, (int)got, 0)) break;
       uint8_t *ws = wring + (size_t)slot * kWStage;
       const uint32_t ng = min(2u, (p.K - s * kBK) / 32u);   // groups in this stage (the last may hold one)
-      if (p.wtma) {
+      if (p.wtma && Q8) {
+        if (lane == 0) {   // one q8 record of each row tile: the stage's 64 k
+          tc::mbar_expect_tx(&full[slot], xbytes + 2u * 4224u);
+          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), (int32_t)m0);
+          bulk_g2s(ws, p.W + ((size_t)t0 * p.wG + g0 + s) * 4224u, 4224u, &full[slot]);
+          bulk_g2s(ws + 4224u, p.W + ((size_t)t1 * p.wG + g0 + s) * 4224u, 4224u, &full[slot]);
+        }
+      } else if (p.wtma) {
         if (lane == 0) {
           tc::mbar_expect_tx(&full[slot], xbytes + 2u * ng * 1280u);
           tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), (int32_t)m0);
           bulk_g2s(ws, p.W + ((size_t)t0 * p.wG + g0 + 2u * s) * 1280u, ng * 1280u, &full[slot]);
           bulk_g2s(ws + 2560u, p.W + ((size_t)t1 * p.wG + g0 + 2u * s) * 1280u, ng * 1280u, &full[slot]);
+        }
+      } else if (Q8) {
+        // q8 rows that are not whole tiles: [h][lane] 32 code bytes, then one scale per row
+        for (uint32_t i = 0; i < 4; i++) {
+          const uint32_t nl = i * 32u + lane, row = weight_row(p, nB, nl);
+          const uint8_t *rec = p.W + ((size_t)(row >> 6) * p.wG + g0 + s) * 4224u;
+          for (uint32_t h = 0; h < ng; h++) {
+            const uint8_t *src = rec + (row & 63u) * 64u + h * 32u;
+            *reinterpret_cast<uint4 *>(ws + (h * 128u + nl) * 32u) = ldg_w(src);
+            *reinterpret_cast<uint4 *>(ws + (h * 128u + nl) * 32u + 16u) = ldg_w(src + 16);
+          }
+          *reinterpret_cast<uint16_t *>(ws + 8192u + nl * 2u) = *reinterpret_cast<const uint16_t *>(rec + 4096u + (row & 63u) * 2u);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_expect_tx(&full[slot], xbytes);
+          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), (int32_t)m0);
         }
       } else {
         // rows that are not whole tiles: the warp gathers them into lane order ([h][lane] 16-byte codes, then tails)
@@ -284,7 +336,16 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
     const uint32_t tq = tmem + ((q * 32u) << 16);
     // where this thread's 16 code bytes and (s, mn) word sit in a weight stage
     uint32_t code_off, tail_off;
-    if (p.wtma) {
+    if (Q8) {
+      if (p.wtma) {
+        const uint32_t ts = p.epi == P0_GEPI_SWIGLU ? (nl & 1u) : (nl >> 6), r = p.epi == P0_GEPI_SWIGLU ? (nl >> 1) : (nl & 63u);
+        code_off = ts * 4224u + r * 64u + h * 32u;
+        tail_off = ts * 4224u + 4096u + r * 2u;
+      } else {
+        code_off = (h * 128u + nl) * 32u;
+        tail_off = 8192u + nl * 2u;
+      }
+    } else if (p.wtma) {
       const uint32_t ts = p.epi == P0_GEPI_SWIGLU ? (nl & 1u) : (nl >> 6), r = p.epi == P0_GEPI_SWIGLU ? (nl >> 1) : (nl & 63u);
       code_off = ts * 2560u + h * 1280u + r * 16u;
       tail_off = ts * 2560u + h * 1280u + 1024u + r * 4u;
@@ -300,7 +361,11 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
       uint32_t r[16];
       if (s * kBK + h * 32u < p.K) {
         const uint8_t *ws = wring + (size_t)slot * kWStage;
-        deq_row16(*reinterpret_cast<const uint4 *>(ws + code_off), *reinterpret_cast<const uint32_t *>(ws + tail_off), r);
+        if (Q8)
+          deq_row16_q8(*reinterpret_cast<const uint4 *>(ws + code_off), *reinterpret_cast<const uint4 *>(ws + code_off + 16u),
+                       *reinterpret_cast<const uint16_t *>(ws + tail_off), r);
+        else
+          deq_row16(*reinterpret_cast<const uint4 *>(ws + code_off), *reinterpret_cast<const uint32_t *>(ws + tail_off), r);
       } else {
 #pragma unroll
         for (int i = 0; i < 16; i++) r[i] = 0u;   // k beyond K: zero weights (X is zero-filled there as well)
@@ -431,6 +496,22 @@ __global__ void deq_dump_q4(const uint8_t *W, uint32_t rows, uint32_t cols, uint
   for (int i = 0; i < 16; i++) o[i] = r[i];
 }
 
+// the q8 dequantiser of the GEMM, dumped: out[row][k] = f16(q*s) for a q8 view, one thread per (row, 32-k half group)
+__global__ void deq_dump_q8(const uint8_t *W, uint32_t rows, uint32_t cols, uint32_t wG, uint16_t *out) {
+  const uint32_t H = cols / 32;
+  const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (uint64_t)rows * H) return;
+  const uint32_t row = (uint32_t)(idx / H), hh = (uint32_t)(idx % H), g = hh / 2, h = hh % 2;
+  const uint8_t *rec = W + ((size_t)(row >> 6) * wG + g) * 4224u;
+  const uint8_t *src = rec + (row & 63u) * 64u + h * 32u;
+  uint32_t r[16];
+  deq_row16_q8(*reinterpret_cast<const uint4 *>(src), *reinterpret_cast<const uint4 *>(src + 16),
+               *reinterpret_cast<const uint16_t *>(rec + 4096u + (row & 63u) * 2u), r);
+  uint32_t *o = reinterpret_cast<uint32_t *>(out + (size_t)row * cols + (size_t)hh * 32u);
+#pragma unroll
+  for (int i = 0; i < 16; i++) o[i] = r[i];
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -458,18 +539,21 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   const uint32_t enc = a->w.enc;
   if (enc != P0_ENC_Q4G32A_T64 && enc != P0_ENC_Q8G64S_T64 && enc != P0_ENC_F16)
     return p0_fail(c, P0_EINVAL, "gemm: unsupported weight encoding %u", enc);
-  if (enc != P0_ENC_Q4G32A_T64) return p0_fail(c, P0_EINVAL, "gemm: weight encoding %s is not built in this library yet", enc == 2 ? "q8g64s.t64" : "f16");
+  if (enc == P0_ENC_F16) return p0_fail(c, P0_EINVAL, "gemm: weight encoding f16 is not built in this library yet");
+  const bool q8 = enc == P0_ENC_Q8G64S_T64;
+  const uint32_t GK = q8 ? 64u : 32u, RB = q8 ? 4224u : 1280u;
   const uint32_t M = a->M, N = a->N, K = a->K;
   if (K % 32) return p0_fail(c, P0_EINVAL, "gemm: K must be a multiple of 32");
   if (a->epi > P0_GEPI_SWIGLU) return p0_fail(c, P0_EINVAL, "gemm: epilogue %u is not built in this library yet", a->epi);
   if (a->acc != 0) return p0_fail(c, P0_EINVAL, "gemm: acc 'f16' (fp16 partial sums) is not built; the tensor cores accumulate in f32");
   if (a->post_gelu && a->epi != P0_GEPI_BIAS) return p0_fail(c, P0_EINVAL, "gemm: post_gelu applies to the 'bias' epilogue only");
   if (!M || !N || !K) return P0_OK;
-  if (a->w.rows == 0 || a->w.cols % 32 || a->wk0 % 32 || a->wk0 + K > a->w.cols)
-    return p0_fail(c, P0_EINVAL, "gemm: weight view %ux%u does not cover k [%u, %u) in whole 32-k groups", a->w.rows, a->w.cols, a->wk0, a->wk0 + K);
-  if (a->w.rows % 64) return p0_fail(c, P0_EINVAL, "gemm: q4g32a.t64 rows must be a multiple of 64");
+  if (a->w.rows == 0 || a->w.cols % GK || a->wk0 % GK || a->wk0 + K > a->w.cols)
+    return p0_fail(c, P0_EINVAL, "gemm: weight view %ux%u does not cover k [%u, %u) in whole %u-k groups", a->w.rows, a->w.cols, a->wk0,
+                   a->wk0 + K, GK);
+  if (a->w.rows % 64) return p0_fail(c, P0_EINVAL, "gemm: %s rows must be a multiple of 64", q8 ? "q8g64s.t64" : "q4g32a.t64");
   if (N % 4) return p0_fail(c, P0_EALIGN, "gemm: N must be a multiple of 4 (the reference stores whole vec4s)");
-  const uint32_t ldx = a->x_ld ? a->x_ld : K, ldy = a->y_ld ? a->y_ld : N, wG = a->w.cols / 32;
+  const uint32_t ldx = a->x_ld ? a->x_ld : K, ldy = a->y_ld ? a->y_ld : N, wG = a->w.cols / GK;
   const bool swi = a->epi == P0_GEPI_SWIGLU, f32y = a->epi == P0_GEPI_F32 || a->epi == P0_GEPI_RESADD;
   const uint32_t es = f32y ? 4 : 2, ncols_out = swi ? N / 2 : N;
   if (ldx % 8 || (a->x_off + 2ull * a->x_k0) % 16)
@@ -477,7 +561,7 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   if (ldy % 4 || a->y_n0 % 4 || a->y_off % (4 * es)) return p0_fail(c, P0_EALIGN, "gemm: y must be vec4-aligned (ld %% 4, n0 %% 4, off)");
   p0_status st;
   P0Range rw, rx, ry, re, rb;
-  if ((st = p0_range(c, a->w.buf, a->w.off, (uint64_t)(a->w.rows / 64) * wG * 1280u, op, "W", &rw))) return st;
+  if ((st = p0_range(c, a->w.buf, a->w.off, (uint64_t)(a->w.rows / 64) * wG * RB, op, "W", &rw))) return st;
   if ((uintptr_t)rw.base % 16) return p0_fail(c, P0_EALIGN, "gemm: weight offset must be 16-byte aligned");
   if ((st = p0_range(c, a->x, a->x_off, ((uint64_t)(M - 1) * ldx + a->x_k0 + K) * 2, op, "X", &rx))) return st;
   if ((st = p0_range(c, a->y, a->y_off, ((uint64_t)(M - 1) * ldy + a->y_n0 + ncols_out) * es, op, "Y", &ry))) return st;
@@ -514,21 +598,23 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   // bulk-copy weight path: every CTA's 128 lanes read two whole 64-row tiles
   p.wtma = swi ? (a->wr0 % 64 == 0 && a->wr1 % 64 == 0 && (N / 2) % 64 == 0) : (a->wr0 % 64 == 0);
   cudaSetDevice(c->device);
-  if (cfg3) {
+  dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
+  if (q8) {   // q8 weights: Cfg1's shape
+    const size_t smem = Cfg1::kRingBytes + (size_t)Cfg1::kStages * w_stage<true>() + 1024 + 256;
+    cudaFuncSetAttribute(gemm_q4_tc<Cfg1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    gemm_q4_tc<Cfg1, true><<<grid, Cfg1::kThreads, smem, c->stream>>>(tm, p);
+  } else if (cfg3) {
     const size_t smem = Cfg3::kRingBytes + (size_t)Cfg3::kStages * kWStage + 1024 + 256;
-    cudaFuncSetAttribute(gemm_q4_tc<Cfg3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
-    gemm_q4_tc<Cfg3><<<grid, Cfg3::kThreads, smem, c->stream>>>(tm, p);
+    cudaFuncSetAttribute(gemm_q4_tc<Cfg3, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    gemm_q4_tc<Cfg3, false><<<grid, Cfg3::kThreads, smem, c->stream>>>(tm, p);
   } else if (cfg2) {
     const size_t smem = Cfg2::kRingBytes + (size_t)Cfg2::kStages * kWStage + 1024 + 256;
-    cudaFuncSetAttribute(gemm_q4_tc<Cfg2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
-    gemm_q4_tc<Cfg2><<<grid, Cfg2::kThreads, smem, c->stream>>>(tm, p);
+    cudaFuncSetAttribute(gemm_q4_tc<Cfg2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    gemm_q4_tc<Cfg2, false><<<grid, Cfg2::kThreads, smem, c->stream>>>(tm, p);
   } else {
     const size_t smem = Cfg1::kRingBytes + (size_t)Cfg1::kStages * kWStage + 1024 + 256;
-    cudaFuncSetAttribute(gemm_q4_tc<Cfg1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
-    gemm_q4_tc<Cfg1><<<grid, Cfg1::kThreads, smem, c->stream>>>(tm, p);
+    cudaFuncSetAttribute(gemm_q4_tc<Cfg1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    gemm_q4_tc<Cfg1, false><<<grid, Cfg1::kThreads, smem, c->stream>>>(tm, p);
   }
   if ((st = p0_launched(c, "gemm"))) return st;
   if (flops) *flops = 2.0 * M * N * K;
@@ -538,17 +624,20 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
 
 p0_status p0_dequant_f16(p0_ctx *c, const p0_wview *w, p0_buf out) {
   if (!c || !w) return P0_EINVAL;
-  if (w->enc != P0_ENC_Q4G32A_T64) return p0_fail(c, P0_EINVAL, "dequant: encoding %u is not built in this library yet", w->enc);
-  if (w->rows % 64 || w->cols % 32) return p0_fail(c, P0_EINVAL, "dequant: q4g32a.t64 needs rows %% 64 and cols %% 32");
+  const bool q8 = w->enc == P0_ENC_Q8G64S_T64;
+  if (w->enc != P0_ENC_Q4G32A_T64 && !q8) return p0_fail(c, P0_EINVAL, "dequant: encoding %u is not built in this library yet", w->enc);
+  const uint32_t GK = q8 ? 64u : 32u, RB = q8 ? 4224u : 1280u;
+  if (w->rows % 64 || w->cols % GK) return p0_fail(c, P0_EINVAL, "dequant: needs rows %% 64 and cols %% %u", GK);
   p0_status st;
   P0Range rw, ro;
-  const uint32_t wG = w->cols / 32;
-  if ((st = p0_range(c, w->buf, w->off, (uint64_t)(w->rows / 64) * wG * 1280u, "dequant", "W", &rw))) return st;
+  const uint32_t wG = w->cols / GK;
+  if ((st = p0_range(c, w->buf, w->off, (uint64_t)(w->rows / 64) * wG * RB, "dequant", "W", &rw))) return st;
   if ((uintptr_t)rw.base % 16) return p0_fail(c, P0_EALIGN, "dequant: weight offset must be 16-byte aligned");
   if ((st = p0_range(c, out, 0, (uint64_t)w->rows * w->cols * 2, "dequant", "out", &ro))) return st;
-  const uint64_t n = (uint64_t)w->rows * wG;
+  const uint64_t n = (uint64_t)w->rows * (w->cols / 32);
   cudaSetDevice(c->device);
-  deq_dump_q4<<<(unsigned)((n + 255) / 256), 256, 0, c->stream>>>(rw.base, w->rows, w->cols, wG, (uint16_t *)ro.base);
+  if (q8) deq_dump_q8<<<(unsigned)((n + 255) / 256), 256, 0, c->stream>>>(rw.base, w->rows, w->cols, wG, (uint16_t *)ro.base);
+  else deq_dump_q4<<<(unsigned)((n + 255) / 256), 256, 0, c->stream>>>(rw.base, w->rows, w->cols, wG, (uint16_t *)ro.base);
   return p0_launched(c, "dequant");
 }
 

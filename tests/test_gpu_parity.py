@@ -346,6 +346,8 @@ def run_gemm(g, b, X16, M, N, K, y_init=None, y_bytes=None, **a):
     yb = g.upload(y_init) if y_init is not None else g.upload(np.full(nb // 2, 0x7E00, np.uint16))
     args = {"w": wview(wb, a.pop("rows", N), a.pop("cols", K)), "x": {"buf": xb, **a.pop("x", {})}, "M": M, "N": N, "K": K,
             "y": {"buf": yb, **a.pop("y", {})}}
+    if "enc" in a:
+        args["w"]["enc"] = a.pop("enc")
     for k in ("ev", "bv"):
         if k in a:
             v = a.pop(k)

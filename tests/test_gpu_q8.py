@@ -94,3 +94,51 @@ def test_gemvM_q8_geglu(g, M):
                  "pro": "rms", "epi": "geglu", "norm": {"buf": g.upload(nw), "off": 0}, "stat": {"buf": g.upload(st), "off": 0, "ld": 1}})
     want, _, _ = ref.gemvM(b, X, M, N, K, enc=Q8, pro="rms", epi="geglu", norm=nw, stat=st, stat_off=0, stat_ld=1)
     assert_close(g.read(yb, 0, M * N * 4, np.float32), want)
+
+
+# ---------------------------------------------------------------- GEMM over q8 weights (gemm.js:150-160)
+from .test_gpu_parity import run_gemm  # noqa: E402
+
+
+@pytest.mark.parametrize("N,K", [(64, 128), (192, 1024)])
+def test_dequant_q8_bit_exact(g, N, K):
+    W = ref.randn(N * K, 740, 0.05)
+    W[:64] = 0.0
+    W[K:K + 64] = np.linspace(-1e-6, 1e-6, 64, dtype=np.float32)   # subnormal scale: subnormal products
+    b, _ = ref.pack_q8(W, N, K)
+    out = g.buffer(N * K * 2)
+    p0.dequant_f16(g, q8view(g.upload(b), N, K), out)
+    assert np.array_equal(g.read(out, 0, N * K * 2, np.uint16), ref.deq16(b, N, K, enc=Q8).ravel())
+
+
+@pytest.mark.parametrize("M,N,K", [(32, 128, 256), (300, 384, 320), (129, 256, 2048), (4, 128, 64), (64, 256, 96)])
+def test_gemm_q8_f16(g, M, N, K):
+    Kw = -(-K // 64) * 64                      # the weight's columns cover K in whole 64-k groups
+    b, _ = ref.pack_q8(ref.randn(N * Kw, 750 + M, 0.02), N, Kw)
+    X = ref.f2h(ref.round_f16(ref.randn(M * K, 751)))
+    y = run_gemm(g, b, X, M, N, K, enc=Q8, cols=Kw)
+    want = ref.gemm(b, X, M, N, K, enc=Q8, cols=Kw)
+    assert_close(ref.h2f(y), ref.h2f(want))
+
+
+def test_gemm_q8_bias_gelu_and_swiglu(g):
+    M, N, K = 200, 512, 1024
+    b, _ = ref.pack_q8(ref.randn(N * K, 760, 0.02), N, K)
+    X = ref.f2h(ref.round_f16(ref.randn(M * K, 761)))
+    bias = ref.randn(N, 762, 0.01)
+    y = run_gemm(g, b, X, M, N, K, enc=Q8, epi="bias", ev=(bias, 0), post_gelu=True)
+    assert_close(ref.h2f(y), ref.h2f(ref.gemm(b, X, M, N, K, enc=Q8, epi="bias", ev=bias, post_gelu=True)))
+    # swiglu: gate rows [0, N/2), up rows [N/2, N), interleaved by the kernel as the reference's wrow() does
+    y = run_gemm(g, b, X, M, N, K, enc=Q8, epi="swiglu", act="gelu", wr0=0, wr1=N // 2, y={"ld": N // 2})
+    want = ref.gemm(b, X, M, N, K, enc=Q8, epi="swiglu", act="gelu", wr0=0, wr1=N // 2, ldy=N // 2)
+    assert_close(ref.h2f(y), ref.h2f(want))
+
+
+def test_gemm_q8_row_and_k_offsets(g):
+    # a weight sub-view: rows from 64 on (whole tiles) and k from 64 on; x from its column 64
+    M, N, K, Nw, Kw = 96, 256, 512, 384, 640
+    b, _ = ref.pack_q8(ref.randn(Nw * Kw, 770, 0.02), Nw, Kw)
+    X = ref.f2h(ref.round_f16(ref.randn(M * Kw, 771)))
+    y = run_gemm(g, b, X, M, N, K, enc=Q8, rows=Nw, cols=Kw, wr0=64, wk0=64, x={"ld": Kw, "k0": 64})
+    want = ref.gemm(b, X, M, N, K, enc=Q8, rows=Nw, cols=Kw, ldx=Kw, kx0=64, wr0=64, wk0=64)
+    assert_close(ref.h2f(y), ref.h2f(want))
