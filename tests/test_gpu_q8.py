@@ -1,7 +1,8 @@
-"""q8g64s.t64 on the GPU: the device packQ8 bit for bit against the oracle (engine/kcheck.js:40-53 restated), and the
+"""q8g64s.t64 on the GPU: the device packQ8 bit for bit against the oracle (engine/kcheck.js:40-53 restated); the
 GEMV / gemvM over q8 weights (the lgemv / lgemvM q8 arithmetic of lops.js:72-81, lops_spec.js restated) within the
-parity tolerance, for the forms the reference's 8-bit layers use: raw and rms prologues, store / softcap / geglu
-epilogues, k-splits, M up to 8."""
+parity tolerance, for the forms the reference's 8-bit layers use (raw and rms prologues, store / softcap / geglu
+epilogues, k-splits, M up to 8); and the GEMM over q8 weights (gemm.js:150-160): its dequantised weights bit for bit,
+its outputs within the tolerance, on whole-tile and gathered row views."""
 import numpy as np
 import pytest
 
@@ -142,3 +143,12 @@ def test_gemm_q8_row_and_k_offsets(g):
     y = run_gemm(g, b, X, M, N, K, enc=Q8, rows=Nw, cols=Kw, wr0=64, wk0=64, x={"ld": Kw, "k0": 64})
     want = ref.gemm(b, X, M, N, K, enc=Q8, rows=Nw, cols=Kw, ldx=Kw, kx0=64, wr0=64, wk0=64)
     assert_close(ref.h2f(y), ref.h2f(want))
+
+
+def test_gemm_q8_gathered_rows(g):
+    # rows from 32 on: not whole 64-row tiles, so the producer gathers each row's codes and scale
+    M, N, K, Nw = 70, 128, 256, 256
+    b, _ = ref.pack_q8(ref.randn(Nw * K, 780, 0.02), Nw, K)
+    X = ref.f2h(ref.round_f16(ref.randn(M * K, 781)))
+    y = run_gemm(g, b, X, M, N, K, enc=Q8, rows=Nw, wr0=32)
+    assert_close(ref.h2f(y), ref.h2f(ref.gemm(b, X, M, N, K, enc=Q8, rows=Nw, wr0=32)))
