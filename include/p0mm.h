@@ -160,7 +160,8 @@ enum { P0_ACT_SILU = 0, P0_ACT_GELU = 1 };
  * bv {buf, off (floats), up} (resadd / swiglu bias); res; store.
  * post_gelu (bias epilogue only) applies engine/ops/misc.js ew op 'gelu' to the fp16 result in the same pass:
  * the pair gemm(epi:'bias') -> ew(op:'gelu') of pocketflux-engine.js:3052-3053 as one call.
- * acc: 0 = 'f32' (the only mode the tensor-core path computes; 'f16' partial sums are rejected). */
+ * acc: 0 = 'f32' (the only mode the tensor-core path computes; 'f16' partial sums are rejected).
+ * The f32 x prologues run as a pass that writes the fp16 X into the context's workspace (M*K*2 bytes), then the GEMM. */
 typedef struct {
   p0_wview w;
   p0_buf x;  uint64_t x_off; uint32_t x_ld, x_k0;
@@ -171,7 +172,14 @@ typedef struct {
   p0_buf ev; uint32_t ev_off;
   p0_buf bv; uint32_t bv_off, bv_up;
   uint32_t res, store, post_gelu;
+  /* x prologue (gemm.js:55-63): P0_XPRO_F16 (x fp16, the default), or an f32 x turned into fp16 per element:
+   * P0_XPRO_LNMOD f16(((x - mean) * rstd) * (1 + pv[k]) + pv[pv_stride + k]), P0_XPRO_RMS f16((x * rstd) * pv[k]), with
+   * {mean, rstd} = stats[(stats_off + m) * 2 ..] (rows of ops/misc.js rowstats) and k counted from x.k0; x.ld in floats */
+  uint32_t x_mode;
+  p0_buf stats; uint32_t stats_off;
+  p0_buf pv;    uint32_t pv_off, pv_stride;
 } p0_gemm_args;
+enum { P0_XPRO_F16 = 0, P0_XPRO_LNMOD = 1, P0_XPRO_RMS = 2 };
 p0_status p0_gemm(p0_ctx *ctx, const p0_gemm_args *a, double *flops);
 
 /* ---------------------------------------------------------------------------------------------- quantiser */

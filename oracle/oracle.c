@@ -483,3 +483,31 @@ int or_max_threads(void) {
 void or_f2h_arr(const double *x, int64_t n, uint16_t *o) { for (int64_t i = 0; i < n; i++) o[i] = or_f2h(x[i]); }
 void or_h2f_arr(const uint16_t *h, int64_t n, double *o) { for (int64_t i = 0; i < n; i++) o[i] = or_h2f(h[i]); }
 void or_hfma_arr(const uint16_t *a, const uint16_t *b, const uint16_t *c, int64_t n, uint16_t *o) { for (int64_t i = 0; i < n; i++) o[i] = hfma(a[i], b[i], c[i]); }
+
+/* ------------------------------------------------------------------ GEMM x prologues (ops/gemm.js:55-63)
+ * The fp16 X the reference's xload() yields for the f32 x modes: row m, k = 0..K-1 of X f32 [row * ldx + kx0 + k],
+ * stats ST[(statOff + m) * 2] = {mean, rstd}, vectors PV (scale at pvOff, shift at pvOff + pvStride, indexed by
+ * kx0 + k), in the WGSL's order of operations:
+ *   lnmod: f16(((x - mean) * rstd) * (1 + PV[pvOff + k']) + PV[pvOff + pvStride + k'])
+ *   rms:   f16((x * rstd) * PV[pvOff + k'])                                        (k' = kx0 + k) */
+void or_gemm_xpro(int mode, const float *X, uint32_t M, uint32_t K, uint32_t ldx, uint32_t kx0, const float *ST, uint32_t statOff,
+                  const float *PV, uint32_t pvOff, uint32_t pvStride, uint16_t *out) {
+  for (uint32_t m = 0; m < M; m++) {
+    const float mean = ST[(size_t)(statOff + m) * 2], rstd = ST[(size_t)(statOff + m) * 2 + 1];
+    for (uint32_t k = 0; k < K; k++) {
+      const uint32_t kk = kx0 + k;
+      const float x = X[(size_t)m * ldx + kk];
+      float v;
+      if (mode == 1) {
+        v = x - mean;
+        v = v * rstd;
+        v = v * (1.0f + PV[pvOff + kk]);
+        v = v + PV[pvOff + pvStride + kk];
+      } else {
+        v = x * rstd;
+        v = v * PV[pvOff + kk];
+      }
+      out[(size_t)m * K + k] = or_f2h((double)v);
+    }
+  }
+}

@@ -58,6 +58,7 @@ def lib():
         L.or_gemv.argtypes = [_i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp] + [_u32] * 11 + [ctypes.c_float] + [_u32] * 4
         L.or_gemvM.argtypes = [_i, _i, _i, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _vp] + [_u32] * 14 + [ctypes.c_float] + [_u32] * 4
         L.or_gemm.argtypes = [_i] * 9 + [_vp] * 5 + [_u32] * 15 + [_i]
+        L.or_gemm_xpro.argtypes = [_i, _f32p, _u32, _u32, _u32, _u32, _f32p, _u32, _f32p, _u32, _u32, _u16p]
         L.or_dot64.argtypes = [_f32p, _f64p, _i64, _i64, _i64, _f64p]
         L.or_gemv_cpu_mt.argtypes = [_f32p, _u32p, _f32p, _u32, _u32, _u32, _u32, _i]
         L.or_max_threads.restype = _i
@@ -268,6 +269,15 @@ def gemm(W, X16, M, N, K, *, enc="q4g32a.t64", rows=None, cols=None, ldx=None, k
                   _p(_f32(ev) if ev is not None else dummy), _p(_f32(bv) if bv is not None else dummy),
                   M, N, K, ldx, kx0, wr0, wr1, wG, wk0, ldy, ny0, rows, ev_off, bv_off, bv_up, int(threads))
     return Y
+
+
+def gemm_xpro(mode, X, M, K, *, ldx=None, kx0=0, stats=None, stat_off=0, pv=None, pv_off=0, pv_stride=0):
+    """the fp16 X [M][K] of gemm()'s f32 x prologues (gemm.js:55-63): mode 'lnmod' or 'rms'; stats = ST f32 rows of
+    {mean, rstd}; pv = the scale (and, for lnmod, shift at pv_off + pv_stride) vectors. Returns uint16 fp16 bits."""
+    out = np.empty(M * K, np.uint16)
+    lib().or_gemm_xpro({"lnmod": 1, "rms": 2}[mode], _f32(X), M, K, ldx or K, kx0, _f32(stats), stat_off, _f32(pv), pv_off,
+                       pv_stride, out)
+    return out
 
 
 def dot64(deq, x, M, N, K):

@@ -17,6 +17,7 @@ PRO = {"raw": 0, "rms": 1, "sum": 2, "pleg": 3}
 EPI = {"store": 0, "geglu": 1, "softcap": 2}
 GEPI = {"f16": 0, "f32": 1, "bias": 2, "resadd": 3, "swiglu": 4}
 ACT = {"silu": 0, "gelu": 1}
+XPRO = {"f16": 0, "lnmod": 1, "rms": 2}
 
 # every symbol include/p0mm.h declares
 EXPORTS = ["p0_init", "p0_destroy", "p0_set_stream", "p0_set_overlap", "p0_last_error", "p0_stats", "p0_buffer", "p0_wrap", "p0_upload", "p0_read",
@@ -57,7 +58,8 @@ class p0_gemm_args(ctypes.Structure):
     _fields_ = [("w", p0_wview), ("x", p0_buf), ("x_off", ctypes.c_uint64), ("x_ld", _u32), ("x_k0", _u32), ("M", _u32),
                 ("N", _u32), ("K", _u32), ("wr0", _u32), ("wr1", _u32), ("wk0", _u32), ("epi", _u32), ("act", _u32), ("acc", _u32),
                 ("y", p0_buf), ("y_off", ctypes.c_uint64), ("y_ld", _u32), ("y_n0", _u32), ("ev", p0_buf), ("ev_off", _u32),
-                ("bv", p0_buf), ("bv_off", _u32), ("bv_up", _u32), ("res", _u32), ("store", _u32), ("post_gelu", _u32)]
+                ("bv", p0_buf), ("bv_off", _u32), ("bv_up", _u32), ("res", _u32), ("store", _u32), ("post_gelu", _u32),
+                ("x_mode", _u32), ("stats", p0_buf), ("stats_off", _u32), ("pv", p0_buf), ("pv_off", _u32), ("pv_stride", _u32)]
 
 
 _lib = None

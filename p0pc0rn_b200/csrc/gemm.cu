@@ -496,6 +496,41 @@ __global__ void deq_dump_q4(const uint8_t *W, uint32_t rows, uint32_t cols, uint
   for (int i = 0; i < 16; i++) o[i] = r[i];
 }
 
+// The f32 x prologues of gemm.js:55-63, as a pass that writes the fp16 X [M][K] the GEMM's TMA then reads: one thread
+// per 8 consecutive k of a row, the reference's order of operations (no contraction), round to nearest even.
+__global__ void gemm_xpro_kernel(int mode, const float *__restrict__ X, uint32_t ldx, uint32_t kx0, const float *__restrict__ ST,
+                                 uint32_t statOff, const float *__restrict__ PV, uint32_t pvOff, uint32_t pvStride, uint32_t M,
+                                 uint32_t K, uint16_t *__restrict__ out) {
+  const uint32_t K8 = K / 8;
+  const uint64_t n8 = (uint64_t)M * K8;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t m = (uint32_t)(i / K8), k = (uint32_t)(i % K8) * 8u;
+    const float mean = ST[(size_t)(statOff + m) * 2], rstd = ST[(size_t)(statOff + m) * 2 + 1];
+    const float *x = X + (size_t)m * ldx + kx0 + k;
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      float v[2];
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const uint32_t kk = kx0 + k + j + h;
+        float t;
+        if (mode == P0_XPRO_LNMOD) {
+          t = __fsub_rn(x[j + h], mean);
+          t = __fmul_rn(t, rstd);
+          t = __fmul_rn(t, __fadd_rn(1.0f, PV[pvOff + kk]));
+          t = __fadd_rn(t, PV[pvOff + pvStride + kk]);
+        } else {
+          t = __fmul_rn(__fmul_rn(x[j + h], rstd), PV[pvOff + kk]);
+        }
+        v[h] = t;
+      }
+      o[j / 2] = (uint32_t)__half_as_ushort(__float2half_rn(v[0])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[1])) << 16);
+    }
+    *reinterpret_cast<uint4 *>(out + (size_t)m * K + k) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // the q8 dequantiser of the GEMM, dumped: out[row][k] = f16(q*s) for a q8 view, one thread per (row, 32-k half group)
 __global__ void deq_dump_q8(const uint8_t *W, uint32_t rows, uint32_t cols, uint32_t wG, uint16_t *out) {
   const uint32_t H = cols / 32;
@@ -556,14 +591,24 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   const uint32_t ldx = a->x_ld ? a->x_ld : K, ldy = a->y_ld ? a->y_ld : N, wG = a->w.cols / GK;
   const bool swi = a->epi == P0_GEPI_SWIGLU, f32y = a->epi == P0_GEPI_F32 || a->epi == P0_GEPI_RESADD;
   const uint32_t es = f32y ? 4 : 2, ncols_out = swi ? N / 2 : N;
-  if (ldx % 8 || (a->x_off + 2ull * a->x_k0) % 16)
+  const uint32_t xmode = a->x_mode;
+  if (xmode > P0_XPRO_RMS) return p0_fail(c, P0_EINVAL, "gemm: x prologue %u is not built in this library yet", xmode);
+  if (xmode == P0_XPRO_F16 && (ldx % 8 || (a->x_off + 2ull * a->x_k0) % 16))
     return p0_fail(c, P0_EALIGN, "gemm: x rows must start on 16-byte boundaries (ld %% 8, off + 2*k0 %% 16)");
+  if (xmode != P0_XPRO_F16 && a->x_off % 4) return p0_fail(c, P0_EALIGN, "gemm: f32 x must start on a 4-byte boundary");
   if (ldy % 4 || a->y_n0 % 4 || a->y_off % (4 * es)) return p0_fail(c, P0_EALIGN, "gemm: y must be vec4-aligned (ld %% 4, n0 %% 4, off)");
   p0_status st;
   P0Range rw, rx, ry, re, rb;
   if ((st = p0_range(c, a->w.buf, a->w.off, (uint64_t)(a->w.rows / 64) * wG * RB, op, "W", &rw))) return st;
   if ((uintptr_t)rw.base % 16) return p0_fail(c, P0_EALIGN, "gemm: weight offset must be 16-byte aligned");
-  if ((st = p0_range(c, a->x, a->x_off, ((uint64_t)(M - 1) * ldx + a->x_k0 + K) * 2, op, "X", &rx))) return st;
+  if ((st = p0_range(c, a->x, a->x_off, ((uint64_t)(M - 1) * ldx + a->x_k0 + K) * (xmode == P0_XPRO_F16 ? 2 : 4), op, "X", &rx)))
+    return st;
+  P0Range rst, rpv;
+  if (xmode != P0_XPRO_F16) {
+    if ((st = p0_range(c, a->stats, 0, ((uint64_t)a->stats_off + M) * 8, op, "stats", &rst))) return st;
+    const uint64_t pvneed = (uint64_t)a->pv_off + (xmode == P0_XPRO_LNMOD ? a->pv_stride : 0) + a->x_k0 + K;
+    if ((st = p0_range(c, a->pv, 0, pvneed * 4, op, "pv", &rpv))) return st;
+  }
   if ((st = p0_range(c, a->y, a->y_off, ((uint64_t)(M - 1) * ldy + a->y_n0 + ncols_out) * es, op, "Y", &ry))) return st;
   const bool need_ev = a->epi == P0_GEPI_BIAS || (a->epi == P0_GEPI_RESADD && a->ev.id);
   if (need_ev && (st = p0_range(c, a->ev, 0, ((uint64_t)a->ev_off + N) * 4, op, "EV", &re))) return st;
@@ -578,12 +623,29 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   const uint32_t BT = M <= 64 ? 64u : (M <= 128 || cfg2) ? 128u : 256u;
   auto enc_fn = tensor_map_encoder();
   if (!enc_fn) return p0_fail(c, P0_EDEVICE, "gemm: cuTensorMapEncodeTiled is unavailable");
+  // the fp16 X the GEMM reads: x itself, or the prologue pass's output in the context workspace
+  const uint8_t *xbase = rx.base + 2ull * a->x_k0;
+  uint32_t xld = ldx;
+  if (xmode != P0_XPRO_F16) {
+    uint32_t *unused_cnt = nullptr;
+    void *scratch = nullptr;
+    if ((st = p0_workspace(c, 0, (size_t)M * K * 2, &unused_cnt, &scratch))) return st;
+    cudaSetDevice(c->device);
+    const uint64_t n8 = (uint64_t)M * (K / 8);
+    const unsigned blocks = (unsigned)((n8 + 255) / 256 < (uint64_t)c->sm_count * 8 ? (n8 + 255) / 256 : (uint64_t)c->sm_count * 8);
+    gemm_xpro_kernel<<<blocks, 256, 0, c->stream>>>((int)xmode, (const float *)rx.base, ldx, a->x_k0, (const float *)rst.base,
+                                                    a->stats_off, (const float *)rpv.base, a->pv_off, a->pv_stride, M, K,
+                                                    (uint16_t *)scratch);
+    if ((st = p0_launched(c, "gemm x prologue"))) return st;
+    xbase = (const uint8_t *)scratch;
+    xld = K;
+  }
   CUtensorMap tm;
   cuuint64_t dims[2] = {K, M};
-  cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+  cuuint64_t strides[1] = {(cuuint64_t)xld * 2};
   cuuint32_t box[2] = {(cuuint32_t)kBK, BT};
   cuuint32_t estr[2] = {1, 1};
-  CUresult cr = enc_fn(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)(rx.base + 2ull * a->x_k0), dims, strides, box, estr,
+  CUresult cr = enc_fn(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)xbase, dims, strides, box, estr,
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return p0_fail(c, P0_EDEVICE, "gemm: tensor map encode failed (%d)", (int)cr);

@@ -4,9 +4,10 @@
                                                             ldy, stat: {buf, off}, norm: {buf, off}, ev: {buf, off},
                                                             src: {n, ld}, mx: {buf}, cap})
   gemvM(g, a)  -> nsplit   engine/llm/lops_spec.js:159-191  (adds M, x.ldx, y.ldm / y.ldy, stat.ld, ev.ld)
-  gemm(gpu, a) -> flops    engine/ops/gemm.js:255-322       (a = {w, x: {buf, off, ld, k0}, M, N, K, wr0, wr1, wk0,
+  gemm(gpu, a) -> flops    engine/ops/gemm.js:255-322       (a = {w, x: {buf, off, ld, k0, mode}, M, N, K, wr0, wr1, wk0,
                                                             epi, act, acc, y: {buf, off, ld, n0}, ev: {buf, off},
-                                                            bv: {buf, off, up}, res, store} + post_gelu)
+                                                            bv: {buf, off, up}, res, store, stats: {buf, off},
+                                                            pv: {buf, off, stride}} + post_gelu)
 w = {buf, off (bytes), bytes, enc, rows, cols} as WeightStore.t() returns it (core/store.js:249-253).
 Every call enqueues one kernel on the context's stream; results are read with g.read() after it. Errors raise
 P0Error with the reference's messages. There is no CPU path: these always run the CUDA kernels in libp0mm.so.
@@ -83,21 +84,25 @@ def _gemvM(g, a, entry):
 
 
 def gemm(gpu, a):
-    """gemm(gpu, a) -> flops (gemm.js:264-322). x prologue 'f16'; acc 'f32'."""
+    """gemm(gpu, a) -> flops (gemm.js:264-322). x prologues 'f16', 'lnmod', 'rms'; acc 'f32'."""
     x, y = a["x"], a["y"]
     ev, bv = a.get("ev"), a.get("bv")
     epi = a.get("epi") or "f16"
     if epi not in L.GEPI:
         raise P0Error(L.P0_EINVAL, "gemm: epilogue %s is not built in this library yet" % epi)
-    if (x.get("mode") or "f16") != "f16" or a.get("conv"):
-        raise P0Error(L.P0_EINVAL, "gemm: x prologue %s is not built in this library yet" % (x.get("mode") or "conv"))
+    xmode = x.get("mode") or "f16"
+    if xmode not in L.XPRO or a.get("conv"):
+        raise P0Error(L.P0_EINVAL, "gemm: x prologue %s is not built in this library yet" % ("conv" if a.get("conv") else xmode))
+    stats, pv = a.get("stats"), a.get("pv")
     acc = a.get("acc") or "f32"
     args = L.p0_gemm_args(
         _wview(a["w"], "gemm"), handle(x["buf"]), int(x.get("off") or 0), int(x.get("ld") or 0), int(x.get("k0") or 0), int(a["M"]),
         int(a["N"]), int(a["K"]), int(a.get("wr0") or 0), int(a.get("wr1") or 0), int(a.get("wk0") or 0), L.GEPI[epi],
         L.ACT[a.get("act") or "silu"], 0 if acc == "f32" else 1, handle(y["buf"]), int(y.get("off") or 0), int(y.get("ld") or 0),
         int(y.get("n0") or 0), _b(ev), int((ev or {}).get("off") or 0), _b(bv), int((bv or {}).get("off") or 0),
-        int((bv or {}).get("up") or 0), int(bool(a.get("res"))), int(bool(a.get("store"))), int(bool(a.get("post_gelu"))))
+        int((bv or {}).get("up") or 0), int(bool(a.get("res"))), int(bool(a.get("store"))), int(bool(a.get("post_gelu"))),
+        L.XPRO[xmode], _b(stats), int((stats or {}).get("off") or 0), _b(pv), int((pv or {}).get("off") or 0),
+        int((pv or {}).get("stride") or 0))
     fl = ctypes.c_double()
     gpu._check(gpu._lib.p0_gemm(gpu.ctx, ctypes.byref(args), ctypes.byref(fl)))
     return fl.value

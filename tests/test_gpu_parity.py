@@ -339,7 +339,7 @@ def test_gemvM_geglu_pleg_ld(g):
 
 # ---------------------------------------------------------------- GEMM
 def run_gemm(g, b, X16, M, N, K, y_init=None, y_bytes=None, **a):
-    wb, xb = g.upload(b), g.upload(X16)
+    wb, xb = g.upload(b), g.upload(X16)   # X16: fp16 bits, or f32 for the x prologues
     f32y = a.get("epi") in ("f32", "resadd")
     ldy = a.get("y", {}).get("ld") or (N // 2 if a.get("epi") == "swiglu" else N)
     nb = y_bytes or M * ldy * (4 if f32y else 2)
@@ -352,6 +352,14 @@ def run_gemm(g, b, X16, M, N, K, y_init=None, y_bytes=None, **a):
         if k in a:
             v = a.pop(k)
             args[k] = {"buf": g.upload(v[0]), "off": v[1], **({"up": v[2]} if len(v) > 2 else {})}
+    a.pop("stats", None)
+    a.pop("pv", None)
+    if "_stats" in a:   # x prologue inputs: stats (rows of {mean, rstd}) and pv vectors
+        v = a.pop("_stats")
+        args["stats"] = {"buf": g.upload(v[0]), "off": v[1]}
+    if "_pv" in a:
+        v = a.pop("_pv")
+        args["pv"] = {"buf": g.upload(v[0]), "off": v[1], "stride": v[2]}
     args.update(a)
     fl = p0.gemm(g, args)
     assert fl == 2.0 * M * N * K
