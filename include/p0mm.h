@@ -150,7 +150,7 @@ p0_status p0_gemvM(p0_ctx *ctx, const p0_gemvM_args *a, uint32_t *nsplit);
 p0_status p0_gemvM_noalloc(p0_ctx *ctx, const p0_gemvM_args *a, uint32_t *nsplit);
 
 /* ---------------------------------------------------------------------------------------------- GEMM */
-enum { P0_GEPI_F16 = 0, P0_GEPI_F32 = 1, P0_GEPI_BIAS = 2, P0_GEPI_RESADD = 3, P0_GEPI_SWIGLU = 4 };
+enum { P0_GEPI_F16 = 0, P0_GEPI_F32 = 1, P0_GEPI_BIAS = 2, P0_GEPI_RESADD = 3, P0_GEPI_SWIGLU = 4, P0_GEPI_HEADS = 5, P0_GEPI_ONORMGATE = 6 };
 enum { P0_ACT_SILU = 0, P0_ACT_GELU = 1 };
 
 /* gemm(gpu, a) -> flops (engine/ops/gemm.js:255-322): Y[m, n] = sum_k X[m, k] * W[n, k], W dequantised in-kernel
@@ -178,8 +178,23 @@ typedef struct {
   uint32_t x_mode;
   p0_buf stats; uint32_t stats_off;
   p0_buf pv;    uint32_t pv_off, pv_stride;
+  /* epilogues that reduce over one 128-wide head (gemm.js:212-250; N % 128 == 0, head hd = column / 128), fields of
+   * a.heads {Ltot, Hq, Hkv, rowOff, eps (0 = 1e-6), ropeMode, rope} and a.gt; inv = 1/sqrt(sum of the head's 128 squared
+   * accumulators / 128 + eps), c = column % 128:
+   * P0_GEPI_HEADS (QK-RMSNorm + RoPE + head-major write): heads hd < Hq are q, hd < Hq + Hkv k, the rest v. q / k:
+   *   v = a * inv * ev[ev_off + (k ? 128 : 0) + c], rotated by the (cos, sin) pairs of rope row rowOff + m (128 f32 per
+   *   row): P0_ROPE_HALF pairs dims (d, d + 64) with pair d (rotate_half), P0_ROPE_INTER pairs (2p, 2p + 1) with pair p.
+   *   v heads: the accumulator. Y fp16 head-major: Y[((hd * Ltot) + rowOff + m) * 128 + c]; y.ld and y.n0 unused.
+   * P0_GEPI_ONORMGATE: Y[m * ld + n0 + n] = f16(a * inv * ev[ev_off + c] / (1 + exp(-gt[m * Ltot + n0 + n]))), gt fp16.
+   * rope and gt are read from the start of their buffers, as the reference binds them whole. */
+  uint32_t h_Ltot, h_Hq, h_Hkv, h_rowOff;
+  float h_eps;
+  uint32_t h_rope_mode;
+  p0_buf rope;
+  p0_buf gt;
 } p0_gemm_args;
 enum { P0_XPRO_F16 = 0, P0_XPRO_LNMOD = 1, P0_XPRO_RMS = 2 };
+enum { P0_ROPE_INTER = 0, P0_ROPE_HALF = 1 };
 p0_status p0_gemm(p0_ctx *ctx, const p0_gemm_args *a, double *flops);
 
 /* ---------------------------------------------------------------------------------------------- quantiser */

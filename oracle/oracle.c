@@ -511,3 +511,73 @@ void or_gemm_xpro(int mode, const float *X, uint32_t M, uint32_t K, uint32_t ldx
     }
   }
 }
+
+/* ------------------------------------------------------------------ GEMM epilogues that reduce over one 128-wide head
+ * (ops/gemm.js:212-250), applied to the f32 accumulators A[m * N + n] of one call (N % 128 == 0, one head per 128
+ * columns, hd = n / 128). Per row and head, s = the sum of the 128 squared accumulators, summed as the WGSL does without
+ * subgroups: 16 threads tx each take dot(a_0, a_0) + dot(a_1, a_1) over their 8 columns (rope 'half': columns
+ * 4tx..4tx+3 and 64+4tx..; else 8tx..8tx+7), then one thread adds the 16 in order; inv = inverseSqrt(s / 128 + eps).
+ *   onormgate (:223-229): Y[m*ldy + ny0 + n] = f16(a * inv * EV[evOff + c] / (1 + exp(-f32(GT[m*Ltot + ny0 + n])))), c = n % 128
+ *     (the vec4 indices floor (m*Ltot + ny0 + n) / 4 like the WGSL's u32 division)
+ *   heads (:231-249): section sec = 0 (q) for hd < Hq, 1 (k) for hd < Hq + Hkv, else 2 (v); row = rowOff + m.
+ *     q / k: v = a * inv * EV[evOff + (sec ? 128 : 0) + c], then RoPE from RP (per row 128 floats):
+ *       rope_half (rotate_half, pairs (d, d + 64)): cos = RP[row*128 + 2d], sin = RP[row*128 + 2d + 1],
+ *         out[d] = v[d]*cos - v[d+64]*sin, out[d+64] = v[d+64]*cos + v[d]*sin   (d < 64)
+ *       interleaved (pairs (2p, 2p+1)): cos = RP[row*128 + 2p], sin = RP[row*128 + 2p + 1],
+ *         out[2p] = v[2p]*cos - v[2p+1]*sin, out[2p+1] = v[2p]*sin + v[2p+1]*cos
+ *     v: out = a. Stored head-major: Y[(hd*Ltot + row)*128 + c] = f16(out[c]). */
+void or_gemm_red128(int onormgate, int rope_half, const float *A, uint32_t M, uint32_t N, uint16_t *Y, const float *EV,
+                    uint32_t evOff, const uint16_t *GT, const float *RP, uint32_t ldy, uint32_t ny0, uint32_t rowOff,
+                    uint32_t Ltot, uint32_t Hq, uint32_t Hkv, float eps) {
+  const int split = !onormgate && rope_half;
+  for (uint32_t m = 0; m < M; m++) {
+    for (uint32_t hd = 0; hd < N / 128; hd++) {
+      const float *a = A + (size_t)m * N + hd * 128;
+      float s = 0.0f;
+      for (uint32_t tx = 0; tx < 16; tx++) {
+        const uint32_t i0 = split ? tx * 4 : tx * 8, i1 = split ? 64 + tx * 4 : tx * 8 + 4;
+        s = s + (dot4(a + i0, a + i0) + dot4(a + i1, a + i1));
+      }
+      const float inv = (float)(1.0 / sqrt((double)(s / 128.0f + eps)));
+      if (onormgate) {
+        const size_t gb = ((size_t)m * Ltot + ny0) & ~(size_t)3, yb = ((size_t)m * ldy + ny0) & ~(size_t)3;
+        for (uint32_t c = 0; c < 128; c++) {
+          const uint32_t n = hd * 128 + c;
+          const float g = h2f32(GT[gb + n]);
+          float v = a[c] * inv;
+          v = v * EV[evOff + c];
+          v = v / (1.0f + expf(-g));
+          Y[yb + n] = or_f2h((double)v);
+        }
+        continue;
+      }
+      const uint32_t sec = hd < Hq ? 0u : hd < Hq + Hkv ? 1u : 2u, row = rowOff + m;
+      uint16_t *yo = Y + ((size_t)hd * Ltot + row) * 128;
+      if (sec == 2) {
+        for (uint32_t c = 0; c < 128; c++) yo[c] = or_f2h((double)a[c]);
+        continue;
+      }
+      float v[128];
+      for (uint32_t c = 0; c < 128; c++) {
+        const float t = a[c] * inv;
+        v[c] = t * EV[evOff + (sec ? 128u : 0u) + c];
+      }
+      const float *rp = RP + (size_t)row * 128;
+      if (split) {
+        for (uint32_t d = 0; d < 64; d++) {
+          const float cs = rp[2 * d], sn = rp[2 * d + 1];
+          const float lo = v[d] * cs - v[d + 64] * sn, hi = v[d + 64] * cs + v[d] * sn;
+          yo[d] = or_f2h((double)lo);
+          yo[d + 64] = or_f2h((double)hi);
+        }
+      } else {
+        for (uint32_t p = 0; p < 64; p++) {
+          const float cs = rp[2 * p], sn = rp[2 * p + 1];
+          const float x0 = v[2 * p], x1 = v[2 * p + 1];
+          yo[2 * p] = or_f2h((double)(x0 * cs - x1 * sn));
+          yo[2 * p + 1] = or_f2h((double)(x0 * sn + x1 * cs));
+        }
+      }
+    }
+  }
+}

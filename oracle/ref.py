@@ -59,6 +59,7 @@ def lib():
         L.or_gemvM.argtypes = [_i, _i, _i, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _vp] + [_u32] * 14 + [ctypes.c_float] + [_u32] * 4
         L.or_gemm.argtypes = [_i] * 9 + [_vp] * 5 + [_u32] * 15 + [_i]
         L.or_gemm_xpro.argtypes = [_i, _f32p, _u32, _u32, _u32, _u32, _f32p, _u32, _f32p, _u32, _u32, _u16p]
+        L.or_gemm_red128.argtypes = [_i, _i, _f32p, _u32, _u32, _u16p, _f32p, _u32, _u16p, _f32p] + [_u32] * 6 + [ctypes.c_float]
         L.or_dot64.argtypes = [_f32p, _f64p, _i64, _i64, _i64, _f64p]
         L.or_gemv_cpu_mt.argtypes = [_f32p, _u32p, _f32p, _u32, _u32, _u32, _u32, _i]
         L.or_max_threads.restype = _i
@@ -245,9 +246,14 @@ WENC = {"q4g32a.t64": 0, "q8g64s.t64": 1, "f16": 2}
 
 def gemm(W, X16, M, N, K, *, enc="q4g32a.t64", rows=None, cols=None, ldx=None, kx0=0, wr0=0, wr1=0, wk0=0,
          epi="f16", act="silu", acc="f32", Y=None, ldy=None, ny0=0, ev=None, ev_off=0, bv=None, bv_off=0, bv_up=0,
-         res=False, store=False, post_gelu=False, threads=1):
+         res=False, store=False, post_gelu=False, threads=1, heads=None, gt=None):
     """gemm.js gemm() (:264-322) + gemmCode arithmetic for the 'f16' x prologue. X16 is uint16 fp16 bits [M, ldx].
-    Y: uint16 (f16/bias/swiglu) or float32 (f32/resadd), updated in place when given. Returns Y."""
+    Y: uint16 (f16/bias/swiglu/heads/onormgate) or float32 (f32/resadd), updated in place when given. Returns Y.
+    epi 'heads' / 'onormgate' (gemm.js:212-250): heads = {Ltot, Hq, Hkv, rowOff, eps, ropeMode, rope (f32 array, read
+    from element 0 like the reference's whole-buffer binding)}; gt = the onormgate gate, fp16 bits, from element 0."""
+    if epi in ("heads", "onormgate"):
+        return _gemm_red128(W, X16, M, N, K, enc=enc, rows=rows, cols=cols, ldx=ldx, kx0=kx0, wr0=wr0, wk0=wk0, epi=epi,
+                            Y=Y, ldy=ldy, ny0=ny0, ev=ev, ev_off=ev_off, heads=heads or {}, gt=gt, threads=threads)
     if K % 32:
         raise ValueError("gemm: K must be a multiple of 32")
     rows = rows or N
@@ -268,6 +274,26 @@ def gemm(W, X16, M, N, K, *, enc="q4g32a.t64", rows=None, cols=None, ldx=None, k
                   _p(np.ascontiguousarray(X16, dtype=np.uint16)), _p(Wu), _p(Y),
                   _p(_f32(ev) if ev is not None else dummy), _p(_f32(bv) if bv is not None else dummy),
                   M, N, K, ldx, kx0, wr0, wr1, wG, wk0, ldy, ny0, rows, ev_off, bv_off, bv_up, int(threads))
+    return Y
+
+
+def _gemm_red128(W, X16, M, N, K, *, enc, rows, cols, ldx, kx0, wr0, wk0, epi, Y, ldy, ny0, ev, ev_off, heads, gt, threads):
+    """the f32 accumulators of the call (gemm() with epi 'f32'), then the head-reducing epilogue on them"""
+    if N % 128:
+        raise ValueError("gemm: the %s epilogue reduces over whole 128-wide heads (N %% 128)" % epi)
+    A = gemm(W, X16, M, N, K, enc=enc, rows=rows, cols=cols, ldx=ldx, kx0=kx0, wr0=wr0, wk0=wk0, epi="f32", threads=threads)
+    h = heads
+    Ltot, Hq, Hkv, rowOff = int(h.get("Ltot") or 0), int(h.get("Hq") or 0), int(h.get("Hkv") or 0), int(h.get("rowOff") or 0)
+    eps = float(h.get("eps") or 1e-6)
+    ldy = ldy or N
+    if Y is None:
+        n = ((N // 128 - 1) * Ltot + rowOff + M) * 128 if epi == "heads" else (M - 1) * ldy + ny0 + N
+        Y = np.zeros(n, np.uint16)
+    dummy = np.zeros(64, np.float32)
+    rp = _f32(h["rope"]) if h.get("rope") is not None else dummy
+    g16 = np.ascontiguousarray(gt, dtype=np.uint16) if gt is not None else np.zeros(64, np.uint16)
+    lib().or_gemm_red128(int(epi == "onormgate"), int(h.get("ropeMode") == "half"), _f32(A), M, N, Y,
+                         _f32(ev) if ev is not None else dummy, ev_off, g16, rp, ldy, ny0, rowOff, Ltot, Hq, Hkv, eps)
     return Y
 
 

@@ -15,9 +15,10 @@ STATUS = {0: "P0_OK", 1: "P0_EINVAL", 2: "P0_EALIGN", 3: "P0_ENOMEM", 4: "P0_EDE
 ENC = {"q4g32a.t64": 1, "q8g64s.t64": 2, "f16": 3}
 PRO = {"raw": 0, "rms": 1, "sum": 2, "pleg": 3}
 EPI = {"store": 0, "geglu": 1, "softcap": 2}
-GEPI = {"f16": 0, "f32": 1, "bias": 2, "resadd": 3, "swiglu": 4}
+GEPI = {"f16": 0, "f32": 1, "bias": 2, "resadd": 3, "swiglu": 4, "heads": 5, "onormgate": 6}
 ACT = {"silu": 0, "gelu": 1}
 XPRO = {"f16": 0, "lnmod": 1, "rms": 2}
+P0_ROPE_INTER, P0_ROPE_HALF = 0, 1
 
 # every symbol include/p0mm.h declares
 EXPORTS = ["p0_init", "p0_destroy", "p0_set_stream", "p0_set_overlap", "p0_last_error", "p0_stats", "p0_buffer", "p0_wrap", "p0_upload", "p0_read",
@@ -59,7 +60,9 @@ class p0_gemm_args(ctypes.Structure):
                 ("N", _u32), ("K", _u32), ("wr0", _u32), ("wr1", _u32), ("wk0", _u32), ("epi", _u32), ("act", _u32), ("acc", _u32),
                 ("y", p0_buf), ("y_off", ctypes.c_uint64), ("y_ld", _u32), ("y_n0", _u32), ("ev", p0_buf), ("ev_off", _u32),
                 ("bv", p0_buf), ("bv_off", _u32), ("bv_up", _u32), ("res", _u32), ("store", _u32), ("post_gelu", _u32),
-                ("x_mode", _u32), ("stats", p0_buf), ("stats_off", _u32), ("pv", p0_buf), ("pv_off", _u32), ("pv_stride", _u32)]
+                ("x_mode", _u32), ("stats", p0_buf), ("stats_off", _u32), ("pv", p0_buf), ("pv_off", _u32), ("pv_stride", _u32),
+                ("h_Ltot", _u32), ("h_Hq", _u32), ("h_Hkv", _u32), ("h_rowOff", _u32), ("h_eps", ctypes.c_float),
+                ("h_rope_mode", _u32), ("rope", p0_buf), ("gt", p0_buf)]
 
 
 _lib = None

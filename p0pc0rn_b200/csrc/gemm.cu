@@ -1,6 +1,6 @@
 // gemm.cu -- the dequant-fused W4A16 GEMM on sm_100a tensor cores: gemm(gpu, a) of engine/ops/gemm.js:255-322 for
-// q4g32a.t64 weights and the 'f16' x prologue, epilogues f16 / f32 / bias (+res, + the ew gelu that follows it) /
-// resadd / swiglu (gemm.js:187-211).
+// q4g32a.t64 / q8g64s.t64 weights, the x prologues f16 / lnmod / rms, epilogues f16 / f32 / bias (+res, + the ew gelu
+// that follows it) / resadd / swiglu (gemm.js:187-211) and the head-reducing heads / onormgate (gemm.js:212-250).
 //
 // Y[m, n] = sum_k X[m, k] * Wdq[n, k], Wdq[n, k] = f16(q * s + mn) (gemm.js:147-148), fp32 accumulation.
 //
@@ -58,7 +58,12 @@ struct GemmParams {
   const uint8_t *W;   // weight view base
   uint8_t *Y;         // y buffer + y.off
   const float *EV, *BV;
+  const float *RP;      // heads: rope (cos, sin) rows
+  const uint16_t *GT;   // onormgate: the fp16 gate
   uint32_t M, N, K, wR0, wR1, wG, wk0, Nw, ldy, ny0, evOff, bvOff, bvUp;
+  uint32_t Ltot, Hq, Hkv, rowOff;
+  float eps;
+  int rope_half;
   int epi, act, res, store, gate, bias, post_gelu;
   uint32_t BT, nk;
   int wtma;           // 1: the CTA's 128 rows are two whole 64-row tiles -> records arrive by bulk copy
@@ -196,6 +201,77 @@ __device__ __forceinline__ void cta_tiles(const GemmParams &p, uint32_t nB, uint
   }
   t0 = t0 < nt ? t0 : nt - 1;
   t1 = t1 < nt ? t1 : nt - 1;
+}
+
+__device__ __forceinline__ uint2 pack_h4(const float *v) {
+  return make_uint2((uint32_t)__half_as_ushort(__float2half_rn(v[0])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[1])) << 16),
+                    (uint32_t)__half_as_ushort(__float2half_rn(v[2])) | ((uint32_t)__half_as_ushort(__float2half_rn(v[3])) << 16));
+}
+
+// the epilogues that reduce over one 128-wide head (gemm.js:212-250). The CTA's 128 columns are one head, staged as
+// [BT][128] f32 accumulators; a warp takes a token row at a time, lane l columns 4l..4l+3, and the head's sum of
+// squares comes from a butterfly over the warp. 'half' RoPE pairs dim d (lanes 0-15) with d + 64 (lane + 16).
+__device__ __forceinline__ void store_red128(const GemmParams &p, const float *stg, uint32_t nB, uint32_t m0, uint32_t BT,
+                                             uint32_t wi, uint32_t nwarps, uint32_t lane) {
+  const uint32_t c = lane * 4u, hd = nB >> 7;
+  const bool og = p.epi == P0_GEPI_ONORMGATE;
+  const uint32_t sec = og ? 0u : hd < p.Hq ? 0u : hd < p.Hq + p.Hkv ? 1u : 2u;
+  float w[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+  if (sec < 2u) {
+    const float4 e = *reinterpret_cast<const float4 *>(p.EV + p.evOff + sec * 128u + c);
+    w[0] = e.x; w[1] = e.y; w[2] = e.z; w[3] = e.w;
+  }
+  for (uint32_t ml = wi; ml < BT; ml += nwarps) {
+    const uint32_t m = m0 + ml;
+    if (m >= p.M) break;
+    const float4 t = *reinterpret_cast<const float4 *>(stg + ml * 128u + c);
+    float v[4] = {t.x, t.y, t.z, t.w}, out[4];
+    if (sec < 2u) {
+      float ss = __fmul_rn(v[0], v[0]);
+#pragma unroll
+      for (int i = 1; i < 4; i++) ss = fmaf(v[i], v[i], ss);
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float inv = rsqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / 128.0f), p.eps));
+#pragma unroll
+      for (int i = 0; i < 4; i++) v[i] = __fmul_rn(__fmul_rn(v[i], inv), w[i]);
+    }
+    if (og) {
+      const size_t gi = (size_t)m * p.Ltot + p.ny0 + nB + c;
+      const uint2 g2 = *reinterpret_cast<const uint2 *>(p.GT + gi);
+      const float g[4] = {__half2float(__ushort_as_half((unsigned short)(g2.x & 0xffffu))),
+                          __half2float(__ushort_as_half((unsigned short)(g2.x >> 16))),
+                          __half2float(__ushort_as_half((unsigned short)(g2.y & 0xffffu))),
+                          __half2float(__ushort_as_half((unsigned short)(g2.y >> 16)))};
+#pragma unroll
+      for (int i = 0; i < 4; i++) out[i] = __fdiv_rn(v[i], __fadd_rn(1.0f, expf(-g[i])));
+      *reinterpret_cast<uint2 *>(p.Y + ((size_t)m * p.ldy + p.ny0 + nB + c) * 2) = pack_h4(out);
+      continue;
+    }
+    const uint32_t row = p.rowOff + m;
+    if (sec == 2u) {
+#pragma unroll
+      for (int i = 0; i < 4; i++) out[i] = v[i];
+    } else if (p.rope_half) {
+      float o[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) o[i] = __shfl_xor_sync(0xffffffffu, v[i], 16);
+      const float *rp = p.RP + (size_t)row * 128u + 2u * (c & 63u);
+      const float4 a = *reinterpret_cast<const float4 *>(rp), b = *reinterpret_cast<const float4 *>(rp + 4);
+      const float cs[4] = {a.x, a.z, b.x, b.z}, sn[4] = {a.y, a.w, b.y, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        out[i] = lane < 16u ? __fsub_rn(__fmul_rn(v[i], cs[i]), __fmul_rn(o[i], sn[i]))
+                            : __fadd_rn(__fmul_rn(v[i], cs[i]), __fmul_rn(o[i], sn[i]));
+    } else {
+      const float4 r = *reinterpret_cast<const float4 *>(p.RP + (size_t)row * 128u + c);   // (cos, sin) of pairs c/2, c/2 + 1
+      out[0] = __fsub_rn(__fmul_rn(v[0], r.x), __fmul_rn(v[1], r.y));
+      out[1] = __fadd_rn(__fmul_rn(v[0], r.y), __fmul_rn(v[1], r.x));
+      out[2] = __fsub_rn(__fmul_rn(v[2], r.z), __fmul_rn(v[3], r.w));
+      out[3] = __fadd_rn(__fmul_rn(v[2], r.w), __fmul_rn(v[3], r.z));
+    }
+    *reinterpret_cast<uint2 *>(p.Y + (((size_t)hd * p.Ltot + row) * 128u + c) * 2) = pack_h4(out);
+  }
 }
 
 template <class C, bool Q8>
@@ -427,7 +503,9 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
       }
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kDqWarps * 32) : "memory");
-    if (go && !*abort_flag) {
+    if (go && !*abort_flag && (p.epi == P0_GEPI_HEADS || p.epi == P0_GEPI_ONORMGATE)) {
+      store_red128(p, stg, nB, m0, BT, (threadIdx.x - 64u) >> 5, kDqWarps, lane);
+    } else if (go && !*abort_flag) {
       // coalesced stores: 4 consecutive columns per thread per step (the reference's vec4 granularity)
       const uint32_t OC = swi ? 64u : 128u, q4 = OC / 4u, nOut0 = swi ? (nB >> 1) : nB;
       const uint32_t tid = threadIdx.x - 64u;   // 0 .. kDqWarps*32-1
@@ -559,8 +637,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 const char *gepi_name(uint32_t e) {
-  static const char *n[] = {"f16", "f32", "bias", "resadd", "swiglu"};
-  return e < 5 ? n[e] : "?";
+  static const char *n[] = {"f16", "f32", "bias", "resadd", "swiglu", "heads", "onormgate"};
+  return e < 7 ? n[e] : "?";
 }
 
 }  // namespace
@@ -579,7 +657,7 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   const uint32_t GK = q8 ? 64u : 32u, RB = q8 ? 4224u : 1280u;
   const uint32_t M = a->M, N = a->N, K = a->K;
   if (K % 32) return p0_fail(c, P0_EINVAL, "gemm: K must be a multiple of 32");
-  if (a->epi > P0_GEPI_SWIGLU) return p0_fail(c, P0_EINVAL, "gemm: epilogue %u is not built in this library yet", a->epi);
+  if (a->epi > P0_GEPI_ONORMGATE) return p0_fail(c, P0_EINVAL, "gemm: epilogue %u is not built in this library yet", a->epi);
   if (a->acc != 0) return p0_fail(c, P0_EINVAL, "gemm: acc 'f16' (fp16 partial sums) is not built; the tensor cores accumulate in f32");
   if (a->post_gelu && a->epi != P0_GEPI_BIAS) return p0_fail(c, P0_EINVAL, "gemm: post_gelu applies to the 'bias' epilogue only");
   if (!M || !N || !K) return P0_OK;
@@ -609,9 +687,23 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
     const uint64_t pvneed = (uint64_t)a->pv_off + (xmode == P0_XPRO_LNMOD ? a->pv_stride : 0) + a->x_k0 + K;
     if ((st = p0_range(c, a->pv, 0, pvneed * 4, op, "pv", &rpv))) return st;
   }
-  if ((st = p0_range(c, a->y, a->y_off, ((uint64_t)(M - 1) * ldy + a->y_n0 + ncols_out) * es, op, "Y", &ry))) return st;
-  const bool need_ev = a->epi == P0_GEPI_BIAS || (a->epi == P0_GEPI_RESADD && a->ev.id);
-  if (need_ev && (st = p0_range(c, a->ev, 0, ((uint64_t)a->ev_off + N) * 4, op, "EV", &re))) return st;
+  // the head-reducing epilogues (gemm.js:212-250): whole 128-wide heads; the q / k heads read the norm weights and rope
+  // rows, onormgate its gate (vec4 reads: Ltot % 4 keeps each row's gate on 8-byte boundaries)
+  const bool heads = a->epi == P0_GEPI_HEADS, og = a->epi == P0_GEPI_ONORMGATE;
+  const uint32_t nh = N / 128;
+  const bool hq = heads && a->h_Hq > 0, hk = heads && nh > a->h_Hq && a->h_Hkv > 0;
+  P0Range rrp, rgt;
+  if ((heads || og) && N % 128) return p0_fail(c, P0_EINVAL, "gemm: the %s epilogue reduces over whole 128-wide heads (N %% 128)", gepi_name(a->epi));
+  if (og && a->h_Ltot % 4) return p0_fail(c, P0_EALIGN, "gemm: onormgate reads the gate as vec4s (heads.Ltot %% 4)");
+  const uint64_t ybytes = heads ? ((uint64_t)(nh - 1) * a->h_Ltot + a->h_rowOff + M) * 128 * 2
+                                : ((uint64_t)(M - 1) * ldy + a->y_n0 + ncols_out) * es;
+  if ((st = p0_range(c, a->y, a->y_off, ybytes, op, "Y", &ry))) return st;
+  const bool need_ev = a->epi == P0_GEPI_BIAS || (a->epi == P0_GEPI_RESADD && a->ev.id) || og || hq || hk;
+  const uint64_t evn = og || (hq && !hk) ? 128u : hk ? 256u : N;
+  if (need_ev && (st = p0_range(c, a->ev, 0, ((uint64_t)a->ev_off + evn) * 4, op, "EV", &re))) return st;
+  if ((heads || og) && a->ev_off % 4) return p0_fail(c, P0_EALIGN, "gemm: %s reads its norm weights as vec4s (ev.off %% 4)", gepi_name(a->epi));
+  if ((hq || hk) && (st = p0_range(c, a->rope, 0, ((uint64_t)a->h_rowOff + M) * 128 * 4, op, "rope", &rrp))) return st;
+  if (og && (st = p0_range(c, a->gt, 0, ((uint64_t)(M - 1) * a->h_Ltot + a->y_n0 + N) * 2, op, "gt", &rgt))) return st;
   const bool bias = a->bv.id != 0 && (a->epi == P0_GEPI_RESADD || swi);
   if (bias && (st = p0_range(c, a->bv, 0, ((uint64_t)a->bv_off + (swi ? a->bv_up + N / 2 : N)) * 4, op, "BV", &rb))) return st;
   if (swi && (a->wr0 + N / 2 > a->w.rows || a->wr1 + N / 2 > a->w.rows)) return p0_fail(c, P0_EINVAL, "gemm: swiglu rows beyond the weight");
@@ -656,6 +748,10 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   p.ldy = ldy; p.ny0 = a->y_n0; p.evOff = a->ev_off; p.bvOff = a->bv_off; p.bvUp = a->bv_up;
   p.epi = (int)a->epi; p.act = (int)a->act; p.res = (int)a->res; p.store = (int)a->store; p.gate = a->ev.id != 0;
   p.bias = bias; p.post_gelu = (int)a->post_gelu;
+  p.RP = (hq || hk) ? (const float *)rrp.base : nullptr; p.GT = og ? (const uint16_t *)rgt.base : nullptr;
+  p.Ltot = a->h_Ltot; p.Hq = a->h_Hq; p.Hkv = a->h_Hkv; p.rowOff = a->h_rowOff;
+  p.eps = a->h_eps != 0.0f ? a->h_eps : 1e-6f;   // gemm.js:309 `h.eps || 1e-6`
+  p.rope_half = a->h_rope_mode == P0_ROPE_HALF;
   p.BT = BT; p.nk = (K + kBK - 1) / kBK; p.err = c->d_err;
   // bulk-copy weight path: every CTA's 128 lanes read two whole 64-row tiles
   p.wtma = swi ? (a->wr0 % 64 == 0 && a->wr1 % 64 == 0 && (N / 2) % 64 == 0) : (a->wr0 % 64 == 0);
@@ -680,7 +776,6 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   }
   if ((st = p0_launched(c, "gemm"))) return st;
   if (flops) *flops = 2.0 * M * N * K;
-  (void)gepi_name;
   return P0_OK;
 }
 

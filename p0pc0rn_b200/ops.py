@@ -84,7 +84,8 @@ def _gemvM(g, a, entry):
 
 
 def gemm(gpu, a):
-    """gemm(gpu, a) -> flops (gemm.js:264-322). x prologues 'f16', 'lnmod', 'rms'; acc 'f32'."""
+    """gemm(gpu, a) -> flops (gemm.js:264-322). x prologues 'f16', 'lnmod', 'rms'; acc 'f32'; every epilogue of
+    gemm.js:187-250 ('f16', 'f32', 'bias', 'resadd', 'swiglu', 'heads', 'onormgate')."""
     x, y = a["x"], a["y"]
     ev, bv = a.get("ev"), a.get("bv")
     epi = a.get("epi") or "f16"
@@ -103,6 +104,11 @@ def gemm(gpu, a):
         int((bv or {}).get("up") or 0), int(bool(a.get("res"))), int(bool(a.get("store"))), int(bool(a.get("post_gelu"))),
         L.XPRO[xmode], _b(stats), int((stats or {}).get("off") or 0), _b(pv), int((pv or {}).get("off") or 0),
         int((pv or {}).get("stride") or 0))
+    h = a.get("heads") or {}
+    args.h_Ltot, args.h_Hq, args.h_Hkv, args.h_rowOff = (int(h.get(k) or 0) for k in ("Ltot", "Hq", "Hkv", "rowOff"))
+    args.h_eps = float(h.get("eps") or 0.0)
+    args.h_rope_mode = L.P0_ROPE_HALF if h.get("ropeMode") == "half" else L.P0_ROPE_INTER
+    args.rope, args.gt = _b(h.get("rope")), _b(a.get("gt"))   # bound from the buffer start, as gemm.js:302-303 binds them
     fl = ctypes.c_double()
     gpu._check(gpu._lib.p0_gemm(gpu.ctx, ctypes.byref(args), ctypes.byref(fl)))
     return fl.value

@@ -217,3 +217,68 @@ def test_golden_fixtures():
         for k, arr in arrays.items():
             stored = np.fromfile(os.path.join(GOLD, ent[k]["file"]), dtype=ent[k]["dtype"])
             assert np.array_equal(stored, np.ascontiguousarray(arr).ravel().view(stored.dtype)), (name, k)
+
+
+# ---------------------------------------------------------------- head-reducing GEMM epilogues (gemm.js:212-250)
+# The reference's tests hold no vectors for these epilogues, so the restatement is pinned by identities of the math
+# it states, checked in f64 from the same accumulators: RMSNorm scaling, the rotation's pair norms, the identity rope,
+# the untouched v heads and the sigmoid gate.
+def _acc_and_inputs(M, N, K, seed):
+    b, _ = ref.pack_q4(ref.randn(N * K, seed, 0.03), N, K)
+    X = ref.f2h(ref.round_f16(ref.randn(M * K, seed + 1)))
+    A = ref.gemm(b, X, M, N, K, epi="f32").reshape(M, N).astype(np.float64)
+    return b, X, A
+
+
+@pytest.mark.parametrize("mode", ["half", "inter"])
+def test_heads_oracle_identities(mode):
+    M, K, Hq, Hkv = 6, 128, 1, 1
+    N = 3 * 128
+    b, X, A = _acc_and_inputs(M, N, K, 960)
+    ev = (ref.randn(256, 962, 0.2) + 1).astype(np.float32)
+    eps = 1e-6
+    inv = 1.0 / np.sqrt(np.stack([(A[:, h * 128:(h + 1) * 128] ** 2).sum(1) / 128 + eps for h in range(3)], 1))   # [M][head]
+    # identity rope (cos 1, sin 0): out = a * inv * w
+    rp = np.zeros(M * 128, np.float32)
+    rp[0::2] = 1.0
+    h = {"Ltot": M, "Hq": Hq, "Hkv": Hkv, "rowOff": 0, "eps": eps, "ropeMode": mode, "rope": rp}
+    y = ref.h2f(ref.gemm(b, X, M, N, K, epi="heads", ev=ev, heads=h)).reshape(3, M, 128)
+    for hd in range(2):
+        want = A[:, hd * 128:(hd + 1) * 128] * inv[:, hd:hd + 1] * ev[hd * 128:(hd + 1) * 128]
+        assert np.max(np.abs(y[hd] - want)) <= 2e-3 * max(1.0, np.max(np.abs(want)))
+    assert np.array_equal(ref.gemm(b, X, M, N, K, epi="heads", ev=ev, heads=h).reshape(3, M, 128)[2],
+                          ref.f2h(A[:, 256:384].astype(np.float32).astype(np.float64)))   # v: f16(acc), unnormalised
+    # random rope, unit norm weights: each rotated pair keeps its length, sqrt(2) * |normalised pair|
+    ang = ref.randn(M * 64, 963, 3.0).astype(np.float64)
+    rp = np.empty(M * 128, np.float32)
+    rp[0::2], rp[1::2] = np.cos(ang), np.sin(ang)
+    y = ref.h2f(ref.gemm(b, X, M, N, K, epi="heads", ev=np.ones(256, np.float32), heads={**h, "rope": rp})).reshape(3, M, 128)
+    for hd in range(2):
+        v = A[:, hd * 128:(hd + 1) * 128] * inv[:, hd:hd + 1]
+        if mode == "half":
+            pn_in, pn_out = v[:, :64] ** 2 + v[:, 64:] ** 2, y[hd][:, :64] ** 2 + y[hd][:, 64:] ** 2
+            c, s = np.cos(ang).reshape(M, 64), np.sin(ang).reshape(M, 64)
+            lo = v[:, :64] * c - v[:, 64:] * s
+            assert np.max(np.abs(y[hd][:, :64] - lo)) <= 5e-3
+        else:
+            pn_in, pn_out = v[:, 0::2] ** 2 + v[:, 1::2] ** 2, y[hd][:, 0::2] ** 2 + y[hd][:, 1::2] ** 2
+            c, s = np.cos(ang).reshape(M, 64), np.sin(ang).reshape(M, 64)
+            assert np.max(np.abs(y[hd][:, 1::2] - (v[:, 0::2] * s + v[:, 1::2] * c))) <= 5e-3
+        assert np.max(np.abs(pn_out - pn_in)) <= 2e-2
+
+
+def test_onormgate_oracle_identities():
+    M, K, LDG = 5, 128, 132
+    b, X, A = _acc_and_inputs(M, 128, K, 970)
+    ev = (ref.randn(128, 972, 0.2) + 1).astype(np.float32)
+    eps = 1e-9
+    inv = 1.0 / np.sqrt((A ** 2).sum(1, keepdims=True) / 128 + eps)
+    gate = ref.randn(M * LDG, 973, 2.0)
+    gt = ref.f2h(ref.round_f16(gate))
+    y = ref.gemm(b, X, M, 128, K, epi="onormgate", ev=ev, ldy=256, ny0=4, heads={"Ltot": LDG, "eps": eps}, gt=gt,
+                 Y=np.zeros(M * 256, np.uint16))
+    y = ref.h2f(y).reshape(M, 256)
+    g = ref.h2f(gt).reshape(M, LDG)[:, 4:132]
+    want = A * inv * ev / (1 + np.exp(-g))
+    assert np.max(np.abs(y[:, 4:132] - want)) <= 2e-3 * max(1.0, np.max(np.abs(want)))
+    assert not y[:, :4].any() and not y[:, 132:].any()   # columns outside the head untouched
