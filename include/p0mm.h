@@ -197,6 +197,50 @@ enum { P0_XPRO_F16 = 0, P0_XPRO_LNMOD = 1, P0_XPRO_RMS = 2 };
 enum { P0_ROPE_INTER = 0, P0_ROPE_HALF = 1 };
 p0_status p0_gemm(p0_ctx *ctx, const p0_gemm_args *a, double *flops);
 
+/* ---------------------------------------------------------------------------------------------- decode-path operators */
+/* argmax(g, a) (engine/llm/lops.js:416-436) / argmaxM(g, a) (lops_spec.js:326-348): for each of M rows of n
+ * (max, bitcast index) pairs, mx f32 [M][n][2] (the GEMV's softcap MX), out[2m] = the index of the largest max (ties:
+ * the lowest index; NaN maxima never win; none: 0xffffffff with -3.4e38), out[2m + 1] = the bits of that max.
+ * argmax is M = 1. Both buffers are read from their start, as the reference binds them. */
+p0_status p0_argmaxM(p0_ctx *ctx, p0_buf mx, uint32_t n, uint32_t M, p0_buf out);
+
+/* embed(g, a) (lops.js:323-365): x[(rowOut + m) * K + k] = dequant(E[ids[m]])[k] * scale for m < n, E a q4g32a.t64 /
+ * q8g64s.t64 table view [rows][K] (the lm_head's records); st[st_off + m] = 1 / sqrt(sum_k x^2 / K + eps) (eps 0 =
+ * 1e-6). ids, x and st are read from their start (st_off in floats). An id >= w.rows reads as a row of zeros. */
+typedef struct {
+  p0_wview w;
+  p0_buf ids, x, st;
+  uint32_t st_off, K, n, rowOut;
+  float scale, eps;
+} p0_embed_args;
+p0_status p0_embed(p0_ctx *ctx, const p0_embed_args *a);
+
+/* normadd(g, a) (lops.js:143-180): for rows m < M (0 = 1) of D: tv = the sum of the t_n (0 = 1) partial rows
+ * t[j * t_ld + m * D + i] (t_ld floats, 0 = D * M); mode 0: x = (x + tv * rsqrt(mean tv^2 + eps) * w[w_off + i]) *
+ * scale, mode 1: x = tv; st[st_off + m] = rsqrt(mean x^2 + eps). eps 0 = 1e-6; scale has no default here (the
+ * reference's is 1). Buffers from their start; D * 4 bytes <= 200 KB. */
+typedef struct {
+  p0_buf t; uint32_t t_n, t_ld;
+  p0_buf w; uint32_t w_off;
+  p0_buf x, st; uint32_t st_off;
+  uint32_t D, M, mode;
+  float eps, scale;
+} p0_normadd_args;
+p0_status p0_normadd(p0_ctx *ctx, const p0_normadd_args *a);
+
+/* dhead(g, a) (lops_spec.js:428-482): the drafter's head over selected clusters. Block b < nsel * tPer scores tile
+ * sel[b / tPer] * tPer + b % tPer of a q4 / q8 head view [rows][K] (K <= 512) against x * stat[stat_off] *
+ * norm[norm_off + k]: mx[2b] = the tile's largest row dot, mx[2b + 1] = bitcast(tile * 64 + row) (lowest row on
+ * ties). A tile beyond the head gives (-3.4e38, 0xffffffff). x, stat, norm, sel, mx from their start. */
+typedef struct {
+  p0_wview w;
+  p0_buf x, stat; uint32_t stat_off;
+  p0_buf norm; uint32_t norm_off;
+  p0_buf sel, mx;
+  uint32_t K, tPer, nsel;
+} p0_dhead_args;
+p0_status p0_dhead(p0_ctx *ctx, const p0_dhead_args *a);
+
 /* ---------------------------------------------------------------------------------------------- quantiser */
 /* packQ4 (engine/kcheck.js:22-38) on the device, bit for bit: W f32 [N][ldw] at w_off (bytes) -> q4g32a.t64 records
  * (N*K*5/8 bytes) at out_off. N % 64 == 0, K % 32 == 0. The dequantised value of code q is q*s + mn. */

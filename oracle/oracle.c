@@ -581,3 +581,137 @@ void or_gemm_red128(int onormgate, int rope_half, const float *A, uint32_t M, ui
     }
   }
 }
+
+/* ------------------------------------------------------------------ decode-path operators around the GEMV
+ * argmax / argmaxM (engine/llm/lops.js:416-436, lops_spec.js:326-348): for each row m of n (max, bitcast index) pairs,
+ * OUT[2m] = the index of the largest max, ties to the lowest index, NaN maxima never win (start: -3.4e38, index
+ * 0xffffffff); OUT[2m + 1] = the bits of that max. The tie rule makes the result independent of the scan order. */
+void or_argmaxM(const float *MX, uint32_t n, uint32_t M, uint32_t *OUT) {
+  for (uint32_t m = 0; m < M; m++) {
+    float bv = -3.4e38f; uint32_t bi = 0xffffffffu;
+    for (uint32_t i = 0; i < n; i++) {
+      const float v = MX[2 * ((size_t)m * n + i)]; uint32_t id; memcpy(&id, &MX[2 * ((size_t)m * n + i) + 1], 4);
+      if (v > bv || (v == bv && id < bi)) { bv = v; bi = id; }
+    }
+    OUT[2 * m] = bi; memcpy(&OUT[2 * m + 1], &bv, 4);
+  }
+}
+
+/* the 256-thread tree sum of the WGSL reductions: red[t] partials, halving strides 128..1 */
+static float tree256(float *red) {
+  for (uint32_t k = 128; k > 0; k >>= 1) for (uint32_t t = 0; t < k; t++) red[t] = red[t] + red[t + k];
+  return red[0];
+}
+
+/* embed (lops.js:323-365): x[(rowOut + m) * K + k] = dequant(E[ids[m]])[k] * scale, E a q4g32a.t64 / q8g64s.t64 table
+ * [V][K] (word-indexed W); ST[statOff + m] = inverseSqrt(sum x^2 / K + eps), the sum as 256 strided thread partials
+ * and the tree. q4: (f32(q) * s + mn) * scale; q8: f32(q) * s * scale. */
+void or_embed(int q8, const uint32_t *W, const uint32_t *IDS, uint32_t n, uint32_t K, uint32_t wG, float scale, float eps,
+              uint32_t statOff, uint32_t rowOut, float *X, float *ST) {
+  float red[256];
+  for (uint32_t m = 0; m < n; m++) {
+    const uint32_t id = IDS[m], tile = id >> 6, r = id & 63u;
+    for (uint32_t t = 0; t < 256; t++) {
+      float s = 0.0f;
+      for (uint32_t k = t; k < K; k += 256) {
+        float v;
+        if (q8) {
+          const uint32_t gi = k >> 6, rec = (tile * wG + gi) * 1056u, kk = k & 63u;
+          const uint32_t qb = (W[rec + r * 16u + (kk >> 2)] >> (8u * (kk & 3u))) & 255u;
+          const float qs = (float)(int32_t)(int8_t)qb;
+          const uint32_t s2 = W[rec + 1024u + (r >> 1)];
+          const float sc = h2f32((uint16_t)((r & 1u) ? (s2 >> 16) : (s2 & 0xffffu)));
+          v = qs * sc; v = v * scale;
+        } else {
+          const uint32_t gi = k >> 5, rec = (tile * wG + gi) * 320u, kk = k & 31u;
+          const uint32_t q = (W[rec + r * 4u + (kk >> 3)] >> (4u * (kk & 7u))) & 15u, sm = W[rec + 256u + r];
+          v = (float)q * h2f32((uint16_t)(sm & 0xffffu)); v = v + h2f32((uint16_t)(sm >> 16)); v = v * scale;
+        }
+        X[(size_t)(rowOut + m) * K + k] = v;
+        s = s + v * v;
+      }
+      red[t] = s;
+    }
+    ST[statOff + m] = (float)(1.0 / sqrt((double)(tree256(red) / (float)K + eps)));
+  }
+}
+
+/* normadd (lops.js:143-180): per row m < M of D: tv = sum over the nsrc partial rows T[j * ldp + m * D + i] (j in order);
+ * rs = inverseSqrt(sum tv^2 / D + eps); mode 0: x = (x + tv * rs * W[wOff + i]) * scale, mode 1: x = tv;
+ * ST[statOff + m] = inverseSqrt(sum x^2 / D + eps). Sums as 256 strided partials and the tree. */
+void or_normadd(const float *T, uint32_t nsrc, uint32_t ldp, const float *W, uint32_t wOff, float *X, float *ST, uint32_t statOff,
+                uint32_t D, uint32_t M, uint32_t mode, float eps, float scale) {
+  float red[256];
+  float *tv = (float *)malloc(sizeof(float) * D);
+  for (uint32_t m = 0; m < M; m++) {
+    const size_t xb = (size_t)m * D;
+    for (uint32_t t = 0; t < 256; t++) {
+      float s = 0.0f;
+      for (uint32_t i = t; i < D; i += 256) {
+        float v = 0.0f;
+        for (uint32_t j = 0; j < nsrc; j++) v = v + T[(size_t)j * ldp + xb + i];
+        tv[i] = v; s = s + v * v;
+      }
+      red[t] = s;
+    }
+    const float rs = (float)(1.0 / sqrt((double)(tree256(red) / (float)D + eps)));
+    for (uint32_t t = 0; t < 256; t++) {
+      float s2 = 0.0f;
+      for (uint32_t i = t; i < D; i += 256) {
+        float x = X[xb + i];
+        if (mode == 0) { float u = tv[i] * rs; u = u * W[wOff + i]; x = (x + u) * scale; } else x = tv[i];
+        X[xb + i] = x; s2 = s2 + x * x;
+      }
+      red[t] = s2;
+    }
+    ST[statOff + m] = (float)(1.0 / sqrt((double)(tree256(red) / (float)D + eps)));
+  }
+  free(tv);
+}
+
+/* dhead (lops_spec.js:428-482): the drafter's head over selected clusters. Workgroup wt < nsel * tPer scores tile
+ * SEL[wt / tPer] * tPer + wt % tPer of a q4 / q8 head [rows][K] (K <= 512) against xs = X * ST[statOff] * NW[nOff + k]:
+ * row r's dot in 4 k-quarter lanes w (q4: group g's k = 32g + 8w..+7, acc += s * (q . x) + mn * sum(x); q8: k = 64g +
+ * 16w..+15, acc += s * (q . x)), lane sums in order w = 0..3, then the tile's max with the lowest row index winning ties:
+ * MX[wt * 2] = max, MX[wt * 2 + 1] = bitcast(tile * 64 + row). */
+void or_dhead(int q8, const float *X, const uint32_t *W, const float *ST, const float *NW, const uint32_t *SEL, uint32_t statOff,
+              uint32_t nOff, uint32_t K, uint32_t wG, uint32_t tPer, uint32_t nsel, float *MX) {
+  float xs[512];
+  const float rs = ST[statOff];
+  for (uint32_t k = 0; k < K; k++) { float v = X[k] * rs; xs[k] = v * NW[nOff + k]; }
+  for (uint32_t wt = 0; wt < nsel * tPer; wt++) {
+    const uint32_t tile = SEL[wt / tPer] * tPer + (wt % tPer), tb = tile * wG;
+    float best = 0.0f; uint32_t bidx = 0;
+    for (uint32_t r = 0; r < 64; r++) {
+      float red[4];
+      for (uint32_t w = 0; w < 4; w++) {
+        float acc = 0.0f;
+        for (uint32_t g = 0; g < wG; g++) {
+          if (q8) {
+            const uint32_t rec = (tb + g) * 1056u, s2 = W[rec + 1024u + (r >> 1)];
+            const float sc = h2f32((uint16_t)((r & 1u) ? (s2 >> 16) : (s2 & 0xffffu)));
+            float d = 0.0f;
+            for (uint32_t u = 0; u < 4; u++) {
+              const uint32_t q = W[rec + r * 16u + w * 4u + u], xb = g * 64u + w * 16u + u * 4u;
+              float qv[4]; for (int b = 0; b < 4; b++) qv[b] = (float)(int32_t)(int8_t)((q >> (8 * b)) & 255u);
+              d = d + dot4(qv, xs + xb);
+            }
+            acc = acc + sc * d;
+          } else {
+            const uint32_t rec = (tb + g) * 320u, q = W[rec + r * 4u + w], sm = W[rec + 256u + r], xb = g * 32u + w * 8u;
+            float qa[4], qb[4];
+            for (int b = 0; b < 4; b++) { qa[b] = (float)((q >> (4 * b)) & 15u); qb[b] = (float)((q >> (16 + 4 * b)) & 15u); }
+            const float one[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+            const float s = h2f32((uint16_t)(sm & 0xffffu)), mn = h2f32((uint16_t)(sm >> 16));
+            const float dq = dot4(qa, xs + xb) + dot4(qb, xs + xb + 4), dx = dot4(xs + xb, one) + dot4(xs + xb + 4, one);
+            acc = acc + s * dq + mn * dx;
+          }
+        }
+        red[w] = acc;
+      }
+      const float tot = red[0] + red[1] + red[2] + red[3];
+      if (r == 0 || tot > best) { best = tot; bidx = tile * 64u + r; }
+    }
+    MX[wt * 2] = best; memcpy(&MX[wt * 2 + 1], &bidx, 4);
+  }
+}

@@ -59,6 +59,10 @@ def lib():
         L.or_gemvM.argtypes = [_i, _i, _i, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _vp] + [_u32] * 14 + [ctypes.c_float] + [_u32] * 4
         L.or_gemm.argtypes = [_i] * 9 + [_vp] * 5 + [_u32] * 15 + [_i]
         L.or_gemm_xpro.argtypes = [_i, _f32p, _u32, _u32, _u32, _u32, _f32p, _u32, _f32p, _u32, _u32, _u16p]
+        L.or_argmaxM.argtypes = [_f32p, _u32, _u32, _u32p]
+        L.or_embed.argtypes = [_i, _u32p, _u32p, _u32, _u32, _u32, ctypes.c_float, ctypes.c_float, _u32, _u32, _f32p, _f32p]
+        L.or_normadd.argtypes = [_f32p, _u32, _u32, _f32p, _u32, _f32p, _f32p, _u32, _u32, _u32, _u32, ctypes.c_float, ctypes.c_float]
+        L.or_dhead.argtypes = [_i, _f32p, _u32p, _f32p, _f32p, _u32p] + [_u32] * 6 + [_f32p]
         L.or_gemm_red128.argtypes = [_i, _i, _f32p, _u32, _u32, _u16p, _f32p, _u32, _u16p, _f32p] + [_u32] * 6 + [ctypes.c_float]
         L.or_dot64.argtypes = [_f32p, _f64p, _i64, _i64, _i64, _f64p]
         L.or_gemv_cpu_mt.argtypes = [_f32p, _u32p, _f32p, _u32, _u32, _u32, _u32, _i]
@@ -323,3 +327,44 @@ def gemv_cpu_mt(Wbytes, X, M, N, K, threads=0):
 
 def max_threads():
     return lib().or_max_threads()
+
+
+# ---------------------------------------------------------------- decode-path operators (lops.js, lops_spec.js)
+def _words(b):
+    return np.frombuffer(np.ascontiguousarray(b, dtype=np.uint8).tobytes() + b"\0" * 16, dtype=np.uint32)
+
+
+def argmaxM(MX, n, M):
+    """argmax / argmaxM (lops.js:416-436, lops_spec.js:326-348): MX f32 [M][n][2] (max, bitcast index) -> uint32 [M][2]
+    (index, bits of the max)"""
+    out = np.empty(2 * M, np.uint32)
+    lib().or_argmaxM(_f32(MX), n, M, out)
+    return out
+
+
+def embed(W, ids, K, *, enc="q4g32a.t64", scale=1.0, eps=1e-6, st_off=0, row_out=0, X=None, ST=None):
+    """embed (lops.js:323-365): rows ids of a q4 / q8 table -> X[(row_out + m) * K + k] (dequant * scale), ST[st_off + m]
+    = rstd of the row. X / ST updated in place when given; returns (X, ST)."""
+    q8 = enc == "q8g64s.t64"
+    ids = np.ascontiguousarray(ids, np.uint32)
+    n = ids.size
+    X = np.zeros((row_out + n) * K, np.float32) if X is None else X
+    ST = np.zeros(st_off + n, np.float32) if ST is None else ST
+    lib().or_embed(int(q8), _words(W), ids, n, K, K // (64 if q8 else 32), float(scale), float(eps), st_off, row_out, X, ST)
+    return X, ST
+
+
+def normadd(T, nsrc, ldp, W, w_off, X, ST, st_off, D, M, *, mode=0, eps=1e-6, scale=1.0):
+    """normadd (lops.js:143-180) on X [M][D] in place; ST[st_off + m] = rstd of the new row"""
+    lib().or_normadd(_f32(T), nsrc, ldp, _f32(W) if W is not None else np.zeros(1, np.float32), w_off, X, ST, st_off, D, M, mode,
+                     float(eps), float(scale))
+    return X, ST
+
+
+def dhead(W, X, ST, NW, SEL, K, tPer, nsel, *, enc="q4g32a.t64", stat_off=0, norm_off=0):
+    """dhead (lops_spec.js:428-482): per selected tile its max and argmax row -> MX f32 [nsel * tPer][2]"""
+    q8 = enc == "q8g64s.t64"
+    MX = np.empty(2 * nsel * tPer, np.float32)
+    lib().or_dhead(int(q8), _f32(X), _words(W), _f32(ST), _f32(NW), np.ascontiguousarray(SEL, np.uint32), stat_off, norm_off, K,
+                   K // (64 if q8 else 32), tPer, nsel, MX)
+    return MX

@@ -6,4 +6,4 @@ and mirrors the reference's operator surface with the same argument objects and 
 over Gpu buffers (engine/core/gpu.js), plus the q4g32a.t64 quantiser packQ4 (engine/kcheck.js:22-38) on the device.
 """
 from .gpu import Buffer, Gpu, P0Error, createGpu, version  # noqa: F401
-from .ops import dequant_f16, gemm, gemv, gemvM, gemvM_noalloc, pack_q4, pack_q8  # noqa: F401
+from .ops import argmax, argmaxM, dequant_f16, dhead, embed, gemm, gemv, gemvM, gemvM_noalloc, normadd, pack_q4, pack_q8  # noqa: F401

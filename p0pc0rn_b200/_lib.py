@@ -23,7 +23,7 @@ P0_ROPE_INTER, P0_ROPE_HALF = 0, 1
 # every symbol include/p0mm.h declares
 EXPORTS = ["p0_init", "p0_destroy", "p0_set_stream", "p0_set_overlap", "p0_last_error", "p0_stats", "p0_buffer", "p0_wrap", "p0_upload", "p0_read",
            "p0_free", "p0_done", "p0_device_ptr", "p0_gemv", "p0_gemvM", "p0_gemvM_noalloc", "p0_gemm", "p0_pack_q4", "p0_pack_q8",
-           "p0_dequant_f16", "p0_version"]
+           "p0_dequant_f16", "p0_version", "p0_argmaxM", "p0_embed", "p0_normadd", "p0_dhead"]
 P0_NOALLOC_SCRATCH_BYTES = 16 << 20   # include/p0mm.h
 P0_OVERLAP_WEIGHTS = 1
 P0_NOALLOC_COUNTER_BYTES = 64 << 10
@@ -65,6 +65,22 @@ class p0_gemm_args(ctypes.Structure):
                 ("h_rope_mode", _u32), ("rope", p0_buf), ("gt", p0_buf)]
 
 
+
+class p0_embed_args(ctypes.Structure):
+    _fields_ = [("w", p0_wview), ("ids", p0_buf), ("x", p0_buf), ("st", p0_buf), ("st_off", _u32), ("K", _u32), ("n", _u32),
+                ("rowOut", _u32), ("scale", ctypes.c_float), ("eps", ctypes.c_float)]
+
+
+class p0_normadd_args(ctypes.Structure):
+    _fields_ = [("t", p0_buf), ("t_n", _u32), ("t_ld", _u32), ("w", p0_buf), ("w_off", _u32), ("x", p0_buf), ("st", p0_buf),
+                ("st_off", _u32), ("D", _u32), ("M", _u32), ("mode", _u32), ("eps", ctypes.c_float), ("scale", ctypes.c_float)]
+
+
+class p0_dhead_args(ctypes.Structure):
+    _fields_ = [("w", p0_wview), ("x", p0_buf), ("stat", p0_buf), ("stat_off", _u32), ("norm", p0_buf), ("norm_off", _u32),
+                ("sel", p0_buf), ("mx", p0_buf), ("K", _u32), ("tPer", _u32), ("nsel", _u32)]
+
+
 _lib = None
 
 
@@ -97,6 +113,10 @@ def load():
     L.p0_pack_q4.argtypes = [vp, p0_buf, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, p0_buf, ctypes.c_uint64]
     L.p0_pack_q8.argtypes = [vp, p0_buf, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, p0_buf, ctypes.c_uint64]
     L.p0_dequant_f16.argtypes = [vp, ctypes.POINTER(p0_wview), p0_buf]
+    L.p0_argmaxM.argtypes = [vp, p0_buf, ctypes.c_uint32, ctypes.c_uint32, p0_buf]
+    L.p0_embed.argtypes = [vp, ctypes.POINTER(p0_embed_args)]
+    L.p0_normadd.argtypes = [vp, ctypes.POINTER(p0_normadd_args)]
+    L.p0_dhead.argtypes = [vp, ctypes.POINTER(p0_dhead_args)]
     L.p0_version.restype = ctypes.c_char_p
     for name in EXPORTS:
         if name != "p0_version":

@@ -1,0 +1,309 @@
+// lops.cu -- the decode-path operators on either side of the GEMV: the token embedding gather (embed, engine/llm/
+// lops.js:323-365), the residual add + RMS statistics (normadd, lops.js:143-180), the argmax over the head's per-tile
+// maxima (argmax / argmaxM, lops.js:416-436, lops_spec.js:326-348) and the drafter's head over selected clusters
+// (dhead, lops_spec.js:428-482). All are small, latency-bound kernels: one CTA per output row (or tile), coalesced
+// loads, warp-shuffle reductions, no global scratch.
+#include <cuda_fp16.h>
+
+#include "internal.h"
+
+namespace {
+
+constexpr int kT = 256;   // threads per CTA
+
+__device__ __forceinline__ float h2f(uint32_t h16) { return __half2float(__ushort_as_half((unsigned short)(h16 & 0xffffu))); }
+
+// (value, index) pairs: the larger value wins, ties go to the lower index; NaN never wins
+__device__ __forceinline__ void better(float &bv, uint32_t &bi, float v, uint32_t i) {
+  if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+}
+__device__ __forceinline__ void warp_best(float &bv, uint32_t &bi) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) better(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
+}
+// CTA sum of one float per thread (every thread gets the total)
+__device__ __forceinline__ float cta_sum(float v, float *red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kT / 32; i++) t += red[i];
+  return t;
+}
+
+// ---------------------------------------------------------------- argmaxM: one CTA per row of n (max, bitcast index) pairs
+__global__ void __launch_bounds__(kT) argmax_kernel(const float2 *__restrict__ MX, uint32_t n, uint32_t *__restrict__ out) {
+  __shared__ float rv[kT / 32];
+  __shared__ uint32_t ri[kT / 32];
+  const uint32_t m = blockIdx.x;
+  const float2 *row = MX + (size_t)m * n;
+  float bv = -3.4e38f;
+  uint32_t bi = 0xffffffffu;
+  for (uint32_t i = threadIdx.x; i < n; i += kT) {
+    const float2 e = row[i];
+    better(bv, bi, e.x, __float_as_uint(e.y));
+  }
+  warp_best(bv, bi);
+  if ((threadIdx.x & 31) == 0) { rv[threadIdx.x >> 5] = bv; ri[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kT / 32; w++) better(bv, bi, rv[w], ri[w]);
+    out[2 * m] = bi;
+    out[2 * m + 1] = __float_as_uint(bv);
+  }
+}
+
+// ---------------------------------------------------------------- embed: one CTA per token; a thread per 8 (q4) / 4 (q8) k
+// q4: v = (f32(q) * s + mn) * scale, q8: v = f32(q) * s * scale, each operation rounded as written (the oracle's order);
+// an id beyond the table reads as a row of zeros (the WGSL's robust buffer access gives no defined value there)
+template <bool Q8>
+__global__ void __launch_bounds__(kT) embed_kernel(const uint8_t *__restrict__ W, uint32_t V, const uint32_t *__restrict__ ids,
+                                                   uint32_t K, uint32_t wG, float scale, float eps, float *__restrict__ X,
+                                                   uint32_t rowOut, float *__restrict__ ST, uint32_t statOff) {
+  __shared__ float red[kT / 32];
+  const uint32_t m = blockIdx.x, id = ids[m];
+  const bool in = id < V;
+  const uint32_t tile = in ? id >> 6 : 0u, r = id & 63u;
+  float *x = X + (size_t)(rowOut + m) * K;
+  float s2 = 0.0f;
+  if (!Q8) {
+    for (uint32_t u = threadIdx.x; u < K / 8; u += kT) {   // group u / 4, code word u % 4 (k = 8u .. 8u + 7)
+      const uint8_t *rec = W + ((size_t)tile * wG + (u >> 2)) * 1280u;
+      float v[8];
+      if (in) {
+        const uint32_t q = *reinterpret_cast<const uint32_t *>(rec + r * 16u + (u & 3u) * 4u);
+        const uint32_t sm = *reinterpret_cast<const uint32_t *>(rec + 1024u + r * 4u);
+        const float s = h2f(sm), mn = h2f(sm >> 16);
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = __fmul_rn(__fadd_rn(__fmul_rn((float)((q >> (4 * j)) & 15u), s), mn), scale);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = 0.0f;
+      }
+      *reinterpret_cast<float4 *>(x + 8u * u) = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4 *>(x + 8u * u + 4u) = make_float4(v[4], v[5], v[6], v[7]);
+#pragma unroll
+      for (int j = 0; j < 8; j++) s2 = fmaf(v[j], v[j], s2);
+    }
+  } else {
+    for (uint32_t u = threadIdx.x; u < K / 4; u += kT) {   // group u / 16, code word u % 16 (k = 4u .. 4u + 3)
+      const uint8_t *rec = W + ((size_t)tile * wG + (u >> 4)) * 4224u;
+      float v[4];
+      if (in) {
+        const uint32_t q = *reinterpret_cast<const uint32_t *>(rec + r * 64u + (u & 15u) * 4u);
+        const float s = h2f(*reinterpret_cast<const uint16_t *>(rec + 4096u + r * 2u));
+#pragma unroll
+        for (int j = 0; j < 4; j++) v[j] = __fmul_rn(__fmul_rn((float)(int8_t)((q >> (8 * j)) & 255u), s), scale);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; j++) v[j] = 0.0f;
+      }
+      *reinterpret_cast<float4 *>(x + 4u * u) = make_float4(v[0], v[1], v[2], v[3]);
+#pragma unroll
+      for (int j = 0; j < 4; j++) s2 = fmaf(v[j], v[j], s2);
+    }
+  }
+  const float tot = cta_sum(s2, red);
+  if (threadIdx.x == 0) ST[statOff + m] = rsqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), eps));
+}
+
+// ---------------------------------------------------------------- normadd: one CTA per row of D
+// tv = sum over the nsrc partial rows (in order); rs = rsqrt(sum tv^2 / D + eps); mode 0: x = (x + tv * rs * w) * scale,
+// mode 1: x = tv; ST = rsqrt(sum x^2 / D + eps). tv is kept in shared memory between the two passes.
+__global__ void __launch_bounds__(kT) normadd_kernel(const float *__restrict__ T, uint32_t nsrc, uint64_t ldp, const float *__restrict__ Wn,
+                                                     float *__restrict__ X, float *__restrict__ ST, uint32_t statOff, uint32_t D,
+                                                     uint32_t mode, float eps, float scale) {
+  extern __shared__ float tv[];
+  __shared__ float red[kT / 32];
+  const uint32_t m = blockIdx.x;
+  const size_t xb = (size_t)m * D;
+  float s = 0.0f;
+  for (uint32_t i = threadIdx.x; i < D; i += kT) {
+    float v = 0.0f;
+    for (uint32_t j = 0; j < nsrc; j++) v = __fadd_rn(v, T[j * ldp + xb + i]);
+    tv[i] = v;
+    s = fmaf(v, v, s);
+  }
+  const float rs = rsqrtf(__fadd_rn(__fdiv_rn(cta_sum(s, red), (float)D), eps));
+  float s2 = 0.0f;
+  for (uint32_t i = threadIdx.x; i < D; i += kT) {
+    float x = X[xb + i];
+    if (mode == 0) x = __fmul_rn(__fadd_rn(x, __fmul_rn(__fmul_rn(tv[i], rs), Wn[i])), scale);
+    else x = tv[i];
+    X[xb + i] = x;
+    s2 = fmaf(x, x, s2);
+  }
+  const float tot = cta_sum(s2, red);
+  if (threadIdx.x == 0) ST[statOff + m] = rsqrtf(__fadd_rn(__fdiv_rn(tot, (float)D), eps));
+}
+
+// ---------------------------------------------------------------- dhead: one CTA per selected tile, thread = (row, k quarter)
+// Row r's dot runs in 4 lanes w (q4: k = 32g + 8w..+7, acc += s * (q . x) + mn * sum(x); q8: k = 64g + 16w..+15, acc +=
+// s * (q . x)), each operation rounded in the oracle's order; the 4 lane sums are added in order, then the tile's max
+// row (lowest row on ties) by shuffles and one shared-memory step. A tile beyond the head writes (-3.4e38, 0xffffffff),
+// which never wins the argmax.
+__device__ __forceinline__ float dot4r(const float *a, const float *b) {
+  return __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(a[0], b[0]), __fmul_rn(a[1], b[1])), __fmul_rn(a[2], b[2])), __fmul_rn(a[3], b[3]));
+}
+template <bool Q8>
+__global__ void __launch_bounds__(kT) dhead_kernel(const float *__restrict__ X, const uint8_t *__restrict__ W, uint32_t ntile,
+                                                   const float *__restrict__ ST, const float *__restrict__ NW, const uint32_t *__restrict__ SEL,
+                                                   uint32_t K, uint32_t wG, uint32_t tPer, float *__restrict__ MX) {
+  __shared__ float xs[512];
+  __shared__ float rv[kT / 32];
+  __shared__ uint32_t ri[kT / 32];
+  const uint32_t wt = blockIdx.x, tile = SEL[wt / tPer] * tPer + (wt % tPer);
+  const float rs = ST[0];
+  for (uint32_t k = threadIdx.x; k < K; k += kT) xs[k] = __fmul_rn(__fmul_rn(X[k], rs), NW[k]);
+  __syncthreads();
+  const uint32_t r = threadIdx.x >> 2, w = threadIdx.x & 3u;
+  float acc = 0.0f;
+  if (tile < ntile) {
+    for (uint32_t g = 0; g < wG; g++) {
+      if (Q8) {
+        const uint8_t *rec = W + ((size_t)tile * wG + g) * 4224u;
+        const float sc = h2f(*reinterpret_cast<const uint16_t *>(rec + 4096u + r * 2u));
+        const uint4 q4 = *reinterpret_cast<const uint4 *>(rec + r * 64u + w * 16u);
+        const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w};
+        float d = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          float qv[4];
+#pragma unroll
+          for (int b = 0; b < 4; b++) qv[b] = (float)(int8_t)((qw[u] >> (8 * b)) & 255u);
+          d = __fadd_rn(d, dot4r(qv, xs + g * 64u + w * 16u + u * 4u));
+        }
+        acc = __fadd_rn(acc, __fmul_rn(sc, d));
+      } else {
+        const uint8_t *rec = W + ((size_t)tile * wG + g) * 1280u;
+        const uint32_t q = *reinterpret_cast<const uint32_t *>(rec + r * 16u + w * 4u);
+        const uint32_t sm = *reinterpret_cast<const uint32_t *>(rec + 1024u + r * 4u);
+        float qa[4], qb[4];
+#pragma unroll
+        for (int b = 0; b < 4; b++) { qa[b] = (float)((q >> (4 * b)) & 15u); qb[b] = (float)((q >> (16 + 4 * b)) & 15u); }
+        const float *xv = xs + g * 32u + w * 8u;
+        const float one[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+        const float dq = __fadd_rn(dot4r(qa, xv), dot4r(qb, xv + 4)), dx = __fadd_rn(dot4r(xv, one), dot4r(xv + 4, one));
+        acc = __fadd_rn(__fadd_rn(acc, __fmul_rn(h2f(sm), dq)), __fmul_rn(h2f(sm >> 16), dx));
+      }
+    }
+  }
+  // the row total: lanes w = 0..3 of the row are consecutive threads; lane 0 adds them in order
+  const float a1 = __shfl_down_sync(0xffffffffu, acc, 1), a2 = __shfl_down_sync(0xffffffffu, acc, 2), a3 = __shfl_down_sync(0xffffffffu, acc, 3);
+  float bv = -3.4e38f;
+  uint32_t bi = 0xffffffffu;
+  if (w == 0 && tile < ntile) {
+    bv = __fadd_rn(__fadd_rn(__fadd_rn(acc, a1), a2), a3);
+    bi = tile * 64u + r;
+  }
+  warp_best(bv, bi);
+  if ((threadIdx.x & 31) == 0) { rv[threadIdx.x >> 5] = bv; ri[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < kT / 32; i++) better(bv, bi, rv[i], ri[i]);
+    MX[wt * 2] = bv;
+    MX[wt * 2 + 1] = __uint_as_float(bi);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+// argmax(g, a) (lops.js:434-436) is argmaxM with M = 1 (lops_spec.js:346-348)
+p0_status p0_argmaxM(p0_ctx *c, p0_buf mx, uint32_t n, uint32_t M, p0_buf out) {
+  if (!c) return P0_EINVAL;
+  if (!M) return P0_OK;
+  P0Range rm, ro;
+  p0_status st;
+  if ((st = p0_range(c, mx, 0, (uint64_t)M * n * 8, "argmax", "MX", &rm))) return st;
+  if ((st = p0_range(c, out, 0, (uint64_t)M * 8, "argmax", "OUT", &ro))) return st;
+  cudaSetDevice(c->device);
+  argmax_kernel<<<M, kT, 0, c->stream>>>((const float2 *)rm.base, n, (uint32_t *)ro.base);
+  return p0_launched(c, "argmax");
+}
+
+p0_status p0_embed(p0_ctx *c, const p0_embed_args *a) {
+  if (!c || !a) return P0_EINVAL;
+  const bool q8 = a->w.enc == P0_ENC_Q8G64S_T64;
+  if (!q8 && a->w.enc != P0_ENC_Q4G32A_T64) return p0_fail(c, P0_EINVAL, "embed: encoding %u", a->w.enc);
+  const uint32_t GK = q8 ? 64u : 32u, RB = q8 ? 4224u : 1280u, K = a->K;
+  if (!a->n) return P0_OK;
+  if (!K || K % GK) return p0_fail(c, P0_EINVAL, "embed: K must be a multiple of %u", GK);
+  if (a->w.rows % 64 || a->w.cols != K) return p0_fail(c, P0_EINVAL, "embed: the table view must be [rows %% 64][K] (%ux%u)", a->w.rows, a->w.cols);
+  const uint32_t wG = K / GK;
+  P0Range rw, ri, rx, rs;
+  p0_status st;
+  if ((st = p0_range(c, a->w.buf, a->w.off, (uint64_t)(a->w.rows / 64) * wG * RB, "embed", "W", &rw))) return st;
+  if ((uintptr_t)rw.base % 16) return p0_fail(c, P0_EALIGN, "embed: table offset must be 16-byte aligned");
+  if ((st = p0_range(c, a->ids, 0, (uint64_t)a->n * 4, "embed", "IDS", &ri))) return st;
+  if ((st = p0_range(c, a->x, 0, ((uint64_t)a->rowOut + a->n) * K * 4, "embed", "X", &rx))) return st;
+  if ((st = p0_range(c, a->st, 0, ((uint64_t)a->st_off + a->n) * 4, "embed", "ST", &rs))) return st;
+  const float eps = a->eps != 0.0f ? a->eps : 1e-6f;   // lops.js:364 `a.eps || 1e-6`
+  cudaSetDevice(c->device);
+  if (q8)
+    embed_kernel<true><<<a->n, kT, 0, c->stream>>>(rw.base, a->w.rows, (const uint32_t *)ri.base, K, wG, a->scale, eps, (float *)rx.base,
+                                                    a->rowOut, (float *)rs.base, a->st_off);
+  else
+    embed_kernel<false><<<a->n, kT, 0, c->stream>>>(rw.base, a->w.rows, (const uint32_t *)ri.base, K, wG, a->scale, eps, (float *)rx.base,
+                                                     a->rowOut, (float *)rs.base, a->st_off);
+  return p0_launched(c, "embed");
+}
+
+p0_status p0_normadd(p0_ctx *c, const p0_normadd_args *a) {
+  if (!c || !a) return P0_EINVAL;
+  const uint32_t D = a->D, M = a->M ? a->M : 1, nsrc = a->t_n ? a->t_n : 1;
+  if (!D) return P0_OK;
+  if (a->mode > 1) return p0_fail(c, P0_EINVAL, "normadd: mode %u", a->mode);
+  if ((size_t)D * 4 > 200u * 1024u) return p0_fail(c, P0_EINVAL, "normadd: D %u exceeds the shared-memory row (51200)", D);
+  const uint64_t ldp = a->t_ld ? a->t_ld : (uint64_t)D * M;
+  P0Range rt, rw, rx, rs;
+  p0_status st;
+  if ((st = p0_range(c, a->t, 0, ((uint64_t)(nsrc - 1) * ldp + (uint64_t)M * D) * 4, "normadd", "T", &rt))) return st;
+  if (a->mode == 0 && (st = p0_range(c, a->w, 0, ((uint64_t)a->w_off + D) * 4, "normadd", "W", &rw))) return st;
+  if ((st = p0_range(c, a->x, 0, (uint64_t)M * D * 4, "normadd", "X", &rx))) return st;
+  if ((st = p0_range(c, a->st, 0, ((uint64_t)a->st_off + M) * 4, "normadd", "ST", &rs))) return st;
+  const float eps = a->eps != 0.0f ? a->eps : 1e-6f;   // lops.js:177 `a.eps || 1e-6`
+  const size_t smem = (size_t)D * 4;
+  cudaSetDevice(c->device);
+  if (smem > 48u * 1024u) cudaFuncSetAttribute(normadd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  normadd_kernel<<<M, kT, smem, c->stream>>>((const float *)rt.base, nsrc, ldp, a->mode == 0 ? (const float *)rw.base + a->w_off : nullptr,
+                                             (float *)rx.base, (float *)rs.base, a->st_off, D, a->mode, eps, a->scale);
+  return p0_launched(c, "normadd");
+}
+
+p0_status p0_dhead(p0_ctx *c, const p0_dhead_args *a) {
+  if (!c || !a) return P0_EINVAL;
+  const bool q8 = a->w.enc == P0_ENC_Q8G64S_T64;
+  if (!q8 && a->w.enc != P0_ENC_Q4G32A_T64) return p0_fail(c, P0_EINVAL, "dhead: encoding %u", a->w.enc);
+  const uint32_t K = a->K, GK = q8 ? 64u : 32u, RB = q8 ? 4224u : 1280u;
+  if (K > 512) return p0_fail(c, P0_EINVAL, "dhead: K > 512");
+  if (!K || K % GK) return p0_fail(c, P0_EINVAL, "dhead: K must be a multiple of %u", GK);
+  if (a->w.rows % 64 || a->w.cols != K) return p0_fail(c, P0_EINVAL, "dhead: the head view must be [rows %% 64][K] (%ux%u)", a->w.rows, a->w.cols);
+  const uint32_t nblk = a->nsel * a->tPer, wG = K / GK;
+  if (!nblk) return P0_OK;
+  P0Range rx, rw, rs, rn, rsel, rm;
+  p0_status st;
+  if ((st = p0_range(c, a->x, 0, (uint64_t)K * 4, "dhead", "X", &rx))) return st;
+  if ((st = p0_range(c, a->w.buf, a->w.off, (uint64_t)(a->w.rows / 64) * wG * RB, "dhead", "W", &rw))) return st;
+  if ((uintptr_t)rw.base % 16) return p0_fail(c, P0_EALIGN, "dhead: head offset must be 16-byte aligned");
+  if ((st = p0_range(c, a->stat, 0, ((uint64_t)a->stat_off + 1) * 4, "dhead", "ST", &rs))) return st;
+  if ((st = p0_range(c, a->norm, 0, ((uint64_t)a->norm_off + K) * 4, "dhead", "NW", &rn))) return st;
+  if ((st = p0_range(c, a->sel, 0, (uint64_t)a->nsel * 4, "dhead", "SEL", &rsel))) return st;
+  if ((st = p0_range(c, a->mx, 0, (uint64_t)nblk * 8, "dhead", "MX", &rm))) return st;
+  cudaSetDevice(c->device);
+  const float *stp = (const float *)rs.base + a->stat_off, *nw = (const float *)rn.base + a->norm_off;
+  if (q8)
+    dhead_kernel<true><<<nblk, kT, 0, c->stream>>>((const float *)rx.base, rw.base, a->w.rows / 64, stp, nw, (const uint32_t *)rsel.base, K,
+                                                    wG, a->tPer, (float *)rm.base);
+  else
+    dhead_kernel<false><<<nblk, kT, 0, c->stream>>>((const float *)rx.base, rw.base, a->w.rows / 64, stp, nw, (const uint32_t *)rsel.base, K,
+                                                     wG, a->tPer, (float *)rm.base);
+  return p0_launched(c, "dhead");
+}
+
+}  // extern "C"

@@ -134,3 +134,57 @@ def pack_q8(g, w_f32, N, K, out=None, w_off=0, ldw=0, out_off=0):
         out = g.buffer(N * K // 64 * 66, "q8")
     g._check(g._lib.p0_pack_q8(g.ctx, handle(w_f32), int(w_off), int(ldw), int(N), int(K), handle(out), int(out_off)))
     return out
+
+
+# ---------------------------------------------------------------- decode-path operators (lops.js, lops_spec.js)
+def argmax(g, a):
+    """argmax(g, a) (lops.js:434-436): a = {mx: {buf}, n, out: {buf}}; out[0] = the index of the largest of the n
+    (max, bitcast index) pairs (ties: the lowest index), out[1] = the bits of that max"""
+    g._check(g._lib.p0_argmaxM(g.ctx, handle(a["mx"]["buf"]), int(a["n"]), 1, handle(a["out"]["buf"])))
+
+
+def argmaxM(g, a):
+    """argmaxM(g, a) (lops_spec.js:346-348): a = {mx: {buf}, n, M, out: {buf}}; per row m of mx [M][n][2], out[2m] /
+    out[2m + 1] as argmax"""
+    g._check(g._lib.p0_argmaxM(g.ctx, handle(a["mx"]["buf"]), int(a["n"]), int(a["M"]), handle(a["out"]["buf"])))
+
+
+def embed(g, a):
+    """embed(g, a) (lops.js:352-365): a = {w (q4 / q8 table view), ids: {buf}, x: {buf}, st: {buf, off}, K, n, scale,
+    rowOut, eps}; x[(rowOut + m) * K + k] = dequant(w[ids[m]]) * scale, st[off + m] = the row's rstd"""
+    w = a["w"]
+    enc = w.get("enc") or "q4g32a.t64"
+    if enc not in ("q4g32a.t64", "q8g64s.t64"):
+        raise P0Error(L.P0_EINVAL, "embed: encoding " + str(enc))
+    st = a["st"]
+    args = L.p0_embed_args(_wview(w, "embed"), handle(a["ids"]["buf"]), handle(a["x"]["buf"]), handle(st["buf"]),
+                           int(st.get("off") or 0), int(a["K"]), int(a["n"]), int(a.get("rowOut") or 0), float(a["scale"]),
+                           float(a.get("eps") or 0.0))
+    g._check(g._lib.p0_embed(g.ctx, ctypes.byref(args)))
+
+
+def normadd(g, a):
+    """normadd(g, a) (lops.js:174-180): a = {t: {buf, n, ld}, w: {buf, off} (mode 0), x: {buf}, st: {buf, off}, D, M,
+    eps, scale (default 1), mode (0: x = (x + rms(t) * w) * scale, 1: x = t)}"""
+    t, w, st = a["t"], a.get("w"), a["st"]
+    scale = a.get("scale")
+    args = L.p0_normadd_args(handle(t["buf"]), int(t.get("n") or 1), int(t.get("ld") or 0), _b(w), int((w or {}).get("off") or 0),
+                             handle(a["x"]["buf"]), handle(st["buf"]), int(st.get("off") or 0), int(a["D"]), int(a.get("M") or 1),
+                             int(a.get("mode") or 0), float(a.get("eps") or 0.0), 1.0 if scale is None else float(scale))
+    g._check(g._lib.p0_normadd(g.ctx, ctypes.byref(args)))
+
+
+def dhead(g, a):
+    """dhead(g, a) (lops_spec.js:475-482): a = {w (q4 / q8 head view), x: {buf}, stat: {buf, off}, norm: {buf, off},
+    sel: {buf}, mx: {buf}, K (<= 512), tPer, nsel}; per selected tile its largest row dot and that row's index"""
+    w = a["w"]
+    enc = w.get("enc") or "q4g32a.t64"
+    if enc not in ("q4g32a.t64", "q8g64s.t64"):
+        raise P0Error(L.P0_EINVAL, "dhead: encoding " + str(enc))
+    if int(a["K"]) > 512:
+        raise P0Error(L.P0_EINVAL, "dhead: K > 512")
+    stat, norm = a["stat"], a["norm"]
+    args = L.p0_dhead_args(_wview(w, "dhead"), handle(a["x"]["buf"]), handle(stat["buf"]), int(stat.get("off") or 0),
+                           handle(norm["buf"]), int(norm.get("off") or 0), handle(a["sel"]["buf"]), handle(a["mx"]["buf"]),
+                           int(a["K"]), int(a["tPer"]), int(a["nsel"]))
+    g._check(g._lib.p0_dhead(g.ctx, ctypes.byref(args)))

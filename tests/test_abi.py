@@ -40,6 +40,9 @@ STRUCTS = {
     "p0_gemv_args": L.p0_gemv_args,
     "p0_gemvM_args": L.p0_gemvM_args,
     "p0_gemm_args": L.p0_gemm_args,
+    "p0_embed_args": L.p0_embed_args,
+    "p0_normadd_args": L.p0_normadd_args,
+    "p0_dhead_args": L.p0_dhead_args,
 }
 
 

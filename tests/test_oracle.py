@@ -282,3 +282,91 @@ def test_onormgate_oracle_identities():
     want = A * inv * ev / (1 + np.exp(-g))
     assert np.max(np.abs(y[:, 4:132] - want)) <= 2e-3 * max(1.0, np.max(np.abs(want)))
     assert not y[:, :4].any() and not y[:, 132:].any()   # columns outside the head untouched
+
+
+# ---------------------------------------------------------------- decode-path operators (lops.js, lops_spec.js)
+# No reference vectors exist for these; each restatement is pinned against an independent numpy statement of the
+# same math.
+def test_argmax_oracle_rules():
+    rng = np.random.default_rng(5)
+    M, n = 3, 1000
+    v = rng.standard_normal((M, n)).astype(np.float32)
+    idx = rng.permutation(M * n).astype(np.uint32).reshape(M, n)
+    v[1, 17] = v[1, 600] = 9.0                 # a tie: the lower index wins
+    idx[1, 17], idx[1, 600] = 500, 40
+    v[2, 3] = np.nan                           # NaN never wins
+    MX = np.empty((M, n, 2), np.float32)
+    MX[:, :, 0] = v
+    MX[:, :, 1] = idx.view(np.float32)
+    out = ref.argmaxM(MX.ravel(), n, M).reshape(M, 2)
+    for m in range(M):
+        vm = np.where(np.isnan(v[m]), -np.inf, v[m])
+        best = vm.max()
+        assert out[m, 0] == idx[m][vm == best].min()
+        assert out[m, 1] == np.float32(best).view(np.uint32)
+    assert out[1, 0] == 40
+
+
+def _deq_row(b, enc, i, K):
+    """row i of a q4 / q8 table dequantised in numpy f32: q * s + mn (q4) or q * s (q8), before any fp16 rounding"""
+    raw = np.frombuffer(np.asarray(b, np.uint8).tobytes(), np.uint8)
+    t, r = i // 64, i % 64
+    if enc == "q4g32a.t64":
+        rec = [raw[(t * (K // 32) + g) * 1280:(t * (K // 32) + g + 1) * 1280] for g in range(K // 32)]
+        q = np.concatenate([np.stack([rc[r * 16:r * 16 + 16] & 15, rc[r * 16:r * 16 + 16] >> 4], 1).ravel() for rc in rec])
+        sm = np.array([rc[1024 + 4 * r:1028 + 4 * r].view(np.uint16) for rc in rec])
+        s, mn = np.repeat(ref.h2f(sm[:, 0]), 32).astype(np.float32), np.repeat(ref.h2f(sm[:, 1]), 32).astype(np.float32)
+        return q.astype(np.float32) * s + mn
+    rec = [raw[(t * (K // 64) + g) * 4224:(t * (K // 64) + g + 1) * 4224] for g in range(K // 64)]
+    q = np.concatenate([rc[r * 64:r * 64 + 64].view(np.int8) for rc in rec]).astype(np.float32)
+    s = np.repeat(ref.h2f(np.array([rc[4096 + 2 * r:4098 + 2 * r].view(np.uint16)[0] for rc in rec])), 64).astype(np.float32)
+    return q * s
+
+
+@pytest.mark.parametrize("enc", ["q4g32a.t64", "q8g64s.t64"])
+def test_embed_oracle_against_dequant(enc):
+    V, K = 192, 256
+    b, _ = (ref.pack_q4 if enc == "q4g32a.t64" else ref.pack_q8)(ref.randn(V * K, 30, 0.05), V, K)
+    ids = np.array([0, 63, 64, 191, 7], np.uint32)
+    X, ST = ref.embed(b, ids, K, enc=enc, scale=1.5, eps=1e-6)
+    for m, i in enumerate(ids):
+        row = _deq_row(b, enc, int(i), K) * np.float32(1.5)
+        assert np.array_equal(X[m * K:(m + 1) * K], row)
+        want = 1.0 / np.sqrt(np.mean(row.astype(np.float64) ** 2) + 1e-6)
+        assert abs(ST[m] - want) <= 1e-5 * want
+
+
+@pytest.mark.parametrize("mode,nsrc", [(0, 1), (0, 3), (1, 2)])
+def test_normadd_oracle(mode, nsrc):
+    M, D = 3, 1000
+    T = ref.randn(nsrc * M * D, 40, 1.0)
+    W = ref.randn(D + 5, 41, 0.2) + 1
+    X0 = ref.randn(M * D, 42)
+    X, ST = X0.copy(), np.zeros(M + 2, np.float32)
+    ref.normadd(T, nsrc, M * D, W, 5, X, ST, 2, D, M, mode=mode, eps=1e-6, scale=0.7)
+    t = T.astype(np.float64).reshape(nsrc, M, D).sum(0)
+    if mode == 0:
+        rs = 1 / np.sqrt((t ** 2).mean(1, keepdims=True) + 1e-6)
+        want = (X0.astype(np.float64).reshape(M, D) + t * rs * W[5:]) * 0.7
+    else:
+        want = t
+    assert np.max(np.abs(X.reshape(M, D) - want)) <= 1e-5 * max(1.0, np.abs(want).max())
+    assert np.allclose(ST[2:], 1 / np.sqrt((want ** 2).mean(1) + 1e-6), rtol=1e-5)
+
+
+@pytest.mark.parametrize("enc,K", [("q4g32a.t64", 512), ("q8g64s.t64", 256)])
+def test_dhead_oracle(enc, K):
+    V = 64 * 12
+    b, _ = (ref.pack_q4 if enc == "q4g32a.t64" else ref.pack_q8)(ref.randn(V * K, 50, 0.05), V, K)
+    X, NW = ref.randn(K, 51), ref.randn(K + 3, 52, 0.1) + 1
+    ST = np.array([0.0, 0.8], np.float32)
+    SEL = np.array([4, 1, 3], np.uint32)
+    MX = ref.dhead(b, X, ST, NW, SEL, K, 2, 3, enc=enc, stat_off=1, norm_off=3)
+    xs = X.astype(np.float64) * 0.8 * NW[3:]
+    for wt in range(6):
+        tile = SEL[wt // 2] * 2 + wt % 2
+        rows = np.array([_deq_row(b, enc, int(tile) * 64 + r, K) for r in range(64)], np.float64)
+        dots = rows @ xs
+        r = int(np.argmax(dots))
+        assert MX[2 * wt + 1].view(np.uint32) == tile * 64 + r
+        assert abs(MX[2 * wt] - dots[r]) <= 1e-4 * max(1.0, abs(dots[r]))
