@@ -67,6 +67,10 @@ p0_status p0_buffer(p0_ctx *ctx, size_t bytes, const char *label, p0_buf *out);
 p0_status p0_wrap(p0_ctx *ctx, void *device_ptr, size_t bytes, const char *label, p0_buf *out);
 /* Gpu.upload / queue.writeBuffer (gpu.js:98-117): host -> device, ordered on the stream */
 p0_status p0_upload(p0_ctx *ctx, p0_buf buf, size_t dst_off, const void *src, size_t n);
+/* WeightStore.upload's copy loop (core/store.js:222-245) from a pack file: bytes at file_off of the file at path ->
+ * buf at dst_off, in 16 MiB chunks through two pinned staging buffers (disk reads overlap the copies). Returns with the
+ * last copies in flight on the stream; the staging buffers are reused only after their copies have finished. */
+p0_status p0_upload_file(p0_ctx *ctx, p0_buf buf, uint64_t dst_off, const char *path, uint64_t file_off, uint64_t bytes);
 /* Gpu.read(buf, off, n) -> Gpu._readback (gpu.js:118-140): flushes the stream, then device -> host */
 p0_status p0_read(p0_ctx *ctx, p0_buf buf, size_t off, size_t n, void *dst);
 /* Gpu.free (gpu.js:89-94) */

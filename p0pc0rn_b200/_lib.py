@@ -23,7 +23,8 @@ P0_ROPE_INTER, P0_ROPE_HALF = 0, 1
 # every symbol include/p0mm.h declares
 EXPORTS = ["p0_init", "p0_destroy", "p0_set_stream", "p0_set_overlap", "p0_last_error", "p0_stats", "p0_buffer", "p0_wrap", "p0_upload", "p0_read",
            "p0_free", "p0_done", "p0_device_ptr", "p0_gemv", "p0_gemvM", "p0_gemvM_noalloc", "p0_gemm", "p0_pack_q4", "p0_pack_q8",
-           "p0_dequant_f16", "p0_version", "p0_argmaxM", "p0_embed", "p0_normadd", "p0_dhead"]
+           "p0_dequant_f16", "p0_version", "p0_argmaxM", "p0_embed", "p0_normadd", "p0_dhead",
+           "p0_upload_file"]
 P0_NOALLOC_SCRATCH_BYTES = 16 << 20   # include/p0mm.h
 P0_OVERLAP_WEIGHTS = 1
 P0_NOALLOC_COUNTER_BYTES = 64 << 10
@@ -113,6 +114,7 @@ def load():
     L.p0_pack_q4.argtypes = [vp, p0_buf, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, p0_buf, ctypes.c_uint64]
     L.p0_pack_q8.argtypes = [vp, p0_buf, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, p0_buf, ctypes.c_uint64]
     L.p0_dequant_f16.argtypes = [vp, ctypes.POINTER(p0_wview), p0_buf]
+    L.p0_upload_file.argtypes = [vp, p0_buf, ctypes.c_uint64, ctypes.c_char_p, ctypes.c_uint64, ctypes.c_uint64]
     L.p0_argmaxM.argtypes = [vp, p0_buf, ctypes.c_uint32, ctypes.c_uint32, p0_buf]
     L.p0_embed.argtypes = [vp, ctypes.POINTER(p0_embed_args)]
     L.p0_normadd.argtypes = [vp, ctypes.POINTER(p0_normadd_args)]

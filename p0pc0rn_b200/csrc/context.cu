@@ -67,6 +67,10 @@ p0_status p0_destroy(p0_ctx *c) {
   if (c->ws) cudaFree(c->ws);
   if (c->d_err) cudaFree(c->d_err);
   if (c->h_err) cudaFreeHost(c->h_err);
+  for (int i = 0; i < 2; i++) {
+    if (c->io_stage[i]) cudaFreeHost(c->io_stage[i]);
+    if (c->io_done[i]) cudaEventDestroy(c->io_done[i]);
+  }
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete c;
   return P0_OK;

@@ -34,6 +34,9 @@ struct p0_ctx {
   void *ws = nullptr;
   size_t ws_bytes = 0, ws_cnt_bytes = 0;
   bool overlap = false;          // p0_set_overlap: weights are static, GEMVs may fetch them before the call ahead ends
+  // p0_upload_file: two pinned staging chunks and the events that say when the copy out of each has finished
+  void *io_stage[2] = {nullptr, nullptr};
+  cudaEvent_t io_done[2] = {nullptr, nullptr};
   std::mutex mu;
 };
 

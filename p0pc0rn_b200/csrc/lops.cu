@@ -270,7 +270,8 @@ p0_status p0_normadd(p0_ctx *c, const p0_normadd_args *a) {
   const float eps = a->eps != 0.0f ? a->eps : 1e-6f;   // lops.js:177 `a.eps || 1e-6`
   const size_t smem = (size_t)D * 4;
   cudaSetDevice(c->device);
-  if (smem > 48u * 1024u) cudaFuncSetAttribute(normadd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // above the 48 KB default the kernel opts in (its static reduction array counts against the same limit)
+  if (smem > 40u * 1024u) cudaFuncSetAttribute(normadd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   normadd_kernel<<<M, kT, smem, c->stream>>>((const float *)rt.base, nsrc, ldp, a->mode == 0 ? (const float *)rw.base + a->w_off : nullptr,
                                              (float *)rx.base, (float *)rs.base, a->st_off, D, a->mode, eps, a->scale);
   return p0_launched(c, "normadd");

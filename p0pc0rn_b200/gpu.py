@@ -5,6 +5,7 @@ Buffers are opaque handles owned by the context, like WebGPU buffers owned by Gp
 library's message, which keeps the reference's wording (e.g. "gemv: N % 64").
 """
 import ctypes
+import os
 
 import numpy as np
 
@@ -111,6 +112,14 @@ class Gpu:
         self._check(self._lib.p0_upload(self.ctx, b.handle, int(dst_off), a.ctypes.data_as(ctypes.c_void_p), nbytes))
         # the copy is stream-ordered; keep the host array alive until it has been consumed
         self._check(self._lib.p0_done(self.ctx, 0))
+        return b
+
+    def upload_file(self, b, path, file_off=0, nbytes=None, dst_off=0):
+        """nbytes of the file at path (from file_off) into buffer b at dst_off: the native chunked, double-buffered
+        disk -> pinned -> device copy (p0_upload_file); the copies are ordered on the stream"""
+        if nbytes is None:
+            nbytes = os.path.getsize(path) - int(file_off)
+        self._check(self._lib.p0_upload_file(self.ctx, b.handle, int(dst_off), os.fsencode(path), int(file_off), int(nbytes)))
         return b
 
     def write(self, b, data, dst_off=0):
