@@ -270,19 +270,22 @@ def run_ours(args, ws, rank, local):
     R = max(len(c["ring"]) for c in small)
     g_small = [capture(torch, stream, lambda: [sw.launch(c) for c in small]) for _ in range(R)]
     g_head = [(c, capture(torch, stream, lambda c=c: sw.launch(c))) for c in heads]
+    # the whole step as one graph per ring position (small calls, then the head calls): the steps that time the head use
+    # the split graphs above with events between them
+    g_step = [capture(torch, stream, lambda: [sw.launch(c) for c in small + heads]) for _ in range(R)]
     g_copy = capture(torch, stream, copies) if dist else None
 
     def step(s, head_events=None):
-        g_small[s % R].replay()
-        for c, gr in g_head:
-            if head_events is not None:
+        if head_events is None:
+            g_step[s % R].replay()
+        else:
+            g_small[s % R].replay()
+            for c, gr in g_head:
                 e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                 e[0].record()
                 gr.replay()
                 e[1].record()
                 head_events.append((c, e))
-            else:
-                gr.replay()
         if dist:
             g_copy.replay()
             dist.all_gather_into_tensor(gather_dst, gather_src)
@@ -350,8 +353,9 @@ def run_ours(args, ws, rank, local):
             "dtype": "q4 weights, f32 x/accumulate", "data": "synthetic (seeded N(0,0.02) weights packed to q4g32a.t64 on device; N(0,1) fp16 x)",
             "config": {"workload": "config2_gemv_sweep", "M": list(MS), "N": list(NS), "K": K, "parallelism": "column-split x%d + all-gather" % ws,
                        "l2": "weight rings >= 2x L2 per small-N call; head 335 MB > L2", "bytes_per_step": sw.step_bytes * ws,
-                       "launch": "CUDA graphs of the library's calls (small-N calls per ring position, one per head call); "
-                                 "events between graph launches time the head"},
+                       "launch": "one CUDA graph per step (the 12 library calls, per weight-ring position); on ~1% of the "
+                                 "timed steps the small calls and each head call run as separate graphs with events between "
+                                 "them, which time the head"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "traffic": HEAD_TRAFFIC if ws == 1 else None,
                          "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one head launch at M=1 from an ncu "
