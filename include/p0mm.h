@@ -245,6 +245,32 @@ typedef struct {
 } p0_dhead_args;
 p0_status p0_dhead(p0_ctx *ctx, const p0_dhead_args *a);
 
+/* qkrope(g, a) (lops.js:183-233), one decode token: heads of s (the sum of s_n (0 = 1) partial rows of s_ld floats,
+ * 0 = (nq + 2 nkv) * D) laid out [q (nq heads) | k (nkv) | v (nkv)] of D each (k and v only when hasKV).
+ * rs = rsqrt(mean square + eps) (eps 0 = 1e-6). v: vc[(kvh * kvLen + kvRow) * D + i] = f16(x * rs). q / k: a = x[d] rs
+ * norm[w + d], b = x[d + D/2] rs norm[w + d + D/2] (w = qw or kw), rotated by (cos, sin) = rope[rope_off + (pos *
+ * npairs + d) * 2 ..] for d < npairs (else unrotated): q -> q[h * D + d], q[h * D + d + D/2] (f32); k -> kc (fp16,
+ * head-major [nkv][kvLen][D], row kvRow). Buffers from their start. */
+typedef struct {
+  p0_buf s; uint32_t s_n, s_ld;
+  p0_buf norm; uint32_t qw, kw;
+  p0_buf rope; uint32_t rope_off, npairs, pos;
+  p0_buf q, kc, vc;
+  uint32_t D, nq, nkv, hasKV, kvRow, kvLen;
+  float eps;
+} p0_qkrope_args;
+p0_status p0_qkrope(p0_ctx *ctx, const p0_qkrope_args *a);
+
+/* attnDec(g, a) + its combine (lops.js:236-321): decode attention of nh <= 8 query heads (q f32 [nh][D], D % 128 == 0,
+ * D <= 512) over keys [kStart, kEnd) of the fp16 caches kc / vc (head-major [nkv][kvLen][D]; query head h reads KV
+ * head h / (nh / nkv); key j is row j % ring when ring > 0), in chunks of 64 keys (at most 256 chunks): softmax(q . k)
+ * . v per head, no score scale -> out f32 [nh][D]. part: scratch of >= nchunk * nh * (2 + D) floats. */
+typedef struct {
+  p0_buf q, kc, vc, part, out;
+  uint32_t D, nh, nkv, kvLen, kStart, kEnd, ring;
+} p0_attn_dec_args;
+p0_status p0_attn_dec(p0_ctx *ctx, const p0_attn_dec_args *a);
+
 /* ---------------------------------------------------------------------------------------------- quantiser */
 /* packQ4 (engine/kcheck.js:22-38) on the device, bit for bit: W f32 [N][ldw] at w_off (bytes) -> q4g32a.t64 records
  * (N*K*5/8 bytes) at out_off. N % 64 == 0, K % 32 == 0. The dequantised value of code q is q*s + mn. */

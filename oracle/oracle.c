@@ -715,3 +715,100 @@ void or_dhead(int q8, const float *X, const uint32_t *W, const float *ST, const 
     MX[wt * 2] = best; memcpy(&MX[wt * 2 + 1], &bidx, 4);
   }
 }
+
+/* qkrope (lops.js:183-233), decode: per head h of [q (nq) | k (nkv) | v (nkv)] (k and v only when hasKV): hv = the sum
+ * of the nsrc partial rows S[j * ldp + h * D + i]; rs = inverseSqrt(sum hv^2 / D + eps) (256 strided partials, tree).
+ * v heads: VC[(kvh * kvLen + kvRow) * D + i] = f16(hv[i] * rs). q / k heads, d < D/2: a = hv[d] * rs * NW[wo + d],
+ * b = hv[d + D/2] * rs * NW[wo + d + D/2] (wo = qwOff or kwOff); (c, s) = RP[ropeOff + (pos * npairs + d) * 2 ..] for
+ * d < npairs, else (1, 0); lo = a c - b s, hi = b c + a s: q -> Q[h * D + d] = lo, Q[h * D + d + D/2] = hi (f32);
+ * k -> KC[(kvh * kvLen + kvRow) * D + d] = f16(lo), [.. + d + D/2] = f16(hi). */
+void or_qkrope(const float *S, uint32_t nsrc, uint32_t ldp, const float *NW, const float *RP, float *Q, uint16_t *KC, uint16_t *VC,
+               uint32_t D, uint32_t nq, uint32_t nkv, int hasKV, uint32_t pos, float eps, uint32_t qwOff, uint32_t kwOff,
+               uint32_t npairs, uint32_t ropeOff, uint32_t kvRow, uint32_t kvLen) {
+  float *hv = (float *)malloc(sizeof(float) * D);
+  float red[256];
+  const uint32_t nh = nq + (hasKV ? 2 * nkv : 0), half = D / 2;
+  for (uint32_t h = 0; h < nh; h++) {
+    const size_t base = (size_t)h * D;
+    for (uint32_t t = 0; t < 256; t++) {
+      float s = 0.0f;
+      for (uint32_t i = t; i < D; i += 256) {
+        float v = 0.0f;
+        for (uint32_t j = 0; j < nsrc; j++) v = v + S[(size_t)j * ldp + base + i];
+        hv[i] = v; s = s + v * v;
+      }
+      red[t] = s;
+    }
+    const float rs = (float)(1.0 / sqrt((double)(tree256(red) / (float)D + eps)));
+    const int isV = h >= nq + nkv;
+    const uint32_t kvh = isV ? h - nq - nkv : h - nq;
+    const size_t cb = ((size_t)kvh * kvLen + kvRow) * D;
+    if (isV) { for (uint32_t i = 0; i < D; i++) VC[cb + i] = or_f2h((double)(hv[i] * rs)); continue; }
+    const uint32_t wo = h >= nq ? kwOff : qwOff;
+    for (uint32_t d = 0; d < half; d++) {
+      float a = hv[d] * rs; a = a * NW[wo + d];
+      float b = hv[d + half] * rs; b = b * NW[wo + d + half];
+      float c = 1.0f, sn = 0.0f;
+      if (d < npairs) { const size_t rb = ropeOff + ((size_t)pos * npairs + d) * 2; c = RP[rb]; sn = RP[rb + 1]; }
+      const float lo = a * c - b * sn, hi = b * c + a * sn;
+      if (h < nq) { Q[base + d] = lo; Q[base + d + half] = hi; }
+      else { KC[cb + d] = or_f2h((double)lo); KC[cb + d + half] = or_f2h((double)hi); }
+    }
+  }
+  free(hv);
+}
+
+/* attnDec + its combine (lops.js:236-321), decode attention over keys [kStart, kEnd) in chunks of 64: Q f32 [nh][D];
+ * KC / VC fp16 head-major [nkv][kvLen][D] (query head hh reads KV head hh / (nh / nkv)); cache row of key j is j % ring
+ * when ring > 0. Per chunk: s[hh][j] = sum over d of f32(K) Q in 4-wide steps, m = max, p = exp(s - m), l = sum p,
+ * acc[hh][d] = sum_k p V (keys in order); combine per head: M = max m_c, w_c = exp(m_c - M), L = sum w_c l_c,
+ * O[hh][d] = sum_c (w_c / L) acc_c[hh][d]. No score scale (the callers fold it into q). */
+void or_attn_dec(const float *Q, const uint16_t *KC, const uint16_t *VC, float *O, uint32_t D, uint32_t nh, uint32_t nkv,
+                 uint32_t kvLen, uint32_t kStart, uint32_t kEnd, uint32_t ring) {
+  const uint32_t nchunk = (kEnd - kStart + 63) / 64, hpg = nh / nkv;
+  float *m = (float *)malloc(sizeof(float) * nchunk * nh), *l = (float *)malloc(sizeof(float) * nchunk * nh);
+  float *acc = (float *)calloc((size_t)nchunk * nh * D, sizeof(float));
+  float sc[64];
+  for (uint32_t c = 0; c < nchunk; c++) {
+    const uint32_t j0 = kStart + c * 64, nk = kEnd - j0 < 64 ? kEnd - j0 : 64;
+    for (uint32_t hh = 0; hh < nh; hh++) {
+      const uint32_t g = hh / hpg;
+      float mx = -3.0e38f;
+      for (uint32_t j = 0; j < nk; j++) {
+        const uint32_t row = ring ? (j0 + j) % ring : j0 + j;
+        const uint16_t *k = KC + ((size_t)g * kvLen + row) * D;
+        float s = 0.0f;
+        for (uint32_t d = 0; d < D; d += 4) {
+          float t = h2f32(k[d]) * Q[(size_t)hh * D + d];
+          for (uint32_t e = 1; e < 4; e++) t = t + h2f32(k[d + e]) * Q[(size_t)hh * D + d + e];
+          s = s + t;
+        }
+        sc[j] = s; mx = s > mx ? s : mx;
+      }
+      float ls = 0.0f;
+      for (uint32_t j = 0; j < nk; j++) { sc[j] = expf(sc[j] - mx); ls = ls + sc[j]; }
+      m[c * nh + hh] = mx; l[c * nh + hh] = ls;
+      float *a = acc + ((size_t)c * nh + hh) * D;
+      for (uint32_t j = 0; j < nk; j++) {
+        const uint32_t row = ring ? (j0 + j) % ring : j0 + j;
+        const uint16_t *v = VC + ((size_t)g * kvLen + row) * D;
+        for (uint32_t d = 0; d < D; d++) a[d] = a[d] + sc[j] * h2f32(v[d]);
+      }
+    }
+  }
+  for (uint32_t hh = 0; hh < nh; hh++) {
+    float M = -3.0e38f;
+    for (uint32_t c = 0; c < nchunk; c++) M = m[c * nh + hh] > M ? m[c * nh + hh] : M;
+    float L = 0.0f;
+    float *w = (float *)malloc(sizeof(float) * nchunk);
+    for (uint32_t c = 0; c < nchunk; c++) { w[c] = expf(m[c * nh + hh] - M); L = L + w[c] * l[c * nh + hh]; }
+    for (uint32_t c = 0; c < nchunk; c++) w[c] = w[c] / L;
+    for (uint32_t d = 0; d < D; d++) {
+      float o = 0.0f;
+      for (uint32_t c = 0; c < nchunk; c++) o = o + w[c] * acc[((size_t)c * nh + hh) * D + d];
+      O[(size_t)hh * D + d] = o;
+    }
+    free(w);
+  }
+  free(m); free(l); free(acc);
+}

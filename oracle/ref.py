@@ -63,6 +63,8 @@ def lib():
         L.or_embed.argtypes = [_i, _u32p, _u32p, _u32, _u32, _u32, ctypes.c_float, ctypes.c_float, _u32, _u32, _f32p, _f32p]
         L.or_normadd.argtypes = [_f32p, _u32, _u32, _f32p, _u32, _f32p, _f32p, _u32, _u32, _u32, _u32, ctypes.c_float, ctypes.c_float]
         L.or_dhead.argtypes = [_i, _f32p, _u32p, _f32p, _f32p, _u32p] + [_u32] * 6 + [_f32p]
+        L.or_qkrope.argtypes = [_f32p, _u32, _u32, _f32p, _f32p, _f32p, _u16p, _u16p, _u32, _u32, _u32, _i, _u32, ctypes.c_float] + [_u32] * 6
+        L.or_attn_dec.argtypes = [_f32p, _u16p, _u16p, _f32p] + [_u32] * 7
         L.or_gemm_red128.argtypes = [_i, _i, _f32p, _u32, _u32, _u16p, _f32p, _u32, _u16p, _f32p] + [_u32] * 6 + [ctypes.c_float]
         L.or_dot64.argtypes = [_f32p, _f64p, _i64, _i64, _i64, _f64p]
         L.or_gemv_cpu_mt.argtypes = [_f32p, _u32p, _f32p, _u32, _u32, _u32, _u32, _i]
@@ -368,3 +370,23 @@ def dhead(W, X, ST, NW, SEL, K, tPer, nsel, *, enc="q4g32a.t64", stat_off=0, nor
     lib().or_dhead(int(q8), _f32(X), _words(W), _f32(ST), _f32(NW), np.ascontiguousarray(SEL, np.uint32), stat_off, norm_off, K,
                    K // (64 if q8 else 32), tPer, nsel, MX)
     return MX
+
+
+def qkrope(S, nsrc, ldp, NW, RP, D, nq, *, nkv=1, hasKV=True, pos=0, eps=1e-6, qw=0, kw=0, npairs=None, rope_off=0, kv_row=0,
+           kv_len=0, Q=None, KC=None, VC=None):
+    """qkrope (lops.js:183-233): returns (Q f32 [nq][D], KC, VC fp16 bits [nkv][kv_len][D]); arrays updated in place when given"""
+    npairs = D // 2 if npairs is None else npairs
+    Q = np.zeros(nq * D, np.float32) if Q is None else Q
+    KC = np.zeros(max(1, nkv * kv_len * D), np.uint16) if KC is None else KC
+    VC = np.zeros(max(1, nkv * kv_len * D), np.uint16) if VC is None else VC
+    lib().or_qkrope(_f32(S), nsrc, ldp, _f32(NW), _f32(RP), Q, KC, VC, D, nq, nkv, int(bool(hasKV)), pos, float(eps), qw, kw, npairs,
+                    rope_off, kv_row, kv_len)
+    return Q, KC, VC
+
+
+def attn_dec(Q, KC, VC, D, nh, nkv, kv_len, k_start, k_end, ring=0):
+    """attnDec + combine (lops.js:236-321): O f32 [nh][D]"""
+    O = np.empty(nh * D, np.float32)
+    lib().or_attn_dec(_f32(Q), np.ascontiguousarray(KC, np.uint16), np.ascontiguousarray(VC, np.uint16), O, D, nh, nkv, kv_len,
+                      k_start, k_end, ring)
+    return O

@@ -24,7 +24,7 @@ P0_ROPE_INTER, P0_ROPE_HALF = 0, 1
 EXPORTS = ["p0_init", "p0_destroy", "p0_set_stream", "p0_set_overlap", "p0_last_error", "p0_stats", "p0_buffer", "p0_wrap", "p0_upload", "p0_read",
            "p0_free", "p0_done", "p0_device_ptr", "p0_gemv", "p0_gemvM", "p0_gemvM_noalloc", "p0_gemm", "p0_pack_q4", "p0_pack_q8",
            "p0_dequant_f16", "p0_version", "p0_argmaxM", "p0_embed", "p0_normadd", "p0_dhead",
-           "p0_upload_file"]
+           "p0_upload_file", "p0_qkrope", "p0_attn_dec"]
 P0_NOALLOC_SCRATCH_BYTES = 16 << 20   # include/p0mm.h
 P0_OVERLAP_WEIGHTS = 1
 P0_NOALLOC_COUNTER_BYTES = 64 << 10
@@ -82,6 +82,18 @@ class p0_dhead_args(ctypes.Structure):
                 ("sel", p0_buf), ("mx", p0_buf), ("K", _u32), ("tPer", _u32), ("nsel", _u32)]
 
 
+
+class p0_qkrope_args(ctypes.Structure):
+    _fields_ = [("s", p0_buf), ("s_n", _u32), ("s_ld", _u32), ("norm", p0_buf), ("qw", _u32), ("kw", _u32), ("rope", p0_buf),
+                ("rope_off", _u32), ("npairs", _u32), ("pos", _u32), ("q", p0_buf), ("kc", p0_buf), ("vc", p0_buf), ("D", _u32),
+                ("nq", _u32), ("nkv", _u32), ("hasKV", _u32), ("kvRow", _u32), ("kvLen", _u32), ("eps", ctypes.c_float)]
+
+
+class p0_attn_dec_args(ctypes.Structure):
+    _fields_ = [("q", p0_buf), ("kc", p0_buf), ("vc", p0_buf), ("part", p0_buf), ("out", p0_buf), ("D", _u32), ("nh", _u32),
+                ("nkv", _u32), ("kvLen", _u32), ("kStart", _u32), ("kEnd", _u32), ("ring", _u32)]
+
+
 _lib = None
 
 
@@ -115,6 +127,8 @@ def load():
     L.p0_pack_q8.argtypes = [vp, p0_buf, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, p0_buf, ctypes.c_uint64]
     L.p0_dequant_f16.argtypes = [vp, ctypes.POINTER(p0_wview), p0_buf]
     L.p0_upload_file.argtypes = [vp, p0_buf, ctypes.c_uint64, ctypes.c_char_p, ctypes.c_uint64, ctypes.c_uint64]
+    L.p0_qkrope.argtypes = [vp, ctypes.POINTER(p0_qkrope_args)]
+    L.p0_attn_dec.argtypes = [vp, ctypes.POINTER(p0_attn_dec_args)]
     L.p0_argmaxM.argtypes = [vp, p0_buf, ctypes.c_uint32, ctypes.c_uint32, p0_buf]
     L.p0_embed.argtypes = [vp, ctypes.POINTER(p0_embed_args)]
     L.p0_normadd.argtypes = [vp, ctypes.POINTER(p0_normadd_args)]

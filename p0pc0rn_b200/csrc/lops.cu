@@ -1,8 +1,9 @@
 // lops.cu -- the decode-path operators on either side of the GEMV: the token embedding gather (embed, engine/llm/
 // lops.js:323-365), the residual add + RMS statistics (normadd, lops.js:143-180), the argmax over the head's per-tile
 // maxima (argmax / argmaxM, lops.js:416-436, lops_spec.js:326-348) and the drafter's head over selected clusters
-// (dhead, lops_spec.js:428-482). All are small, latency-bound kernels: one CTA per output row (or tile), coalesced
-// loads, warp-shuffle reductions, no global scratch.
+// (dhead, lops_spec.js:428-482), the decode step's q/k norm + RoPE + KV-cache write (qkrope, lops.js:183-233) and
+// its split-key attention (attnDec + combine, lops.js:236-321). Small kernels: one CTA per output row, tile, head or
+// key chunk, coalesced loads, warp-shuffle reductions; only attnDec uses scratch (the caller's `part` buffer).
 #include <cuda_fp16.h>
 
 #include "internal.h"
@@ -210,6 +211,181 @@ __global__ void __launch_bounds__(kT) dhead_kernel(const float *__restrict__ X, 
   }
 }
 
+
+// ---------------------------------------------------------------- qkrope (decode): one CTA per head of [q | k | v]
+// the head's row = the sum of the split partials (in order), kept in shared memory; rs = rsqrt(mean square + eps);
+// v heads -> f16(x * rs) into the value cache row; q / k heads: RMS-normed with their weights, rotate-half RoPE on the
+// first npairs pairs (d, d + D/2), q -> f32 Q, k -> f16 key cache row (head-major [nkv][kvLen][D])
+__global__ void __launch_bounds__(kT) qkrope_kernel(const float *__restrict__ S, uint32_t nsrc, uint64_t ldp, const float *__restrict__ NW,
+                                                    const float *__restrict__ RP, float *__restrict__ Q, __half *__restrict__ KC,
+                                                    __half *__restrict__ VC, uint32_t D, uint32_t nq, uint32_t nkv, uint32_t pos, float eps,
+                                                    uint32_t qwOff, uint32_t kwOff, uint32_t npairs, uint32_t ropeOff, uint32_t kvRow,
+                                                    uint32_t kvLen) {
+  extern __shared__ float hv[];
+  __shared__ float red[kT / 32];
+  const uint32_t h = blockIdx.x, half = D / 2;
+  const size_t base = (size_t)h * D;
+  float s = 0.0f;
+  for (uint32_t i = threadIdx.x; i < D; i += kT) {
+    float v = 0.0f;
+    for (uint32_t j = 0; j < nsrc; j++) v = __fadd_rn(v, S[j * ldp + base + i]);
+    hv[i] = v;
+    s = fmaf(v, v, s);
+  }
+  const float rs = rsqrtf(__fadd_rn(__fdiv_rn(cta_sum(s, red), (float)D), eps));
+  const bool isV = h >= nq + nkv;
+  const uint32_t kvh = isV ? h - nq - nkv : h - nq;
+  const size_t cb = ((size_t)kvh * kvLen + kvRow) * D;
+  if (isV) {
+    for (uint32_t i = threadIdx.x; i < D; i += kT) VC[cb + i] = __float2half_rn(__fmul_rn(hv[i], rs));
+    return;
+  }
+  const float *w = NW + (h >= nq ? kwOff : qwOff);
+  for (uint32_t d = threadIdx.x; d < half; d += kT) {
+    const float a = __fmul_rn(__fmul_rn(hv[d], rs), w[d]), b = __fmul_rn(__fmul_rn(hv[d + half], rs), w[d + half]);
+    float c = 1.0f, sn = 0.0f;
+    if (d < npairs) {
+      const size_t rb = ropeOff + ((size_t)pos * npairs + d) * 2;
+      c = RP[rb];
+      sn = RP[rb + 1];
+    }
+    const float lo = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn)), hi = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, sn));
+    if (h < nq) {
+      Q[base + d] = lo;
+      Q[base + d + half] = hi;
+    } else {
+      KC[cb + d] = __float2half_rn(lo);
+      KC[cb + d + half] = __float2half_rn(hi);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- attnDec (decode attention, split over 64-key chunks)
+// One CTA per chunk. Scores: warp w takes keys 8w..8w+7 of the chunk at once; a lane holds 4 dims in each 128-dim
+// step of those keys' rows (DV steps, coalesced 8-byte loads) and, per query head of the key's KV group, dots them
+// with q from shared memory (q is read once per 8 keys), then a butterfly gives each key's score. Per head: m = max,
+// p = exp(s - m), l = sum p. P.V: a thread owns a pair of dims, every query head's accumulator in registers, each V
+// row read once per CTA. The chunk writes [nh] m | [nh] l | [nh][D] acc to the scratch; the combine merges chunks.
+template <int DV>
+__global__ void __launch_bounds__(kT) attn_chunk_kernel(const float *__restrict__ Q, const __half *__restrict__ KC,
+                                                        const __half *__restrict__ VC, float *__restrict__ PT, uint32_t D, uint32_t nh,
+                                                        uint32_t nkv, uint32_t kvLen, uint32_t kStart, uint32_t kEnd, uint32_t ring) {
+  extern __shared__ float sm[];
+  float *qs = sm, *sc = sm + (size_t)nh * D;   // q [nh][D] | scores [nh][64]
+  __shared__ float mh[8];
+  const uint32_t c = blockIdx.x, j0 = kStart + c * 64u, nk = kEnd - j0 < 64u ? kEnd - j0 : 64u;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, hpg = nh / nkv;
+  for (uint32_t i = threadIdx.x; i < nh * D; i += kT) qs[i] = Q[i];
+  for (uint32_t i = threadIdx.x; i < nh * 64u; i += kT) sc[i] = -3.0e38f;
+  __syncthreads();
+  for (uint32_t g = 0; g < nkv; g++) {
+    float kf[8][DV * 4];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const uint32_t j = warp * 8u + i;
+      const uint32_t row = ring ? (j0 + j) % ring : j0 + j;
+      const __half *kr = KC + ((size_t)g * kvLen + (j < nk ? row : 0u)) * D;
+#pragma unroll
+      for (int v = 0; v < DV; v++) {
+        const uint2 u = j < nk ? *reinterpret_cast<const uint2 *>(kr + 128u * v + 4u * lane) : make_uint2(0u, 0u);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x)), b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+        kf[i][4 * v] = a.x; kf[i][4 * v + 1] = a.y; kf[i][4 * v + 2] = b.x; kf[i][4 * v + 3] = b.y;
+      }
+    }
+    for (uint32_t hh = g * hpg; hh < (g + 1) * hpg; hh++) {
+      float qv[DV * 4];
+#pragma unroll
+      for (int v = 0; v < DV; v++) {
+        const float4 q4 = *reinterpret_cast<const float4 *>(qs + (size_t)hh * D + 128u * v + 4u * lane);
+        qv[4 * v] = q4.x; qv[4 * v + 1] = q4.y; qv[4 * v + 2] = q4.z; qv[4 * v + 3] = q4.w;
+      }
+      float part[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        float t = 0.0f;
+#pragma unroll
+        for (int e = 0; e < DV * 4; e++) t = fmaf(kf[i][e], qv[e], t);
+        part[i] = t;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part[i] += __shfl_xor_sync(0xffffffffu, part[i], o);
+      if (lane < 8u && warp * 8u + lane < nk) {
+        float v = part[0];
+#pragma unroll
+        for (int i = 1; i < 8; i++) v = lane == (uint32_t)i ? part[i] : v;
+        sc[hh * 64u + warp * 8u + lane] = v;
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < nh) {
+    float m = -3.0e38f;
+    for (uint32_t k = 0; k < nk; k++) m = fmaxf(m, sc[threadIdx.x * 64u + k]);
+    mh[threadIdx.x] = m;
+  }
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < nh * 64u; i += kT) {
+    const uint32_t hh = i >> 6, k = i & 63u;
+    sc[i] = k < nk ? expf(sc[i] - mh[hh]) : 0.0f;
+  }
+  __syncthreads();
+  const size_t pb = (size_t)c * nh * (2u + D);
+  if (threadIdx.x < nh) {
+    float l = 0.0f;
+    for (uint32_t k = 0; k < nk; k++) l += sc[threadIdx.x * 64u + k];
+    PT[pb + threadIdx.x] = mh[threadIdx.x];
+    PT[pb + nh + threadIdx.x] = l;
+  }
+  for (uint32_t dp = threadIdx.x; dp < D / 2; dp += kT) {
+    float2 acc[8];
+#pragma unroll
+    for (int hh = 0; hh < 8; hh++) acc[hh] = make_float2(0.0f, 0.0f);
+    for (uint32_t k = 0; k < nk; k++) {
+      const uint32_t row = ring ? (j0 + k) % ring : j0 + k;
+      for (uint32_t g = 0; g < nkv; g++) {
+        const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(VC + ((size_t)g * kvLen + row) * D + 2u * dp));
+#pragma unroll
+        for (int hh = 0; hh < 8; hh++)
+          if ((uint32_t)hh >= g * hpg && (uint32_t)hh < (g + 1) * hpg) {
+            const float p = sc[hh * 64u + k];
+            acc[hh].x = fmaf(p, v.x, acc[hh].x);
+            acc[hh].y = fmaf(p, v.y, acc[hh].y);
+          }
+      }
+    }
+#pragma unroll
+    for (int hh = 0; hh < 8; hh++)
+      if ((uint32_t)hh < nh) *reinterpret_cast<float2 *>(PT + pb + 2u * nh + (size_t)hh * D + 2u * dp) = acc[hh];
+  }
+}
+
+// the chunks' merge, one CTA per head: M = max m_c, w_c = exp(m_c - M) / sum_c exp(m_c - M) l_c, O = sum_c w_c acc_c
+__global__ void __launch_bounds__(kT) attn_combine_kernel(const float *__restrict__ PT, float *__restrict__ O, uint32_t D, uint32_t nh,
+                                                          uint32_t nchunk) {
+  __shared__ float wts[256];
+  const uint32_t h = blockIdx.x;
+  const size_t st = (size_t)nh * (2u + D);
+  if (threadIdx.x == 0) {
+    float M = -3.0e38f;
+    for (uint32_t c = 0; c < nchunk; c++) M = fmaxf(M, PT[c * st + h]);
+    float L = 0.0f;
+    for (uint32_t c = 0; c < nchunk; c++) {
+      const float e = expf(PT[c * st + h] - M);
+      wts[c] = e;
+      L = fmaf(e, PT[c * st + nh + h], L);
+    }
+    for (uint32_t c = 0; c < nchunk; c++) wts[c] = __fdiv_rn(wts[c], L);
+  }
+  __syncthreads();
+  for (uint32_t d = threadIdx.x; d < D; d += kT) {
+    float o = 0.0f;
+    for (uint32_t c = 0; c < nchunk; c++) o = fmaf(wts[c], PT[c * st + 2u * nh + (size_t)h * D + d], o);
+    O[(size_t)h * D + d] = o;
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -305,6 +481,70 @@ p0_status p0_dhead(p0_ctx *c, const p0_dhead_args *a) {
     dhead_kernel<false><<<nblk, kT, 0, c->stream>>>((const float *)rx.base, rw.base, a->w.rows / 64, stp, nw, (const uint32_t *)rsel.base, K,
                                                      wG, a->tPer, (float *)rm.base);
   return p0_launched(c, "dhead");
+}
+
+p0_status p0_qkrope(p0_ctx *c, const p0_qkrope_args *a) {
+  if (!c || !a) return P0_EINVAL;
+  const uint32_t D = a->D, nq = a->nq, nkv = a->nkv ? a->nkv : 1, nsrc = a->s_n ? a->s_n : 1;
+  const uint32_t nh = nq + (a->hasKV ? 2 * nkv : 0);
+  if (!nh || !D) return P0_OK;
+  if (D % 2 || (size_t)D * 4 > 200u * 1024u) return p0_fail(c, P0_EINVAL, "qkrope: D %u must be even and at most 51200", D);
+  if (a->npairs > D / 2) return p0_fail(c, P0_EINVAL, "qkrope: npairs %u > D/2", a->npairs);
+  P0Range rs, rn, rr, rq, rk, rv;
+  p0_status st;
+  const uint64_t ldp = a->s_ld ? a->s_ld : (uint64_t)nh * D;
+  if ((st = p0_range(c, a->s, 0, ((uint64_t)(nsrc - 1) * ldp + (uint64_t)nh * D) * 4, "qkrope", "S", &rs))) return st;
+  const uint32_t wmax = (a->kw > a->qw ? a->kw : a->qw) + D;
+  if ((st = p0_range(c, a->norm, 0, (uint64_t)wmax * 4, "qkrope", "NW", &rn))) return st;
+  if ((st = p0_range(c, a->rope, 0, (a->npairs ? ((uint64_t)a->rope_off + ((uint64_t)a->pos + 1) * a->npairs * 2) : 1) * 4, "qkrope", "RP", &rr))) return st;
+  if ((st = p0_range(c, a->q, 0, (uint64_t)nq * D * 4, "qkrope", "Q", &rq))) return st;
+  if (a->hasKV) {
+    if (a->kvRow >= a->kvLen) return p0_fail(c, P0_EINVAL, "qkrope: kvRow %u outside the cache of %u rows", a->kvRow, a->kvLen);
+    if ((st = p0_range(c, a->kc, 0, (uint64_t)nkv * a->kvLen * D * 2, "qkrope", "KC", &rk))) return st;
+    if ((st = p0_range(c, a->vc, 0, (uint64_t)nkv * a->kvLen * D * 2, "qkrope", "VC", &rv))) return st;
+  }
+  const float eps = a->eps != 0.0f ? a->eps : 1e-6f;   // lops.js:230 `a.eps || 1e-6`
+  const size_t smem = (size_t)D * 4;
+  cudaSetDevice(c->device);
+  if (smem > 40u * 1024u) cudaFuncSetAttribute(qkrope_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  qkrope_kernel<<<nh, kT, smem, c->stream>>>((const float *)rs.base, nsrc, ldp, (const float *)rn.base, (const float *)rr.base, (float *)rq.base,
+                                             a->hasKV ? (__half *)rk.base : nullptr, a->hasKV ? (__half *)rv.base : nullptr, D, nq, nkv, a->pos,
+                                             eps, a->qw, a->kw, a->npairs, a->rope_off, a->kvRow, a->kvLen);
+  return p0_launched(c, "qkrope");
+}
+
+p0_status p0_attn_dec(p0_ctx *c, const p0_attn_dec_args *a) {
+  if (!c || !a) return P0_EINVAL;
+  const uint32_t D = a->D, nh = a->nh, nkv = a->nkv ? a->nkv : 1;
+  if (a->kEnd <= a->kStart || !nh) return p0_fail(c, P0_EINVAL, "attnDec: no keys (kStart %u, kEnd %u) or heads", a->kStart, a->kEnd);
+  const uint32_t nchunk = (a->kEnd - a->kStart + 63u) / 64u;
+  if (nchunk > 256) return p0_fail(c, P0_EINVAL, "attnDec: context too long for one combine (%u chunks)", nchunk);
+  if (nh > 8 || nh % nkv) return p0_fail(c, P0_EINVAL, "attnDec: %u query heads over %u KV heads (at most 8, a multiple)", nh, nkv);
+  if (D % 128 || D > 512) return p0_fail(c, P0_EINVAL, "attnDec: D %u must be a multiple of 128, at most 512", D);
+  const uint32_t rows = a->kvLen;
+  if (a->ring ? a->ring > rows : a->kEnd > rows) return p0_fail(c, P0_EINVAL, "attnDec: keys beyond the cache of %u rows", rows);
+  P0Range rq, rk, rv, rp, ro;
+  p0_status st;
+  if ((st = p0_range(c, a->q, 0, (uint64_t)nh * D * 4, "attnDec", "Q", &rq))) return st;
+  if ((st = p0_range(c, a->kc, 0, (uint64_t)nkv * rows * D * 2, "attnDec", "KC", &rk))) return st;
+  if ((st = p0_range(c, a->vc, 0, (uint64_t)nkv * rows * D * 2, "attnDec", "VC", &rv))) return st;
+  if ((st = p0_range(c, a->part, 0, (uint64_t)nchunk * nh * (2 + D) * 4, "attnDec", "part", &rp))) return st;
+  if ((st = p0_range(c, a->out, 0, (uint64_t)nh * D * 4, "attnDec", "O", &ro))) return st;
+  const size_t smem = ((size_t)nh * D + (size_t)nh * 64) * 4;
+  cudaSetDevice(c->device);
+  auto go = [&](auto kern) {
+    kern<<<nchunk, kT, smem, c->stream>>>((const float *)rq.base, (const __half *)rk.base, (const __half *)rv.base, (float *)rp.base, D, nh, nkv,
+                                          rows, a->kStart, a->kEnd, a->ring);
+  };
+  switch (D / 128) {
+    case 1: go(attn_chunk_kernel<1>); break;
+    case 2: go(attn_chunk_kernel<2>); break;
+    case 3: go(attn_chunk_kernel<3>); break;
+    default: go(attn_chunk_kernel<4>); break;
+  }
+  if ((st = p0_launched(c, "attnDec"))) return st;
+  attn_combine_kernel<<<nh, kT, 0, c->stream>>>((const float *)rp.base, (float *)ro.base, D, nh, nchunk);
+  return p0_launched(c, "attnDec combine");
 }
 
 }  // extern "C"

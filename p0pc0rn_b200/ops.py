@@ -188,3 +188,24 @@ def dhead(g, a):
                            handle(norm["buf"]), int(norm.get("off") or 0), handle(a["sel"]["buf"]), handle(a["mx"]["buf"]),
                            int(a["K"]), int(a["tPer"]), int(a["nsel"]))
     g._check(g._lib.p0_dhead(g.ctx, ctypes.byref(args)))
+
+
+def qkrope(g, a):
+    """qkrope(g, a) (lops.js:226-233): a = {s: {buf, n, ld}, norm: {buf}, rope: {buf, off}, q: {buf}, kc: {buf}, vc: {buf},
+    D, nq, hasKV, pos, eps, qw, kw, npairs, kvRow, nkv, kvLen}; q f32 out, k / v into the fp16 caches at kvRow"""
+    s, rope = a["s"], a["rope"]
+    kc, vc = a.get("kc"), a.get("vc")
+    args = L.p0_qkrope_args(handle(s["buf"]), int(s.get("n") or 1), int(s.get("ld") or 0), handle(a["norm"]["buf"]), int(a.get("qw") or 0),
+                            int(a.get("kw") or 0), handle(rope["buf"]), int(rope.get("off") or 0), int(a["npairs"]), int(a.get("pos") or 0),
+                            handle(a["q"]["buf"]), _b(kc), _b(vc), int(a["D"]), int(a["nq"]), int(a.get("nkv") or 1),
+                            int(bool(a.get("hasKV"))), int(a.get("kvRow") or 0), int(a.get("kvLen") or 0), float(a.get("eps") or 0.0))
+    g._check(g._lib.p0_qkrope(g.ctx, ctypes.byref(args)))
+
+
+def attnDec(g, a):
+    """attnDec(g, a) (lops.js:306-321): a = {q: {buf}, kc: {buf}, vc: {buf}, part: {buf}, out: {buf}, D, nh, kStart, kEnd,
+    ring, nkv, kvLen}; out f32 [nh][D] = softmax(q . k) . v over the keys (a tuner's `ad` choice is not used)"""
+    args = L.p0_attn_dec_args(handle(a["q"]["buf"]), handle(a["kc"]["buf"]), handle(a["vc"]["buf"]), handle(a["part"]["buf"]),
+                              handle(a["out"]["buf"]), int(a["D"]), int(a["nh"]), int(a.get("nkv") or 1), int(a.get("kvLen") or 0),
+                              int(a["kStart"]), int(a["kEnd"]), int(a.get("ring") or 0))
+    g._check(g._lib.p0_attn_dec(g.ctx, ctypes.byref(args)))

@@ -43,6 +43,8 @@ STRUCTS = {
     "p0_embed_args": L.p0_embed_args,
     "p0_normadd_args": L.p0_normadd_args,
     "p0_dhead_args": L.p0_dhead_args,
+    "p0_qkrope_args": L.p0_qkrope_args,
+    "p0_attn_dec_args": L.p0_attn_dec_args,
 }
 
 

@@ -370,3 +370,45 @@ def test_dhead_oracle(enc, K):
         r = int(np.argmax(dots))
         assert MX[2 * wt + 1].view(np.uint32) == tile * 64 + r
         assert abs(MX[2 * wt] - dots[r]) <= 1e-4 * max(1.0, abs(dots[r]))
+
+
+def test_qkrope_oracle():
+    D, nq, nkv, kv_len, row, pos, npairs = 256, 4, 2, 10, 7, 3, 32
+    nh = nq + 2 * nkv
+    S = ref.randn(2 * nh * D, 60, 1.0)
+    NW = ref.randn(2 * D + 4, 61, 0.2) + 1
+    ang = ref.randn(8 * npairs, 62, 2.0).astype(np.float64)
+    RP = np.empty(5 + 16 * npairs, np.float32)
+    RP[5:5 + 16 * npairs:2], RP[6:5 + 16 * npairs:2] = np.cos(ang), np.sin(ang)
+    Q, KC, VC = ref.qkrope(S, 2, nh * D, NW, RP, D, nq, nkv=nkv, pos=pos, qw=4, kw=4 + D, npairs=npairs, rope_off=5, kv_row=row,
+                           kv_len=kv_len)
+    x = S.astype(np.float64).reshape(2, nh, D).sum(0)
+    rs = 1 / np.sqrt((x ** 2).mean(1, keepdims=True) + 1e-6)
+    cs, sn = np.ones(D // 2), np.zeros(D // 2)
+    cs[:npairs], sn[:npairs] = np.cos(ang[pos * npairs:(pos + 1) * npairs]), np.sin(ang[pos * npairs:(pos + 1) * npairs])
+    for h in range(nh):
+        if h >= nq + nkv:
+            want = x[h] * rs[h]
+            got = ref.h2f(VC.reshape(nkv, kv_len, D)[h - nq - nkv, row])
+        else:
+            w = NW[4:4 + D] if h < nq else NW[4 + D:4 + 2 * D]
+            v = x[h] * rs[h] * w
+            a, b = v[:D // 2], v[D // 2:]
+            want = np.concatenate([a * cs - b * sn, b * cs + a * sn])
+            got = Q.reshape(nq, D)[h] if h < nq else ref.h2f(KC.reshape(nkv, kv_len, D)[h - nq, row])
+        assert np.max(np.abs(got - want)) <= (1e-5 if h < nq else 2e-3) * max(1.0, np.abs(want).max())
+
+
+@pytest.mark.parametrize("D,nh,nkv,k0,k1,ring", [(256, 8, 2, 5, 290, 0), (512, 8, 1, 0, 64, 0), (128, 4, 4, 30, 200, 100)])
+def test_attn_dec_oracle(D, nh, nkv, k0, k1, ring):
+    L = 300
+    Q = ref.randn(nh * D, 70, 0.08)
+    KC, VC = ref.f2h(ref.round_f16(ref.randn(nkv * L * D, 71))), ref.f2h(ref.round_f16(ref.randn(nkv * L * D, 72)))
+    O = ref.attn_dec(Q, KC, VC, D, nh, nkv, L, k0, k1, ring)
+    K, V, q = ref.h2f(KC).reshape(nkv, L, D), ref.h2f(VC).reshape(nkv, L, D), Q.reshape(nh, D).astype(np.float64)
+    rows = np.array([j % ring if ring else j for j in range(k0, k1)])
+    for h in range(nh):
+        g = h // (nh // nkv)
+        s = K[g, rows] @ q[h]
+        p = np.exp(s - s.max())
+        assert np.max(np.abs(O[h * D:(h + 1) * D] - (p / p.sum()) @ V[g, rows])) <= 1e-5
