@@ -206,6 +206,6 @@ p0_status p0_device_ptr(p0_ctx *c, p0_buf b, uint64_t *out) {
   return P0_OK;
 }
 
-const char *p0_version(void) { return "p0mm sm_100a gemv-v4 gemm-tc-v1"; }
+const char *p0_version(void) { return "p0mm sm_100a gemv-v5 gemm-tc-v2 lops-v1 io-v1"; }
 
 }  // extern "C"
