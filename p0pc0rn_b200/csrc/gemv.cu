@@ -596,9 +596,14 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
     v4ok = pick == 4 && v4fit;
     v5ok = pick == 5 && v5fit;
   } else {
+    // measured on B200 (graph-free back-to-back calls, weights beyond L2), including the column-split head shapes of
+    // 2 / 4 / 8 ranks (2048 / 1024 / 512 tiles at K = 2048): at M >= 2 the cluster kernel loses once its units pass two
+    // per SM (1024 tiles, M = 4: 68.9 us against v2's 41.2), and from 2048 tiles on the stream-K kernel is the fastest
+    // at every M (M = 1: 51.5 us against 90.7)
+    const uint32_t ntile_all = N / 64;
     v3ok = v3fit;
-    v5ok = !v3ok && v5fit;
-    v4ok = !v3ok && !v5ok && v4fit && M >= 5 && epi != P0_EPI_GEGLU && pl.R >= 8192u;
+    v5ok = !v3ok && v5fit && (M == 1 || p.q8 || p5.units <= 2u * (uint32_t)c->sm_count);
+    v4ok = !v3ok && !v5ok && v4fit && epi != P0_EPI_GEGLU && ((M >= 5 && pl.R >= 8192u) || ntile_all >= 2048u);
   }
   if (v5ok) {
     e = launch_v5(p, p5, c->stream);
