@@ -158,7 +158,8 @@ enum { P0_GEPI_F16 = 0, P0_GEPI_F32 = 1, P0_GEPI_BIAS = 2, P0_GEPI_RESADD = 3, P
 enum { P0_ACT_SILU = 0, P0_ACT_GELU = 1 };
 
 /* gemm(gpu, a) -> flops (engine/ops/gemm.js:255-322): Y[m, n] = sum_k X[m, k] * W[n, k], W dequantised in-kernel
- * to fp16 (q4: f16(q*s + mn), gemm.js:147-148), fp32 accumulation on the tensor cores. x prologue 'f16'.
+ * to fp16 (q4: f16(q*s + mn), gemm.js:147-148; q8: f16(q*s); f16 weights as they are, rows of w.ld halves, ld % 8 and
+ * wk0 % 8 for 16-byte row reads), fp32 accumulation on the tensor cores.
  * Fields mirror `a`: w; x {buf, off (bytes), ld (halves, 0 = K), k0}; M, N, K; wr0, wr1, wk0; epi; act;
  * y {buf, off (bytes), ld (0 = N), n0}; ev {buf, off (floats)} (bias vector for 'bias', gate for 'resadd');
  * bv {buf, off (floats), up} (resadd / swiglu bias); res; store.

@@ -48,10 +48,15 @@ struct GemmCfg {
 using Cfg1 = GemmCfg<16, 5, 256, 1>;
 using Cfg2 = GemmCfg<8, 4, 128, 2>;
 using Cfg3 = GemmCfg<16, 6, 256, 1>;   // Cfg1 with a sixth stage (223 KB of shared memory, 448 TMEM columns)
+using CfgH = GemmCfg<16, 4, 256, 1>;   // fp16 weights: 16 KB of weights per stage, so four stages fit
 constexpr int kDqPerStage = 8;  // dequant warps that fill one stage
 // weights of a stage: q4 2 row tiles x 2 groups of 1280 B; q8 2 row tiles x 1 group of 4224 B (= the gathered layout's
 // 128 rows x 2 halves x 32 code bytes + 128 scales x 2 B + 256 B)
-template <bool Q8> __host__ __device__ constexpr uint32_t w_stage() { return Q8 ? 2u * 4224u : 2u * 2u * 1280u; }
+// weight encodings of the kernel instances: q4g32a.t64, q8g64s.t64, fp16 row-major
+enum { kWQ4 = 0, kWQ8 = 1, kWF16 = 2 };
+// fp16: 128 rows x 64 k x 2 bytes, laid out [k half][16-byte chunk][row] so that a warp's rows are consecutive
+template <int WE> __host__ __device__ constexpr uint32_t w_stage_e() { return WE == kWQ8 ? 2u * 4224u : WE == kWF16 ? 16384u : 2u * 2u * 1280u; }
+template <bool Q8> __host__ __device__ constexpr uint32_t w_stage() { return w_stage_e<Q8 ? kWQ8 : kWQ4>(); }
 constexpr uint32_t kWStage = w_stage<false>();
 
 struct GemmParams {
@@ -274,10 +279,11 @@ __device__ __forceinline__ void store_red128(const GemmParams &p, const float *s
   }
 }
 
-template <class C, bool Q8>
+template <class C, int WE>
 __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const __grid_constant__ CUtensorMap tmx, const GemmParams p) {
+  constexpr bool Q8 = WE == kWQ8, F16 = WE == kWF16;
   constexpr int kStages = C::kStages, kDqWarps = C::kDqWarps;
-  constexpr uint32_t kWStage = w_stage<Q8>();
+  constexpr uint32_t kWStage = w_stage_e<WE>();
   constexpr uint32_t kAcol = C::kAcol, kTmemCols = C::kTmemCols;
   constexpr size_t kXStage = C::kXStage, kRingBytes = C::kRingBytes;
   static_assert((size_t)C::kMaxBT * 128 * 4 <= C::kRingBytes, "the epilogue stages [BT][128] f32 in the X ring");
@@ -330,7 +336,22 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
       if (!__shfl_sync(0xffffffffu, (int)got, 0)) break;
       uint8_t *ws = wring + (size_t)slot * kWStage;
       const uint32_t ng = min(2u, (p.K - s * kBK) / 32u);   // groups in this stage (the last may hold one)
-      if (p.wtma && Q8) {
+      if (F16) {
+        // fp16 rows (any row mapping): each lane copies 4 rows' 64-byte halves as 16-byte chunks into [h][chunk][row]
+        for (uint32_t i = 0; i < 4; i++) {
+          const uint32_t nl = i * 32u + lane, row = weight_row(p, nB, nl);
+          const uint8_t *src = p.W + ((size_t)row * p.wG + p.wk0 + s * kBK) * 2u;
+          for (uint32_t h = 0; h < ng; h++)
+#pragma unroll
+            for (uint32_t j = 0; j < 4; j++)
+              *reinterpret_cast<uint4 *>(ws + ((h * 4u + j) * 128u + nl) * 16u) = ldg_w(src + h * 64u + j * 16u);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_expect_tx(&full[slot], xbytes);
+          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), (int32_t)m0);
+        }
+      } else if (p.wtma && Q8) {
         if (lane == 0) {   // one q8 record of each row tile: the stage's 64 k
           tc::mbar_expect_tx(&full[slot], xbytes + 2u * 4224u);
           tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), (int32_t)m0);
@@ -411,8 +432,10 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
     const uint32_t nl = q * 32u + lane;               // this thread's TMEM lane = weight row of the tile
     const uint32_t tq = tmem + ((q * 32u) << 16);
     // where this thread's 16 code bytes and (s, mn) word sit in a weight stage
-    uint32_t code_off, tail_off;
-    if (Q8) {
+    uint32_t code_off = 0, tail_off = 0;
+    if (F16) {
+      code_off = (h * 4u * 128u + nl) * 16u;   // chunk j of this row's half at code_off + j * 2048
+    } else if (Q8) {
       if (p.wtma) {
         const uint32_t ts = p.epi == P0_GEPI_SWIGLU ? (nl & 1u) : (nl >> 6), r = p.epi == P0_GEPI_SWIGLU ? (nl >> 1) : (nl & 63u);
         code_off = ts * 4224u + r * 64u + h * 32u;
@@ -437,7 +460,13 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
       uint32_t r[16];
       if (s * kBK + h * 32u < p.K) {
         const uint8_t *ws = wring + (size_t)slot * kWStage;
-        if (Q8)
+        if (F16) {
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(ws + code_off + j * 2048u);
+            r[4 * j] = v.x; r[4 * j + 1] = v.y; r[4 * j + 2] = v.z; r[4 * j + 3] = v.w;
+          }
+        } else if (Q8)
           deq_row16_q8(*reinterpret_cast<const uint4 *>(ws + code_off), *reinterpret_cast<const uint4 *>(ws + code_off + 16u),
                        *reinterpret_cast<const uint16_t *>(ws + tail_off), r);
         else
@@ -652,9 +681,8 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   const uint32_t enc = a->w.enc;
   if (enc != P0_ENC_Q4G32A_T64 && enc != P0_ENC_Q8G64S_T64 && enc != P0_ENC_F16)
     return p0_fail(c, P0_EINVAL, "gemm: unsupported weight encoding %u", enc);
-  if (enc == P0_ENC_F16) return p0_fail(c, P0_EINVAL, "gemm: weight encoding f16 is not built in this library yet");
-  const bool q8 = enc == P0_ENC_Q8G64S_T64;
-  const uint32_t GK = q8 ? 64u : 32u, RB = q8 ? 4224u : 1280u;
+  const bool q8 = enc == P0_ENC_Q8G64S_T64, f16w = enc == P0_ENC_F16;
+  const uint32_t GK = q8 ? 64u : f16w ? 1u : 32u, RB = q8 ? 4224u : 1280u;
   const uint32_t M = a->M, N = a->N, K = a->K;
   if (K % 32) return p0_fail(c, P0_EINVAL, "gemm: K must be a multiple of 32");
   if (a->epi > P0_GEPI_ONORMGATE) return p0_fail(c, P0_EINVAL, "gemm: epilogue %u is not built in this library yet", a->epi);
@@ -664,9 +692,13 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   if (a->w.rows == 0 || a->w.cols % GK || a->wk0 % GK || a->wk0 + K > a->w.cols)
     return p0_fail(c, P0_EINVAL, "gemm: weight view %ux%u does not cover k [%u, %u) in whole %u-k groups", a->w.rows, a->w.cols, a->wk0,
                    a->wk0 + K, GK);
-  if (a->w.rows % 64) return p0_fail(c, P0_EINVAL, "gemm: %s rows must be a multiple of 64", q8 ? "q8g64s.t64" : "q4g32a.t64");
+  if (!f16w && a->w.rows % 64) return p0_fail(c, P0_EINVAL, "gemm: %s rows must be a multiple of 64", q8 ? "q8g64s.t64" : "q4g32a.t64");
+  // fp16 weights: rows of w.ld halves (0 = cols, gemm.js:271 `a.w.ld || Ktot`), read as 16-byte chunks
+  const uint32_t wld = f16w ? (a->w.ld ? a->w.ld : a->w.cols) : 0u;
+  if (f16w && wld < a->w.cols) return p0_fail(c, P0_EINVAL, "gemm: f16 weight row stride %u < cols %u", wld, a->w.cols);
+  if (f16w && (wld % 8 || a->wk0 % 8)) return p0_fail(c, P0_EALIGN, "gemm: f16 weight rows must start on 16-byte boundaries (ld %% 8, wk0 %% 8)");
   if (N % 4) return p0_fail(c, P0_EALIGN, "gemm: N must be a multiple of 4 (the reference stores whole vec4s)");
-  const uint32_t ldx = a->x_ld ? a->x_ld : K, ldy = a->y_ld ? a->y_ld : N, wG = a->w.cols / GK;
+  const uint32_t ldx = a->x_ld ? a->x_ld : K, ldy = a->y_ld ? a->y_ld : N, wG = f16w ? wld : a->w.cols / GK;
   const bool swi = a->epi == P0_GEPI_SWIGLU, f32y = a->epi == P0_GEPI_F32 || a->epi == P0_GEPI_RESADD;
   const uint32_t es = f32y ? 4 : 2, ncols_out = swi ? N / 2 : N;
   const uint32_t xmode = a->x_mode;
@@ -677,7 +709,8 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   if (ldy % 4 || a->y_n0 % 4 || a->y_off % (4 * es)) return p0_fail(c, P0_EALIGN, "gemm: y must be vec4-aligned (ld %% 4, n0 %% 4, off)");
   p0_status st;
   P0Range rw, rx, ry, re, rb;
-  if ((st = p0_range(c, a->w.buf, a->w.off, (uint64_t)(a->w.rows / 64) * wG * RB, op, "W", &rw))) return st;
+  const uint64_t wbytes = f16w ? ((uint64_t)(a->w.rows - 1) * wG + a->w.cols) * 2 : (uint64_t)(a->w.rows / 64) * wG * RB;
+  if ((st = p0_range(c, a->w.buf, a->w.off, wbytes, op, "W", &rw))) return st;
   if ((uintptr_t)rw.base % 16) return p0_fail(c, P0_EALIGN, "gemm: weight offset must be 16-byte aligned");
   if ((st = p0_range(c, a->x, a->x_off, ((uint64_t)(M - 1) * ldx + a->x_k0 + K) * (xmode == P0_XPRO_F16 ? 2 : 4), op, "X", &rx)))
     return st;
@@ -757,22 +790,27 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   p.wtma = swi ? (a->wr0 % 64 == 0 && a->wr1 % 64 == 0 && (N / 2) % 64 == 0) : (a->wr0 % 64 == 0);
   cudaSetDevice(c->device);
   dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
-  if (q8) {   // q8 weights: Cfg1's shape
+  if (f16w) {   // fp16 weights: four stages
+    p.wtma = 0;
+    const size_t smem = CfgH::kRingBytes + (size_t)CfgH::kStages * w_stage_e<kWF16>() + 1024 + 256;
+    cudaFuncSetAttribute(gemm_q4_tc<CfgH, kWF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    gemm_q4_tc<CfgH, kWF16><<<grid, CfgH::kThreads, smem, c->stream>>>(tm, p);
+  } else if (q8) {   // q8 weights: Cfg1's shape
     const size_t smem = Cfg1::kRingBytes + (size_t)Cfg1::kStages * w_stage<true>() + 1024 + 256;
-    cudaFuncSetAttribute(gemm_q4_tc<Cfg1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    gemm_q4_tc<Cfg1, true><<<grid, Cfg1::kThreads, smem, c->stream>>>(tm, p);
+    cudaFuncSetAttribute(gemm_q4_tc<Cfg1, kWQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    gemm_q4_tc<Cfg1, kWQ8><<<grid, Cfg1::kThreads, smem, c->stream>>>(tm, p);
   } else if (cfg3) {
     const size_t smem = Cfg3::kRingBytes + (size_t)Cfg3::kStages * kWStage + 1024 + 256;
-    cudaFuncSetAttribute(gemm_q4_tc<Cfg3, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    gemm_q4_tc<Cfg3, false><<<grid, Cfg3::kThreads, smem, c->stream>>>(tm, p);
+    cudaFuncSetAttribute(gemm_q4_tc<Cfg3, kWQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    gemm_q4_tc<Cfg3, kWQ4><<<grid, Cfg3::kThreads, smem, c->stream>>>(tm, p);
   } else if (cfg2) {
     const size_t smem = Cfg2::kRingBytes + (size_t)Cfg2::kStages * kWStage + 1024 + 256;
-    cudaFuncSetAttribute(gemm_q4_tc<Cfg2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    gemm_q4_tc<Cfg2, false><<<grid, Cfg2::kThreads, smem, c->stream>>>(tm, p);
+    cudaFuncSetAttribute(gemm_q4_tc<Cfg2, kWQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    gemm_q4_tc<Cfg2, kWQ4><<<grid, Cfg2::kThreads, smem, c->stream>>>(tm, p);
   } else {
     const size_t smem = Cfg1::kRingBytes + (size_t)Cfg1::kStages * kWStage + 1024 + 256;
-    cudaFuncSetAttribute(gemm_q4_tc<Cfg1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    gemm_q4_tc<Cfg1, false><<<grid, Cfg1::kThreads, smem, c->stream>>>(tm, p);
+    cudaFuncSetAttribute(gemm_q4_tc<Cfg1, kWQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    gemm_q4_tc<Cfg1, kWQ4><<<grid, Cfg1::kThreads, smem, c->stream>>>(tm, p);
   }
   if ((st = p0_launched(c, "gemm"))) return st;
   if (flops) *flops = 2.0 * M * N * K;
