@@ -1,6 +1,6 @@
 """A second, independent transcription of the reference's JS helpers in plain Python (no C), used to pin the C oracle:
 rng / randn (engine/kcheck.js:10-11), f2h / h2f (engine/core/gpu.js:274-295), rhe (kcheck.js:14), packQ4
-(kcheck.js:22-38). JS numbers are f64; Float32Array stores round to f32 (struct pack 'f'); `>>` is JS's signed shift
+(kcheck.js:22-38), packQ8 (kcheck.js:40-53). JS numbers are f64; Float32Array stores round to f32 (struct pack 'f'); `>>` is JS's signed shift
 of the int32 view. Slow: small sizes only.
 """
 import math
@@ -127,4 +127,28 @@ def pack_q4(W, N, K):
                     deq[base + 2 * j + 1] = f32(q1 * s + mn)
                 word = (f2h(s) | (f2h(mn) << 16)) & 0xFFFFFFFF
                 out[rec + 1024 + r * 4: rec + 1028 + r * 4] = struct.pack("<I", word)
+    return bytes(out), deq
+
+
+def pack_q8(W, N, K):
+    NT, G = N // 64, K // 64
+    out = bytearray(NT * G * 4224)
+    deq = [0.0] * (N * K)
+    for t in range(NT):
+        for g in range(G):
+            rec = (t * G + g) * 4224
+            for r in range(64):
+                n = t * 64 + r
+                base = n * K + g * 64
+                am = 0.0
+                for i in range(64):
+                    am = max(am, abs(W[base + i]))
+                s = rf16(am / 127)
+                if s == 0:
+                    s = 1
+                for i in range(64):
+                    q = int(min(127, max(-128, rhe(W[base + i] / s))))
+                    out[rec + r * 64 + i] = q & 255
+                    deq[base + i] = f32(q * s)
+                out[rec + 4096 + r * 2: rec + 4098 + r * 2] = struct.pack("<H", f2h(s))
     return bytes(out), deq

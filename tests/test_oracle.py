@@ -412,3 +412,32 @@ def test_attn_dec_oracle(D, nh, nkv, k0, k1, ring):
         s = K[g, rows] @ q[h]
         p = np.exp(s - s.max())
         assert np.max(np.abs(O[h * D:(h + 1) * D] - (p / p.sum()) @ V[g, rows])) <= 1e-5
+
+
+# ---------------------------------------------------------------- q8g64s.t64 (kcheck.js:40-53) in the oracle
+def test_pack_q8_matches_transcription():
+    N, K = 64, 128
+    W = ref.randn(N * K, 80, 0.05)
+    W[:64] = 0.0                                                   # an all-zero group: s = 1
+    W[K:K + 64] = np.linspace(-1e-6, 1e-6, 64, dtype=np.float32)   # a subnormal fp16 scale
+    W[2 * K:2 * K + 64] = 0.5 * np.arange(64, dtype=np.float32) / 127.0   # ties for round-half-even
+    got, deq = ref.pack_q8(W, N, K)
+    want, wdeq = jsref.pack_q8([float(v) for v in W], N, K)
+    assert bytes(np.asarray(got, np.uint8)) == want
+    assert np.array_equal(np.asarray(deq, np.float32).ravel(), np.asarray(wdeq, np.float32))
+
+
+def test_q8_gemv_and_gemm_oracle_against_dequantised_weights():
+    # the q8 GEMV (f32 x, f32 accumulate) against an f64 dot with q*s; the q8 GEMM against f64 with f16(q*s) tiles
+    N, K, M = 128, 256, 3
+    W = ref.randn(N * K, 81, 0.05)
+    b, deq = ref.pack_q8(W, N, K)
+    deq = np.asarray(deq, np.float64).reshape(N, K)
+    x = ref.randn(K, 82).astype(np.float64)
+    y, _, _ = ref.gemv(b, x.astype(np.float32), N, K, enc="q8g64s.t64")
+    assert np.max(np.abs(y - deq @ x)) <= 1e-4 * max(1.0, np.abs(deq @ x).max())
+    X16 = ref.f2h(ref.round_f16(ref.randn(M * K, 83)))
+    Y = ref.h2f(ref.gemm(b, X16, M, N, K, enc="q8g64s.t64"))
+    w16 = ref.h2f(ref.deq16(b, N, K, enc="q8g64s.t64")).reshape(N, K)
+    want = ref.h2f(X16).reshape(M, K) @ w16.T
+    assert np.max(np.abs(Y.reshape(M, N) - want)) <= 2e-3 * max(1.0, np.abs(want).max())
