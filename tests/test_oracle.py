@@ -441,3 +441,32 @@ def test_q8_gemv_and_gemm_oracle_against_dequantised_weights():
     w16 = ref.h2f(ref.deq16(b, N, K, enc="q8g64s.t64")).reshape(N, K)
     want = ref.h2f(X16).reshape(M, K) @ w16.T
     assert np.max(np.abs(Y.reshape(M, N) - want)) <= 2e-3 * max(1.0, np.abs(want).max())
+
+
+# ---------------------------------------------------------------- the GEMM epilogues (gemm.js:187-211) on the accumulators
+def test_gemm_epilogues_oracle():
+    # every epilogue restated in numpy (f64, then the store's rounding) on the same f32 accumulators (the 'f32' store)
+    M, N, K = 5, 256, 128
+    b, _ = ref.pack_q4(ref.randn(N * K, 90, 0.05), N, K)
+    X = ref.f2h(ref.round_f16(ref.randn(M * K, 91)))
+    A = ref.gemm(b, X, M, N, K, epi="f32").reshape(M, N).astype(np.float64)
+    assert np.array_equal(ref.gemm(b, X, M, N, K), ref.f2h(A.astype(np.float32).astype(np.float64).ravel()))   # 'f16' = f16(acc)
+    bias = ref.randn(N, 92, 0.1).astype(np.float64)
+    y0 = ref.f2h(ref.round_f16(ref.randn(M * N, 93)))
+    got = ref.h2f(ref.gemm(b, X, M, N, K, epi="bias", ev=bias.astype(np.float32), res=True, Y=y0.copy())).reshape(M, N)
+    assert np.max(np.abs(got - (A + bias + ref.h2f(y0).reshape(M, N)))) <= 4e-3 * max(1.0, np.abs(got).max())
+    gate, cb = ref.randn(N, 94, 0.5).astype(np.float64), ref.randn(N, 95, 0.1).astype(np.float64)
+    r0 = ref.randn(M * N, 96)
+    got = ref.gemm(b, X, M, N, K, epi="resadd", ev=gate.astype(np.float32), bv=cb.astype(np.float32), Y=r0.copy()).reshape(M, N)
+    assert np.max(np.abs(got - (r0.reshape(M, N) + gate * (A + cb)))) <= 1e-5 * max(1.0, np.abs(got).max())
+    # swiglu: weight rows [gate 0..N/2) | up [N/2..N), interleaved (gate n, up n) in the accumulator columns
+    for act in ("silu", "gelu"):
+        got = ref.h2f(ref.gemm(b, X, M, N, K, epi="swiglu", act=act, wr0=0, wr1=N // 2, ldy=N // 2)).reshape(M, N // 2)
+        Ar = ref.gemm(b, X, M, N, K, epi="f32").reshape(M, N).astype(np.float64)   # plain rows 0..N-1
+        g_, u = Ar[:, :N // 2], Ar[:, N // 2:]
+        if act == "silu":
+            a = g_ / (1 + np.exp(-g_))
+        else:
+            a = g_ * 0.5 * (1 + np.tanh(np.clip(0.7978845608 * (g_ + 0.044715 * g_ ** 3), -15, 15)))
+        want = a * u
+        assert np.max(np.abs(got - want)) <= 4e-3 * max(1.0, np.abs(want).max())
