@@ -470,3 +470,13 @@ def test_gemm_epilogues_oracle():
             a = g_ * 0.5 * (1 + np.tanh(np.clip(0.7978845608 * (g_ + 0.044715 * g_ ** 3), -15, 15)))
         want = a * u
         assert np.max(np.abs(got - want)) <= 4e-3 * max(1.0, np.abs(want).max())
+
+
+def test_gemm_f16_weights_oracle():
+    # fp16 weights with a row stride wider than the columns and a k offset: the oracle reads W[row * ld + wk0 + k]
+    M, N, K, ld, wk0 = 4, 96, 128, 200, 40
+    W = ref.f2h(ref.round_f16(ref.randn(N * ld, 97, 0.05)))
+    X = ref.f2h(ref.round_f16(ref.randn(M * K, 98)))
+    got = ref.h2f(ref.gemm(W, X, M, N, K, enc="f16", rows=N, cols=ld, wk0=wk0)).reshape(M, N)
+    want = ref.h2f(X).reshape(M, K) @ ref.h2f(W).reshape(N, ld)[:, wk0:wk0 + K].T
+    assert np.max(np.abs(got - want)) <= 2e-3 * max(1.0, np.abs(want).max())
