@@ -480,3 +480,23 @@ def test_gemm_f16_weights_oracle():
     got = ref.h2f(ref.gemm(W, X, M, N, K, enc="f16", rows=N, cols=ld, wk0=wk0)).reshape(M, N)
     want = ref.h2f(X).reshape(M, K) @ ref.h2f(W).reshape(N, ld)[:, wk0:wk0 + K].T
     assert np.max(np.abs(got - want)) <= 2e-3 * max(1.0, np.abs(want).max())
+
+
+@pytest.mark.parametrize("mode", ["lnmod", "rms"])
+def test_gemm_xpro_oracle(mode):
+    # the f32 x prologues (gemm.js:55-63) against numpy in the WGSL's order of f32 operations, then fp16 rounding
+    M, K, ldx, kx0 = 6, 96, 130, 32
+    X = ref.randn(M * ldx, 99)
+    st = np.empty(2 * (M + 2), np.float32)
+    st[0::2], st[1::2] = ref.randn(M + 2, 100, 0.2), 0.5 + np.abs(ref.randn(M + 2, 101, 0.3))
+    pv = ref.randn(4 + 2 * 200, 102, 0.2)
+    got = ref.gemm_xpro(mode, X, M, K, ldx=ldx, kx0=kx0, stats=st, stat_off=2, pv=pv, pv_off=4, pv_stride=200)
+    x = X.reshape(M, ldx)[:, kx0:kx0 + K]
+    mean, rstd = st[4::2][:M, None], st[5::2][:M, None]
+    f = np.float32
+    if mode == "lnmod":
+        v = ((x - mean).astype(f) * rstd).astype(f) * (f(1) + pv[4 + kx0:4 + kx0 + K]).astype(f)
+        v = (v.astype(f) + pv[204 + kx0:204 + kx0 + K]).astype(f)
+    else:
+        v = ((x * rstd).astype(f) * pv[4 + kx0:4 + kx0 + K]).astype(f)
+    assert np.array_equal(got, ref.f2h(v.astype(np.float64).ravel()))
