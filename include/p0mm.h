@@ -142,12 +142,13 @@ p0_status p0_gemvM(p0_ctx *ctx, const p0_gemvM_args *a, uint32_t *nsplit);
  * latency budget that a device-wide wait would break, or a process whose device memory is all owned by another
  * allocator (for example a framework's caching allocator that has reserved the HBM). The scratch lives in a
  * file-scope device array of P0_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until the process
- * exits: P0_NOALLOC_COUNTER_BYTES of per-unit arrival counters (one u32 per 64-row tile x k-split), cleared on the
- * stream by each call, then the partial sums ((tiles x splits + warps of the grid) x halves x M x 64 floats, halves
- * = 2 for geglu). A call that needs more returns P0_EINVAL and says how much; so does a call the stream-K kernel does
+ * exits: P0_NOALLOC_COUNTER_BYTES of per-unit arrival counters (one u32 per 64-row tile x k-split; zero at load, and
+ * every call's kernel returns each counter it uses to zero before it exits, also when one of its waits gives up), then
+ * the partial sums ((tiles x splits + warps of the grid) x halves x M x 64 floats, halves = 2 for geglu). A call that needs more returns P0_EINVAL and says how much; so does a call the stream-K kernel does
  * not take (geglu with k-splits, weight columns < K, M*K > 16384, fewer than 16 weight records).
- * The first call on each device looks up the array's device address; make that first call before any stream
- * capture. Every call on a device shares the one array and keeps the last call's contents: calls whose kernels can
+ * The first call on each device looks up the array's device address and keeps it for the life of the process; make
+ * that first call before any stream capture, and do not reset the device (cudaDeviceReset) after it: a new primary
+ * context would leave the kept address stale. Every call on a device shares the one array and keeps the last call's contents: calls whose kernels can
  * overlap on the GPU (other streams, contexts or threads on the same device) race and give wrong results. */
 #define P0_NOALLOC_SCRATCH_BYTES (16u << 20)
 #define P0_NOALLOC_COUNTER_BYTES (64u << 10)
@@ -165,7 +166,10 @@ enum { P0_ACT_SILU = 0, P0_ACT_GELU = 1 };
  * bv {buf, off (floats), up} (resadd / swiglu bias); res; store.
  * post_gelu (bias epilogue only) applies engine/ops/misc.js ew op 'gelu' to the fp16 result in the same pass:
  * the pair gemm(epi:'bias') -> ew(op:'gelu') of pocketflux-engine.js:3052-3053 as one call.
- * acc: 0 = 'f32' (the only mode the tensor-core path computes; 'f16' partial sums are rejected).
+ * acc: 0 = 'f32', 1 = 'f16' (gemm.js:172-183: fp16 partial sums over each 32-k tile, folded into f32; the default of
+ * the DiT's calls, pocketflux-engine.js:4095). Both compute on the tensor cores with every product accumulated in f32:
+ * the 'f16' mode's results are the f32 ones, closer to the exact sum than the reference's fp16 partials (whose extra
+ * rounding error is up to about 2^-11 of each 32-term partial's magnitude).
  * The f32 x prologues run as a pass that writes the fp16 X into the context's workspace (M*K*2 bytes), then the GEMM. */
 typedef struct {
   p0_wview w;
@@ -285,6 +289,11 @@ p0_status p0_pack_q8(p0_ctx *ctx, p0_buf w, uint64_t w_off, uint32_t ldw, uint32
 /* writes the fp16 weight the GEMM tile holds for rows [0, rows) x k [0, cols) of a q4/q8 view, row-major,
  * into out_f16 (a buffer of rows*cols*2 bytes): the in-kernel dequantisation, dumped for bit-exact checks */
 p0_status p0_dequant_f16(p0_ctx *ctx, const p0_wview *w, p0_buf out_f16);
+/* failure-path check, no counterpart in the reference: enqueues one small kernel whose warp waits on an mbarrier
+ * phase that nothing completes, through the same bounded in-kernel wait as the matmul kernels, giving up after `polls`
+ * tries (1 .. 2^20). It records its code (0x7e1) in the context's error word and returns, so the next p0_done reports
+ * P0_ETIMEOUT (the reference's GpuError at done(), core/gpu.js:141-147) and the context stays usable. */
+p0_status p0_wait_selftest(p0_ctx *ctx, uint32_t polls);
 /* the library build tag (kernel versions), e.g. "p0mm sm_100a gemv-v1 gemm-tc-v1" */
 const char *p0_version(void);
 

@@ -6,6 +6,25 @@
 #include <thread>
 
 #include "internal.h"
+#include "tc.cuh"
+
+namespace {
+// One warp waits on an mbarrier phase that nothing completes (one expected arrival, none made), through the same
+// bounded wait the GEMV / GEMM kernels use for their copies. The wait gives up after `polls` tries, records `code`
+// in the context's error word and the kernel returns: the failure path of an in-kernel wait, with no fault.
+__global__ void wait_selftest_kernel(uint32_t *err, uint32_t polls, uint32_t code) {
+  __shared__ uint64_t bar;
+  __shared__ uint32_t abort_flag;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    abort_flag = 0u;
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  tc::mbar_wait(&bar, 0u, &abort_flag, err, code, polls);
+  __syncthreads();
+}
+}  // namespace
 
 p0_status p0_workspace(p0_ctx *c, size_t cnt_bytes, size_t scratch_bytes, uint32_t **cnt, void **scratch) {
   const size_t MB = (size_t)1 << 20;
@@ -204,6 +223,13 @@ p0_status p0_device_ptr(p0_ctx *c, p0_buf b, uint64_t *out) {
   if (!B) return p0_fail(c, P0_EINVAL, "device_ptr: not a live buffer");
   *out = (uint64_t)(uintptr_t)B->ptr;
   return P0_OK;
+}
+
+p0_status p0_wait_selftest(p0_ctx *c, uint32_t polls) {
+  if (!c) return P0_EINVAL;
+  if (polls == 0 || polls > (1u << 20)) return p0_fail(c, P0_EINVAL, "wait_selftest: polls must be in [1, 2^20]");
+  wait_selftest_kernel<<<1, 32, 0, c->stream>>>(c->d_err, polls, 0x7e1u);
+  return p0_launched(c, "wait_selftest");
 }
 
 const char *p0_version(void) { return "p0mm sm_100a gemv-v5 gemm-tc-v2 lops-v1 io-v1"; }

@@ -686,7 +686,9 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   const uint32_t M = a->M, N = a->N, K = a->K;
   if (K % 32) return p0_fail(c, P0_EINVAL, "gemm: K must be a multiple of 32");
   if (a->epi > P0_GEPI_ONORMGATE) return p0_fail(c, P0_EINVAL, "gemm: epilogue %u is not built in this library yet", a->epi);
-  if (a->acc != 0) return p0_fail(c, P0_EINVAL, "gemm: acc 'f16' (fp16 partial sums) is not built; the tensor cores accumulate in f32");
+  // acc 1 ('f16', the DiT's default, pocketflux-engine.js:4095) asks for fp16 partial sums per 32-k tile
+  // (gemm.js:172-183); the tensor cores accumulate every product in f32, which is at least as accurate, so both modes
+  // run the same kernel. Values other than 0 / 1 fall back to f32 like the reference's `c.acc === 'f16'` test.
   if (a->post_gelu && a->epi != P0_GEPI_BIAS) return p0_fail(c, P0_EINVAL, "gemm: post_gelu applies to the 'bias' epilogue only");
   if (!M || !N || !K) return P0_OK;
   if (a->w.rows == 0 || a->w.cols % GK || a->wk0 % GK || a->wk0 + K > a->w.cols)

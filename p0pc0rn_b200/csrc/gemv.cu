@@ -582,8 +582,9 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
     if ((st = p0_cuda(c, v4_noalloc_scratch(&fixed), op))) return st;
     pl.cnt = (uint32_t *)fixed;
     pl.part = (float *)(fixed + P0_NOALLOC_COUNTER_BYTES);
-    // the counters this call uses start at zero, whatever an earlier call left behind
-    if ((st = p0_cuda(c, cudaMemsetAsync(pl.cnt, 0, cnt_bytes, c->stream), op))) return st;
+    // No clearing pass: the counters start at zero (static device storage) and the kernel returns every counter it
+    // uses to zero before it exits, on its give-up path too (v4_arrive_only), so a call leaves them as it found them.
+    // A memset here would also sit between this launch and the kernel ahead and stop their programmatic overlap.
     if ((st = p0_cuda(c, launch_v4(p, pl, c->stream), op))) return st;
     return p0_launched(c, op);
   }

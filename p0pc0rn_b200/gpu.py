@@ -146,6 +146,11 @@ class Gpu:
         """wait for the device with a bound (gpu.js:141-147); raises P0Error(P0_ETIMEOUT) when it runs out"""
         self._check(self._lib.p0_done(self.ctx, int(timeout_ms)))
 
+    def wait_selftest(self, polls=4096):
+        """enqueue the failure-path check: a kernel whose bounded in-kernel wait runs out after `polls` tries and
+        records its code; the next done() raises P0Error(P0_ETIMEOUT) and the context stays usable"""
+        self._check(self._lib.p0_wait_selftest(self.ctx, int(polls)))
+
     def close(self):
         if self.ctx:
             self._lib.p0_destroy(self.ctx)

@@ -84,7 +84,8 @@ def _gemvM(g, a, entry):
 
 
 def gemm(gpu, a):
-    """gemm(gpu, a) -> flops (gemm.js:264-322). x prologues 'f16', 'lnmod', 'rms'; acc 'f32'; every epilogue of
+    """gemm(gpu, a) -> flops (gemm.js:264-322). x prologues 'f16', 'lnmod', 'rms'; acc 'f32' or 'f16' (both
+    accumulate in f32 on the tensor cores); every epilogue of
     gemm.js:187-250 ('f16', 'f32', 'bias', 'resadd', 'swiglu', 'heads', 'onormgate')."""
     x, y = a["x"], a["y"]
     ev, bv = a.get("ev"), a.get("bv")
@@ -99,7 +100,7 @@ def gemm(gpu, a):
     args = L.p0_gemm_args(
         _wview(a["w"], "gemm"), handle(x["buf"]), int(x.get("off") or 0), int(x.get("ld") or 0), int(x.get("k0") or 0), int(a["M"]),
         int(a["N"]), int(a["K"]), int(a.get("wr0") or 0), int(a.get("wr1") or 0), int(a.get("wk0") or 0), L.GEPI[epi],
-        L.ACT[a.get("act") or "silu"], 0 if acc == "f32" else 1, handle(y["buf"]), int(y.get("off") or 0), int(y.get("ld") or 0),
+        L.ACT[a.get("act") or "silu"], 1 if acc == "f16" else 0, handle(y["buf"]), int(y.get("off") or 0), int(y.get("ld") or 0),
         int(y.get("n0") or 0), _b(ev), int((ev or {}).get("off") or 0), _b(bv), int((bv or {}).get("off") or 0),
         int((bv or {}).get("up") or 0), int(bool(a.get("res"))), int(bool(a.get("store"))), int(bool(a.get("post_gelu"))),
         L.XPRO[xmode], _b(stats), int((stats or {}).get("off") or 0), _b(pv), int((pv or {}).get("off") or 0),
