@@ -59,11 +59,12 @@ class Clocks:
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
 
     def __init__(self, index):
-        self.index, self.proc, self.lines = index, None, []
+        self.index = ",".join(str(i) for i in index) if isinstance(index, (list, tuple)) else str(index)
+        self.proc, self.lines = None, []
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.index, "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
                                           "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=self._read, daemon=True).start()
             t0 = time.time()
@@ -129,54 +130,94 @@ def init_dist(ws, local):
 
 
 # ------------------------------------------------------------------------------------------ our arm
+def call_cost_us(M, N):
+    """rough device time of one GEMV call (a fixed ~3 us per call plus its bytes at 4 TB/s), for placing calls on ranks"""
+    return 3.0 + gemv_bytes(M, N, K, N == HEAD_N) / 4e6
+
+
+def plan_calls(ws):
+    """The 12 calls of a step and where they run. The vocabulary head (N = 262144) is column-split: every rank runs
+    its N/ws rows (whole 64-row tiles) at every M. The small calls (N = 2048, 16384) are independent units and each
+    runs whole on one rank: largest first, onto the rank with the least estimated time so far (ties: lowest rank).
+    Every rank computes the same plan."""
+    calls = [{"M": M, "Nfull": N, "head": N == HEAD_N, "j": j} for N in NS for j, M in enumerate(MS)]
+    load = [0.0] * ws
+    for c in calls:
+        if c["head"]:
+            c["rank"] = None
+            for r in range(ws):
+                load[r] += call_cost_us(c["M"], c["Nfull"] // ws)
+    for c in sorted((c for c in calls if not c["head"]), key=lambda c: -call_cost_us(c["M"], c["Nfull"])):
+        r = min(range(ws), key=lambda r: (load[r], r))
+        c["rank"] = r
+        load[r] += call_cost_us(c["M"], c["Nfull"])
+    return calls
+
+
+def ring_copies(wbytes):
+    """weight copies per matrix so that the copies together are at least 2x the L2 size"""
+    return max(1, -(-2 * L2_BYTES // wbytes))
+
+
+def ring_offset(j, copies):
+    """the copy the j-th M call of one matrix starts on: the four M calls of a step read four different copies"""
+    return j * (copies // 4) if copies >= 4 else j % copies
+
+
 class Sweep:
-    """the config-2 sweep on this rank: weight rings, inputs, outputs, one step = 12 calls"""
+    """the config-2 sweep's calls on this rank: weight rings, inputs, outputs (one step = every rank's calls once)"""
 
     def __init__(self, g, torch, ws, rank, seed=0):
         import p0pc0rn_b200 as p0
         self.p0, self.g, self.torch, self.ws, self.rank = p0, g, torch, ws, rank
         dev = torch.device("cuda", torch.cuda.current_device())
         gen = torch.Generator(device=dev)
-        self.calls = []
-        self.keep = []
+        plan = plan_calls(ws)
+        self.total_bytes = sum(gemv_bytes(c["M"], c["Nfull"], K, c["head"]) for c in plan)   # the whole job's step
+        # the graph count every rank uses: the longest ring of any rank (the same number of replays everywhere)
+        self.R = max(ring_copies((c["Nfull"] // ws if c["head"] else c["Nfull"]) * K * 5 // 8) for c in plan)
+        self.calls, rings = [], {}
         out_floats = 0
-        for N in NS:
-            Nr = N // ws                                     # this rank's rows (whole tiles)
-            head = N == HEAD_N
-            wbytes = Nr * K * 5 // 8
-            copies = 1 if wbytes * 1 >= 2 * L2_BYTES else max(2, -(-2 * L2_BYTES // wbytes))
-            ring = []
-            for c in range(copies):
-                gen.manual_seed(seed * 1000003 + N * 31 + c * 7 + rank)
-                wf = torch.randn(Nr, K, generator=gen, device=dev, dtype=torch.float32) * 0.02
-                wb = g.wrap(wf.data_ptr(), wf.numel() * 4, "wf32")
-                q = p0.pack_q4(g, wb, Nr, K)
-                g.done()
-                g.free(wb)
-                del wf
-                ring.append(q)
-            for M in MS:
-                rng = np.random.default_rng(seed + 17 * M + N)
-                x = rng.standard_normal(M * K).astype(np.float16).astype(np.float32)
-                xb = g.upload(x, "x")
-                NT = Nr // 64
-                c = {"M": M, "N": Nr, "Nfull": N, "head": head, "ring": ring, "i": 0, "x": x, "xb": xb,
-                     "bytes": gemv_bytes(M, Nr, K, head), "out_off": out_floats}
-                c["y"] = g.buffer(M * Nr * 4, "y")
-                if head:
-                    nw = (1.0 + 0.1 * rng.standard_normal(K)).astype(np.float32)
-                    c["nw"] = g.upload(nw, "nw")
-                    mx = np.zeros(M * NT * 2 + 8, np.float32)
-                    c["mxb"] = g.upload(mx, "mx")
-                    c["st"] = g.upload(np.full(8, 0.9, np.float32), "st")
-                    c["stat_off"] = M * NT * 2              # the rstd slot past the tile slots (gemma4.js:504)
-                    g.write(c["mxb"], np.full(1, 0.9, np.float32), dst_off=c["stat_off"] * 4)
-                    out_floats += M * NT * 2
-                else:
-                    out_floats += M * Nr
-                self.calls.append(c)
+        for pc in plan:
+            if not (pc["head"] or pc["rank"] == rank):
+                continue
+            N, M, head = pc["Nfull"], pc["M"], pc["head"]
+            Nr = N // ws if head else N                      # rows this rank runs (whole 64-row tiles)
+            if N not in rings:
+                wbytes = Nr * K * 5 // 8
+                ring = []
+                for c in range(ring_copies(wbytes)):
+                    gen.manual_seed(seed * 1000003 + N * 31 + c * 7 + (rank if head else 0))
+                    wf = torch.randn(Nr, K, generator=gen, device=dev, dtype=torch.float32) * 0.02
+                    wb = g.wrap(wf.data_ptr(), wf.numel() * 4, "wf32")
+                    q = p0.pack_q4(g, wb, Nr, K)
+                    g.done()
+                    g.free(wb)
+                    del wf
+                    ring.append(q)
+                rings[N] = ring
+            ring = rings[N]
+            rng = np.random.default_rng(seed + 17 * M + N)
+            x = rng.standard_normal(M * K).astype(np.float16).astype(np.float32)
+            xb = g.upload(x, "x")
+            NT = Nr // 64
+            c = {"M": M, "N": Nr, "Nfull": N, "head": head, "ring": ring, "i": ring_offset(pc["j"], len(ring)), "x": x, "xb": xb,
+                 "bytes": gemv_bytes(M, Nr, K, head), "out_off": out_floats}
+            c["y"] = g.buffer(M * Nr * 4, "y")
+            if head:
+                nw = (1.0 + 0.1 * rng.standard_normal(K)).astype(np.float32)
+                c["nw"] = g.upload(nw, "nw")
+                mx = np.zeros(M * NT * 2 + 8, np.float32)
+                c["mxb"] = g.upload(mx, "mx")
+                c["st"] = g.upload(np.full(8, 0.9, np.float32), "st")
+                c["stat_off"] = M * NT * 2              # the rstd slot past the tile slots (gemma4.js:504)
+                g.write(c["mxb"], np.full(1, 0.9, np.float32), dst_off=c["stat_off"] * 4)
+                out_floats += M * NT * 2
+            else:
+                out_floats += M * Nr
+            self.calls.append(c)
         self.out_floats = out_floats
-        self.step_bytes = sum(c["bytes"] for c in self.calls)
+        self.step_bytes = sum(c["bytes"] for c in self.calls)    # this rank's share
 
     def args(self, c):
         q = c["ring"][c["i"] % len(c["ring"])]
@@ -192,28 +233,13 @@ class Sweep:
             a["M"] = c["M"]
         return a
 
-    def launch(self, c, ev=None):
+    def launch(self, c):
         a = self.args(c)
-        if ev is not None:
-            ev[0].record()
         if c["M"] == 1:
             self.p0.gemv(self.g, a)
         else:
             self.p0.gemvM(self.g, a)
-        if ev is not None:
-            ev[1].record()
         c["i"] += 1
-
-    def step(self, head_events=None):
-        n = 0
-        for c in self.calls:
-            ev = None
-            if head_events is not None and c["head"]:
-                ev = (self.torch.cuda.Event(enable_timing=True), self.torch.cuda.Event(enable_timing=True))
-                head_events.append((c, ev))
-            self.launch(c, ev)
-            n += 1
-        return n
 
 
 def capture(torch, stream, fn):
@@ -222,6 +248,53 @@ def capture(torch, stream, fn):
     with torch.cuda.graph(gr, stream=stream, capture_error_mode="relaxed"):
         fn()
     return gr
+
+
+def time_graph_us(torch, gr, n):
+    """device time per launch of a graph of n launches: one untimed replay, then one timed by CUDA events"""
+    gr.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / n
+
+
+def run_config1(g, torch, stream):
+    """BASELINE config 1, one W4 GEMV layer: M = 1, N = 8192, K = 2048 (10,526,720 algorithmic bytes per call), raw /
+    store. A graph of 4 launches per ring copy, the copies together >= 2x L2, so every call reads its weights from HBM."""
+    import p0pc0rn_b200 as p0
+    N = 8192
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev)
+    ring = []
+    for c in range(ring_copies(N * K * 5 // 8)):
+        gen.manual_seed(8192 + c)
+        wf = torch.randn(N, K, generator=gen, device=dev) * 0.02
+        wb = g.wrap(wf.data_ptr(), wf.numel() * 4, "wf")
+        ring.append(p0.pack_q4(g, wb, N, K))
+        g.done()
+        g.free(wb)
+        del wf
+    xb = g.upload(np.random.default_rng(11).standard_normal(K).astype(np.float16).astype(np.float32), "x")
+    yb = g.buffer(N * 4, "y")
+    n = 4 * len(ring)
+
+    def body():
+        for i in range(n):
+            p0.gemv(g, {"w": {"buf": ring[i % len(ring)], "off": 0, "enc": "q4g32a.t64", "rows": N, "cols": K}, "x": {"buf": xb},
+                        "N": N, "K": K, "y": {"buf": yb}})
+    gr = capture(torch, stream, body)
+    us = min(time_graph_us(torch, gr, n) for _ in range(3))
+    del gr
+    for b in ring + [xb, yb]:
+        g.free(b)
+    hbm, _, _ = peaks()
+    byts = gemv_bytes(1, N, K, False)
+    return {"M": 1, "N": N, "K": K, "us_per_call": round(us, 2), "GB_s": round(byts / (us * 1e-6) / 1e9, 1),
+            "frac_of_hbm": round(byts / (us * 1e-6) / 1e9 / hbm, 4), "bytes_per_call": byts,
+            "launch": "graph of %d back-to-back calls over %d weight copies (%.0f MB > 2x L2)" % (n, len(ring), len(ring) * N * K * 0.625 / 1e6)}
 
 
 def run_ours(args, ws, rank, local):
@@ -238,9 +311,12 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize()
     # the weights are packed and synchronised: GEMVs may fetch them while the call ahead finishes (p0_set_overlap)
     g.set_overlap(True)
-    # one gather buffer: every call's outputs of this rank, concatenated; one all-gather per step
-    gather_src = torch.empty(sw.out_floats, dtype=torch.float32, device="cuda")
-    gather_dst = torch.empty(sw.out_floats * ws, dtype=torch.float32, device="cuda")
+    # one gather buffer per rank of equal size (ranks own different call sets): every call's outputs of this rank,
+    # concatenated; one all-gather per step
+    per_rank = max(sum((c["M"] * (c["Nfull"] // ws // 64) * 2) if c["head"] else c["M"] * c["Nfull"]
+                       for c in plan_calls(ws) if c["head"] or c["rank"] == r) for r in range(ws))
+    gather_src = torch.zeros(per_rank, dtype=torch.float32, device="cuda")
+    gather_dst = torch.empty(per_rank * ws, dtype=torch.float32, device="cuda")
     outs = []
     for c in sw.calls:
         buf = c["mxb"] if c["head"] else c["y"]
@@ -259,125 +335,130 @@ def run_ours(args, ws, rank, local):
         copies(ptrs)
         dist.all_gather_into_tensor(gather_dst, gather_src)
 
-    # eager warm-up (sizes the library's workspace before any capture), then the step as CUDA graphs: the 8 small-N calls
-    # as one graph per weight-ring position, each head call as its own graph (events between graph launches time the
-    # head inside the timed region), the gather copies as one graph; the NCCL all-gather stays eager
+    # eager warm-up (sizes the library's workspace and sets up NCCL before any capture)
     for _ in range(args.warmup):
-        sw.step()
+        for c in sw.calls:
+            sw.launch(c)
         gather()
     torch.cuda.synchronize()
     small = [c for c in sw.calls if not c["head"]]
     heads = [c for c in sw.calls if c["head"]]
-    R = max(len(c["ring"]) for c in small)
-    # the whole step as one graph per ring position (small calls, then the head calls)
-    g_step = [capture(torch, stream, lambda: [sw.launch(c) for c in small + heads]) for _ in range(R)]
-    # the same step with an event record node before and after each head call (the events bracket the head kernel
-    # inside the graph, without graph-launch gaps); NI such graphs, each with its own events, replayed in turn on ~1% of
-    # the timed steps, so the events of each hold the timing of its last replay
-    NI = 10
-    g_inst = []
-    for _ in range(NI):
-        evs = [(c, torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True)) for c in heads]
+    # the step as one graph per weight-ring position: this rank's small calls, then its head calls between two event
+    # record nodes (they time the head group inside every timed step: the group's time / its launches is the head
+    # kernel's average launch duration, the calls chained back to back as in the step), then the gather copies
+    steps_g = []
+    for _ in range(sw.R):
+        e0, e1 = torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True)
 
-        def body(evs=evs):
+        def body(e0=e0, e1=e1):
             for c in small:
                 sw.launch(c)
-            for c, e0, e1 in evs:
-                e0.record()
+            e0.record()
+            for c in heads:
                 sw.launch(c)
-                e1.record()
-        g_inst.append((capture(torch, stream, body), evs))
-    g_copy = capture(torch, stream, copies) if dist else None
+            e1.record()
+            if dist:
+                copies()
+        steps_g.append((capture(torch, stream, body), e0, e1))
+    # the NCCL all-gather as its own graph (captured once, replayed after every step graph)
+    g_gather = None
+    if dist:
+        g_gather = capture(torch, stream, lambda: dist.all_gather_into_tensor(gather_dst, gather_src))
 
-    def step(s, inst=None):
-        if inst is None:
-            g_step[s % R].replay()
-        else:
-            g_inst[inst % NI][0].replay()
-        if dist:
-            g_copy.replay()
-            dist.all_gather_into_tensor(gather_dst, gather_src)
+    def step(s):
+        steps_g[s % sw.R][0].replay()
+        if g_gather is not None:
+            g_gather.replay()
 
-    for s in range(max(3, args.warmup)):
+    # every step graph replayed before the timed region (a graph's first launch uploads it)
+    for s in range(max(sw.R, args.warmup)):
         step(s)
     torch.cuda.synchronize()
+    clk = Clocks(list(range(ws))) if rank == 0 else None
+    if clk:
+        clk.start()
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    clk = Clocks(local)
-    clk.start()
-    every = max(1, args.steps // 100)   # the instrumented graphs on ~100 of the timed steps
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     w0 = time.time()
     t0.record()
     for s in range(args.steps):
-        step(s, s // every if s % every == 0 else None)
+        step(s)
     t1.record()
     torch.cuda.synchronize()
-    clocks = clk.stop(w0, time.time())
+    w1 = time.time()
     ms = t0.elapsed_time(t1)
+    rank_ms = [ms]
     if dist:
-        tt = torch.tensor([ms], device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
-    head_ms = {}
-    ninst = len(range(0, args.steps, every))
-    for gr, evs in g_inst[:min(NI, ninst)]:
-        for c, a, b in evs:
-            head_ms.setdefault(c["M"], []).append(a.elapsed_time(b))
+        tt = torch.zeros(ws, device="cuda")
+        tt[rank] = ms
+        dist.all_reduce(tt, op=dist.ReduceOp.SUM)
+        rank_ms = [float(v) for v in tt.tolist()]
+        ms = max(rank_ms)
+    clocks = clk.stop(w0, w1) if clk else None
+    # the head group of every graph the timed region replayed (each graph's events hold its last replay)
+    used = sorted({s % sw.R for s in range(args.steps)})
+    head_us = [steps_g[i][1].elapsed_time(steps_g[i][2]) * 1e3 for i in used]
     # ---- per-call device time after the timed region: each call launched once per ring copy (cold weights) in one graph
     calls_us = {}
     for c in sw.calls:
-        n = len(c["ring"]) if not c["head"] else 8
+        n = max(4, len(c["ring"]))
         gr = capture(torch, stream, lambda c=c, n=n: [sw.launch(c) for _ in range(n)])
-        gr.replay()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        gr.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        calls_us["M%d_N%d" % (c["M"], c["Nfull"])] = round(e0.elapsed_time(e1) * 1e3 / n, 2)
+        calls_us["M%d_N%d" % (c["M"], c["Nfull"])] = round(time_graph_us(torch, gr, n), 2)
         del gr
-    del g_step, g_inst, g_copy
+    del steps_g
+    if g_gather is not None:
+        del g_gather
+    torch.cuda.synchronize()
     # ---- e2e: host inputs (pinned) -> device, the public API calls, results -> host, every step
     e2e = run_e2e(args, sw, g, torch, dist, gather)
-    # ---- secondary: GEMM configs 3 and 4; config 5 decode chain (one GPU)
+    # ---- secondary: config 1; GEMM configs 3 and 4; config 5 decode chain
+    config1 = run_config1(g, torch, stream) if rank == 0 else None
     gemm = run_gemm_secondary(args, g, torch, ws, rank, dist)
-    decode = run_decode_chain(args, g, torch, stream) if ws == 1 else None
+    decode = run_decode_chain(args, g, torch, stream, dist, ws, rank)
     res = None
     if rank == 0:
         hbm, tfl, src = peaks()
-        total_bytes = sw.step_bytes * ws * args.steps
-        value = total_bytes / (ms / 1e3) / 1e9
-        # roofline of the dominant kernel: the vocabulary head GEMV, averaged over its launches in the timed region
-        per_m = {M: float(np.mean(v)) for M, v in head_ms.items()}
-        head_bytes = sum(c["bytes"] for c in sw.calls if c["head"])
-        head_time = sum(per_m.values()) / 1e3
-        achieved = head_bytes / head_time / 1e9
+        value = sw.total_bytes * args.steps / (ms / 1e3) / 1e9
+        # roofline of the dominant kernel: the vocabulary head GEMV (this rank's rows), timed inside the timed steps
+        head_bytes = sum(c["bytes"] for c in heads)
+        head_launch_us = float(np.mean(head_us)) / len(heads)
+        achieved = head_bytes / len(heads) / (head_launch_us * 1e-6) / 1e9
         res = {
             "metric": "W4 GEMV GB/s (config 2 sweep: M 1/2/4/8 x N 2048/16384/262144, K 2048)",
             "value": round(value, 1), "unit": "GB/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "q4 weights, f32 x/accumulate", "data": "synthetic (seeded N(0,0.02) weights packed to q4g32a.t64 on device; N(0,1) fp16 x)",
-            "config": {"workload": "config2_gemv_sweep", "M": list(MS), "N": list(NS), "K": K, "parallelism": "column-split x%d + all-gather" % ws,
-                       "l2": "weight rings >= 2x L2 per small-N call; head 335 MB > L2", "bytes_per_step": sw.step_bytes * ws,
-                       "launch": "one CUDA graph per step (the 12 library calls, per weight-ring position); on ~1% of the "
-                                 "timed steps the step graph carries event record nodes around each head call, which time the "
-                                 "head kernel"},
+            "dtype": "q4 weights (fp16 scale/min), f32 accumulate; x as an fp16 hi+lo pair (~22 significant bits) on the tensor cores",
+            "data": "synthetic (seeded N(0,0.02) weights packed to q4g32a.t64 on device; N(0,1) fp16 x)",
+            "config": sweep_config(ws),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                         "traffic": HEAD_TRAFFIC if ws == 1 else None,
-                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one head launch at M=1 from an ncu "
-                                         "capture (335.7 + 4.7 MB); algorithmic 336.6 MB", "kernel": "gemv head (rms+softcap) N=%d/rank K=%d, M=1/2/4/8" % (HEAD_N // ws, K),
-                         "per_M_us": {str(k): round(v * 1e3, 2) for k, v in sorted(per_m.items())}, "peak_source": src},
-            "e2e": e2e, "gpu_launches": len(sw.calls) * args.steps, "clocks": clocks, "gemm": gemm,
-            "calls_us": calls_us, "decode": decode,
+                         "traffic": HEAD_TRAFFIC * (1.0 / ws) if ws in (1, 2, 4, 8) else None,
+                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one head launch at M=1 (N=262144) from an ncu "
+                                         "capture (335.7 + 4.7 MB; algorithmic 336.6 MB), scaled by this rank's rows at N>1",
+                         "kernel": "gemv head (rms+softcap) N=%d/rank K=%d, M=1/2/4/8" % (HEAD_N // ws, K),
+                         "launch_us": round(head_launch_us, 2), "launches_timed": len(used) * len(heads),
+                         "timing": "event record nodes around this rank's 4 head calls inside every timed step graph; achieved = "
+                                   "the head calls' algorithmic bytes / the group's device time", "peak_source": src},
+            "e2e": e2e, "gpu_launches": len(sw.calls) * args.steps, "clocks": clocks, "rank_ms": [round(v, 4) for v in rank_ms],
+            "config1": config1, "gemm": gemm, "calls_us": calls_us, "decode": decode,
         }
         res["cpu_baseline"] = cpu_baseline(args) if ws == 1 else None
     if dist:
         dist.barrier()
     g.close()
     return res
+
+
+def sweep_config(ws):
+    return {"workload": "config2_gemv_sweep", "M": list(MS), "N": list(NS), "K": K,
+            "parallelism": ("head column-split x%d, each small call whole on one rank, one all-gather per step" % ws) if ws > 1 else "one GPU",
+            "l2": "every call reads weights from HBM: each matrix has copies totalling >= 2x L2 (or one copy > 2x L2) and the "
+                  "four M calls of a matrix read four different copies in a step",
+            "bytes_per_step": sum(gemv_bytes(c["M"], c["Nfull"], K, c["head"]) for c in plan_calls(ws)),
+            "launch": "one CUDA graph per step and weight-ring position (every rank's calls; the head group between two event "
+                      "record nodes)" + (", then the NCCL all-gather graph" if ws > 1 else "")}
 
 
 _cudart = None
@@ -476,8 +557,7 @@ def run_e2e(args, sw, g, torch, dist, gather):
         tt = torch.tensor([dt], device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         dt = float(tt.item())
-    ws = dist.get_world_size() if dist else 1
-    val = sw.step_bytes * ws * steps / dt / 1e9
+    val = sw.total_bytes * steps / dt / 1e9
     return {"value": round(val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": round(dt / steps * 1e3, 4),
             "path": "p0pc0rn_b200.gemv/gemvM (ctypes -> libp0mm.so C ABI), pinned host x in, outputs out; copies on a second "
@@ -506,17 +586,24 @@ def _memcpy_kind(dst, src, nbytes, stream, kind):
 CHAIN_LAYERS, CHAIN_D, CHAIN_QKV, CHAIN_FF = 26, 2048, 2560, 8192
 
 
-def run_decode_chain(args, g, torch, stream):
+def run_decode_chain(args, g, torch, stream, dist=None, ws=1, rank=0):
     """config 5: the linear chain of one decode pass of a random-init 26-layer decoder (hidden 2048): per layer QKV
-    2560x2048 (rms prologue), O 2048x2048, GeGLU 2x8192x2048 (rms prologue), down 2048x8192 (kPer 2048 -> 4 split
+    2560x2048 (rms prologue), O 2048x2048, GeGLU 2x8192x2048 (rms prologue), down 2048x8192 (kPer 2048 split
     partials, as gemma4.js runs it), then the head 262144x2048 (rms prologue, softcap + per-tile argmax). Attention,
     norms and residual adds are excluded (as config 5 states): each matmul reads a resident synthetic activation.
-    Every weight is its own q4g32a.t64 matrix (1.31 GB per pass > L2). One pass = one CUDA graph of the 105 calls;
-    tok/s = M tokens per pass / pass time (M = 1 decode, M = 4 draft-verify)."""
+    Every weight is its own q4g32a.t64 matrix (1.31 GB per pass > L2). With ws GPUs the FFN and the head are
+    tensor-parallel: rank r owns 1/ws of the GeGLU's gate and up rows, the matching 1/ws k-slice of the down
+    projection (its split partials are all-gathered, so every rank holds the partials a one-GPU normadd sums) and 1/ws
+    of the head's rows (their per-tile max / argmax pairs are all-gathered); QKV and O run whole on every rank. One
+    pass = one CUDA graph of the calls and collectives; tok/s = M tokens per pass / pass time (max over ranks; M = 1
+    decode, M = 4 draft-verify)."""
     import p0pc0rn_b200 as p0
     dev = torch.device("cuda", torch.cuda.current_device())
     gen = torch.Generator(device=dev)
     D = CHAIN_D
+    FFr, HEADr = CHAIN_FF // ws, HEAD_N // ws
+    kp = min(2048, FFr)
+    nsp = -(-FFr // kp)
 
     def packed(rows, cols, seed):
         gen.manual_seed(seed)
@@ -530,10 +617,11 @@ def run_decode_chain(args, g, torch, stream):
 
     layers = []
     for l in range(CHAIN_LAYERS):
-        layers.append((packed(CHAIN_QKV, D, 7000 + 4 * l), packed(D, D, 7001 + 4 * l), packed(2 * CHAIN_FF, D, 7002 + 4 * l),
-                       packed(D, CHAIN_FF, 7003 + 4 * l)))
-    head = packed(HEAD_N, D, 7999)
-    wbytes = (sum(w["rows"] * w["cols"] for ws_ in layers for w in ws_) + HEAD_N * D) * 0.625
+        s0 = 7000 + 4 * l + 1000 * rank
+        layers.append((packed(CHAIN_QKV, D, s0), packed(D, D, s0 + 1), packed(2 * FFr, D, s0 + 2), packed(D, FFr, s0 + 3)))
+    head = packed(HEADr, D, 7999 + rank)
+    # the whole job's weight bytes per pass (QKV and O on every rank)
+    wbytes = (CHAIN_LAYERS * ((CHAIN_QKV * D + D * D) * ws + 2 * CHAIN_FF * D + D * CHAIN_FF) + HEAD_N * D) * 0.625
     rng = np.random.default_rng(5)
     out = {}
     for M in (1, 4):
@@ -541,8 +629,15 @@ def run_decode_chain(args, g, torch, stream):
         nw = g.upload((1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32), "nw")
         st = g.upload(np.full(8, 0.9, np.float32), "st")
         y = g.buffer(4 * M * 2 * CHAIN_FF * 4, "y")
-        mx = g.buffer(M * (HEAD_N // 64) * 8 + 64, "mx")
-        yh = g.buffer(M * HEAD_N * 4, "yh")
+        mx = g.buffer(M * (HEADr // 64) * 8 + 64, "mx")
+        yh = g.buffer(M * HEADr * 4, "yh")
+        coll = None
+        if dist:
+            part = torch.empty(nsp * M * D, dtype=torch.float32, device=dev)
+            part_all = torch.empty(ws * nsp * M * D, dtype=torch.float32, device=dev)
+            mxt = torch.empty(M * (HEADr // 64) * 2, dtype=torch.float32, device=dev)
+            mx_all = torch.empty(ws * mxt.numel(), dtype=torch.float32, device=dev)
+            coll = (part, part_all, mxt, mx_all, g.wrap(part.data_ptr(), part.numel() * 4, "part"), g.wrap(mxt.data_ptr(), mxt.numel() * 4, "mxt"))
 
         def call(w, N, Kk, pro="raw", epi="store", kPer=0, yb=y, extra=None):
             a = {"w": w, "x": {"buf": xd}, "N": N, "K": Kk, "y": {"buf": yb}, "pro": pro, "epi": epi}
@@ -564,19 +659,32 @@ def run_decode_chain(args, g, torch, stream):
             for wq, wo, wg, wd in layers:
                 call(wq, CHAIN_QKV, D, pro="rms")
                 call(wo, D, D)
-                call(wg, CHAIN_FF, D, pro="rms", epi="geglu")
-                call(wd, D, CHAIN_FF, kPer=2048)
+                call(wg, FFr, D, pro="rms", epi="geglu")
+                if coll:
+                    call(wd, D, FFr, kPer=kp, yb=coll[4])
+                    dist.all_gather_into_tensor(coll[1], coll[0])
+                else:
+                    call(wd, D, FFr, kPer=kp)
+            mxb = coll[5] if coll else mx
             if M == 1:   # the head's rstd is read from the mx buffer past the tile slots (lops.js:125)
-                call(head, HEAD_N, D, pro="rms", epi="softcap", yb=yh,
-                     extra={"mx": {"buf": mx}, "stat": {"buf": mx, "off": HEAD_N // 64 * 2}, "cap": 30.0})
+                extra = {"mx": {"buf": mx}, "stat": {"buf": mx, "off": HEADr // 64 * 2}, "cap": 30.0}
             else:
-                call(head, HEAD_N, D, pro="rms", epi="softcap", yb=yh, extra={"mx": {"buf": mx}, "cap": 30.0})
+                extra = {"mx": {"buf": mxb}, "cap": 30.0}
+            call(head, HEADr, D, pro="rms", epi="softcap", yb=yh, extra=extra)
+            if coll:
+                if M == 1:
+                    _memcpy_d2d(coll[2].data_ptr(), mx.ptr, coll[2].numel() * 4, stream.cuda_stream)
+                dist.all_gather_into_tensor(coll[3], coll[2])
 
         one_pass()
         torch.cuda.synchronize()
         gr = capture(torch, stream, one_pass)
-        for _ in range(2):
+        for _ in range(3):
             gr.replay()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+            torch.cuda.synchronize()
         reps = max(3, min(50, args.steps // 40))
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -585,14 +693,22 @@ def run_decode_chain(args, g, torch, stream):
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / reps
-        # algorithmic bytes: weights + x reads + outputs (down: 4 split partials; head: logits + MX)
-        act = (M * D * 4 + M * CHAIN_QKV * 4) + (M * D * 4 * 2) + (M * D * 4 + M * CHAIN_FF * 4) + (M * CHAIN_FF * 4 + 4 * M * D * 4)
-        pass_bytes = wbytes + CHAIN_LAYERS * act + M * D * 4 + M * HEAD_N * 4 + M * (HEAD_N // 64) * 8
+        if dist:
+            tt = torch.tensor([ms], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        # algorithmic bytes: weights + x reads + outputs (down: its split partials; head: logits + MX), whole job
+        act = (M * D * 4 + M * CHAIN_QKV * 4) * ws + (M * D * 4 * 2) * ws + (M * D * 4 + M * CHAIN_FF * 4) + (M * CHAIN_FF * 4 + 4 * M * D * 4)
+        pass_bytes = wbytes + CHAIN_LAYERS * act + M * D * 4 * ws + M * HEAD_N * 4 + M * (HEAD_N // 64) * 8
         out["M%d" % M] = {"ms_per_pass": round(ms, 4), "tok_s": round(M / (ms / 1e3), 1), "GB_s": round(pass_bytes / (ms / 1e3) / 1e9, 1),
-                          "calls_per_pass": CHAIN_LAYERS * 4 + 1}
+                          "calls_per_pass": CHAIN_LAYERS * 4 + 1, "collectives_per_pass": (CHAIN_LAYERS + 1) if dist else 0}
         del gr
         for b in (xd, nw, st, y, mx, yh):
             g.free(b)
+        if coll:
+            g.free(coll[4])
+            g.free(coll[5])
+            del coll
     for ws_ in layers:
         for w in ws_:
             g.free(w["buf"])
@@ -600,7 +716,10 @@ def run_decode_chain(args, g, torch, stream):
     hbm, _, _ = peaks()
     return {"metric": "linear-chain decode tok/s (config 5: 26 x [QKV, O, GeGLU, down] + head, attention excluded)",
             "weights_GB": round(wbytes / 1e9, 3), "hbm_peak_gbs": hbm, "passes": out,
-            "frac_of_hbm_M1": round(out["M1"]["GB_s"] / hbm, 4), "launch": "one CUDA graph per pass"}
+            "frac_of_hbm_M1": round(out["M1"]["GB_s"] / (hbm * ws), 4),
+            "parallelism": "one GPU" if ws == 1 else "FFN and head tensor-parallel x%d (NCCL all-gather of the down partials "
+                           "and of the head's max/argmax pairs), QKV and O on every rank" % ws,
+            "launch": "one CUDA graph per pass"}
 
 
 # ------------------------------------------------------------------------------------------ GEMM (secondary)
@@ -667,40 +786,85 @@ def run_gemm_secondary(args, g, torch, ws, rank, dist):
 
 
 # ------------------------------------------------------------------------------------------ CPU baseline / reference arm
+HEAD_SLICE = 8192
+
+
+def host_cores():
+    """the host threads this process may run on (torchrun sets OMP_NUM_THREADS=1 for its ranks; the CPU legs set their
+    OpenMP thread count from this instead)"""
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+class CpuSweep:
+    """The reference's GEMV arithmetic on the host cores over the sweep's own calls: the oracle's C restatement of
+    lgemv / lgemvM (lops.js:30-106, lops_spec.js:44-157; scalar C, no SIMD, OpenMP over 64-row tiles), raw / store.
+    The N = 2048 and 16384 calls run whole; the vocabulary head runs on an 8192-row slice (1/32 of its rows, its
+    rms / softcap work left out) and its time is scaled by 32. One step = the 12 calls; its time estimates the full
+    sweep step."""
+
+    def __init__(self, threads):
+        from oracle import ref
+        self.ref, self.threads = ref, threads
+        rng = np.random.default_rng(1)
+        self.w = {}
+        for N in (2048, 16384, HEAD_SLICE):
+            W = (rng.standard_normal(N * K) * 0.02).astype(np.float32)
+            self.w[N] = ref.pack_q4(W, N, K)[0]
+        self.x = {M: rng.standard_normal(M * K).astype(np.float16).astype(np.float32) for M in MS}
+
+    def step(self):
+        t = 0.0
+        for N in NS:
+            Nr = HEAD_SLICE if N == HEAD_N else N
+            for M in MS:
+                t0 = time.perf_counter()
+                self.ref.gemv_cpu_mt(self.w[Nr], self.x[M], M, Nr, K, self.threads)
+                t += (time.perf_counter() - t0) * (N // Nr)
+        return t
+
+    @staticmethod
+    def sample(steps):
+        return ("the config-2 sweep's 12 calls per step (N=2048 and 16384 whole; the N=262144 head on an %d-row slice, "
+                "time x%d), %d steps, scalar C restatement of lgemv/lgemvM with OpenMP" % (HEAD_SLICE, HEAD_N // HEAD_SLICE, steps))
+
+
 def cpu_baseline(args, budget_s=12.0):
-    """The reference's GEMV arithmetic on this host's cores: the oracle's C restatement of lgemv/lgemvM (OpenMP over
-    64-row tiles, all threads), on a bounded sample of the workload: the config-2 calls with N cut to a slice."""
-    from oracle import ref
-    thr = ref.max_threads()
-    rng = np.random.default_rng(1)
-    Ns = 8192
-    W = (rng.standard_normal(Ns * K) * 0.02).astype(np.float32)
-    b, _ = ref.pack_q4(W, Ns, K)
-    t_total, bytes_total, calls = 0.0, 0.0, 0
-    t_start = time.perf_counter()
-    while time.perf_counter() - t_start < budget_s:
-        for M in MS:
-            X = rng.standard_normal(M * K).astype(np.float32)
-            t0 = time.perf_counter()
-            ref.gemv_cpu_mt(b, X, M, Ns, K, thr)
-            t_total += time.perf_counter() - t0
-            bytes_total += gemv_bytes(M, Ns, K, False)
-            calls += 1
-    return {"value": round(bytes_total / t_total / 1e9, 3), "unit": "GB/s", "cores": thr, "kind": "port",
-            "sample": "config-2 GEMV calls M=1/2/4/8 at N=8192 rows, K=2048, repeated for ~%.0f s (%d calls)" % (budget_s, calls)}
+    """the same sweep through the CPU restatement on all host cores, repeated for about budget_s seconds"""
+    thr = host_cores()
+    cs = CpuSweep(thr)
+    cs.step()
+    total = sum(gemv_bytes(c["M"], c["Nfull"], K, c["head"]) for c in plan_calls(1))
+    t, n, t_start = 0.0, 0, time.perf_counter()
+    while time.perf_counter() - t_start < budget_s or n < 3:
+        t += cs.step()
+        n += 1
+    return {"value": round(total * n / t / 1e9, 3), "unit": "GB/s", "cores": thr, "kind": "port", "sample": cs.sample(n)}
 
 
 def run_reference(args, ws, rank):
+    """the reference arm: the reference's own GEMV arithmetic for this path on the host cores (the reference is JS +
+    WebGPU: no JS engine and no CPU WebGPU adapter here, so the oracle's C restatement stands in, kind "port"); rank 0
+    alone at N > 1. W warm-up steps, then K timed steps of the sweep (each a bounded sample: the head on a slice)."""
     if rank != 0:
         return None
-    cb = cpu_baseline(args, budget_s=max(5.0, min(60.0, 3.0 * args.steps)))
-    return {"impl": "reference", "metric": "W4 GEMV GB/s (config 2 sweep: M 1/2/4/8 x N 2048/16384/262144, K 2048)", "value": cb["value"],
-            "unit": "GB/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "q4 weights, f32 x/accumulate", "data": "synthetic",
-            "config": {"workload": "config2_gemv_sweep", "M": list(MS), "N": list(NS), "K": K},
-            "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    thr = host_cores()
+    cs = CpuSweep(thr)
+    for _ in range(args.warmup):
+        cs.step()
+    t = sum(cs.step() for _ in range(args.steps))
+    total = sum(gemv_bytes(c["M"], c["Nfull"], K, c["head"]) for c in plan_calls(1))
+    value = round(total * args.steps / t / 1e9, 3)
+    cb = {"value": value, "unit": "GB/s", "cores": thr, "kind": "port", "sample": cs.sample(args.steps)}
+    return {"impl": "reference", "metric": "W4 GEMV GB/s (config 2 sweep: M 1/2/4/8 x N 2048/16384/262144, K 2048)", "value": value,
+            "unit": "GB/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "q4 weights (fp16 scale/min), f32 x and accumulate", "data": "synthetic", "config": sweep_config(1),
+            "cpu_baseline": cb, "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference is JS + WebGPU (no CPU WebGPU adapter or JS engine on this box): its lgemv/lgemvM arithmetic "
-                    "restated in C (oracle/oracle.c) on the host cores"}
+                    "restated in C (oracle/oracle.c) on the host cores, the same calls as the GPU arm"}
 
 
 def run_case(args):

@@ -1,0 +1,322 @@
+"""A second, independent transcription of the reference's kernel arithmetic for this path, in numpy, used to pin the C
+oracle (oracle/oracle.c) bit for bit on small shapes. It is written from the WGSL the reference generates, not from the
+oracle:
+
+  lgemv   engine/llm/lops.js:30-106        (gemvCode: prologues raw / rms / sum / pleg, q4 and q8 records, epilogues
+                                            store / geglu / softcap with the per-tile max and lowest argmax)
+  lgemvM  engine/llm/lops_spec.js:44-157   (gemvMCode with the default variant: x staged per chunk, same per-row order)
+  gemm    engine/ops/gemm.js:131-211       (the 'f16' x path: fp16 X tile, fp16 W tile f16(q*s + mn) / f16(q*s), f32 FMA
+                                            accumulation or fp16 partial sums per 32-k tile, epilogues f16 / f32 / bias /
+                                            resadd / swiglu)
+
+Conventions, stated once for every WGSL expression: f32 arithmetic rounds after every operation (numpy float32), with
+no contraction of a*b + c unless the WGSL writes fma(); `dot(u, v)` is u.x*v.x + u.y*v.y + u.z*v.z + u.w*v.w added
+left to right; `a + b * c + d * e` is (a + b*c) + d*e; tanh is the C library's tanhf (the WGSL leaves its precision to
+the implementation). A fused f32 FMA of two fp16 values and an f32 is one f32 addition, since the product of two fp16
+values is exact in f32; the fp16 FMA of the 'f16' accumulation rounds the exact f64 value once to fp16. Rows and
+quarter lanes are vectorised with numpy; the loops run over k groups in the WGSL's order.
+"""
+import ctypes
+import ctypes.util
+
+import numpy as np
+
+F = np.float32
+_libm = ctypes.CDLL(ctypes.util.find_library("m") or "libm.so.6")
+_libm.tanhf.restype = ctypes.c_float
+_libm.tanhf.argtypes = [ctypes.c_float]
+_tanhf_vec = np.frompyfunc(lambda v: _libm.tanhf(float(v)), 1, 1)
+_libm.expf.restype = ctypes.c_float
+_libm.expf.argtypes = [ctypes.c_float]
+_expf_vec = np.frompyfunc(lambda v: _libm.expf(float(v)), 1, 1)
+
+C_GELU1, C_GELU2 = F(0.7978845608028654), F(0.044715)
+
+
+def tanhf(a):
+    a = np.asarray(a, F)
+    return np.asarray(_tanhf_vec(a), dtype=np.float64).astype(F).reshape(a.shape)
+
+
+def expf(a):
+    a = np.asarray(a, F)
+    return np.asarray(_expf_vec(a), dtype=np.float64).astype(F).reshape(a.shape)
+
+
+def gelu_lops(v):
+    """lops.js:24 GELU(v): (v * 0.5 * (1.0 + tanh(clamp(0.79788.. * (v + 0.044715 * v * v * v), -15, 15))))"""
+    v = np.asarray(v, F)
+    t = ((C_GELU2 * v) * v) * v
+    u = np.clip(C_GELU1 * (v + t), F(-15.0), F(15.0)).astype(F)
+    return ((v * F(0.5)) * (F(1.0) + tanhf(u))).astype(F)
+
+
+def gelu_gemm(g):
+    """gemm.js:204 swiglu 'gelu': g * 0.5 * (1 + tanh(clamp(0.7978845608 * (g + 0.044715 * g * g * g), -15, 15)))"""
+    g = np.asarray(g, F)
+    t = ((F(0.044715) * g) * g) * g
+    u = np.clip(F(0.7978845608) * (g + t), F(-15.0), F(15.0)).astype(F)
+    return ((g * F(0.5)) * (F(1.0) + tanhf(u))).astype(F)
+
+
+def silu_gemm(g):
+    """gemm.js:204 swiglu 'silu': g / (1 + exp(-g)) (exp: the C library's expf)"""
+    g = np.asarray(g, F)
+    e = expf(-g)
+    return (g / (F(1.0) + e)).astype(F)
+
+
+def words(b):
+    """the weight buffer as u32 words (W: array<u32>)"""
+    return np.frombuffer(np.ascontiguousarray(b, dtype=np.uint8).tobytes(), dtype=np.uint32)
+
+
+def unpack2x16float(w):
+    """WGSL unpack2x16float: (low half, high half) as f32"""
+    w = np.asarray(w, np.uint32)
+    lo = (w & 0xFFFF).astype(np.uint16).view(np.float16).astype(F)
+    hi = (w >> 16).astype(np.uint16).view(np.float16).astype(F)
+    return lo, hi
+
+
+def dot4(u, v):
+    """dot(u, v) over the last axis of length 4, added left to right"""
+    return (((u[..., 0] * v[..., 0]) + (u[..., 1] * v[..., 1])) + (u[..., 2] * v[..., 2])) + (u[..., 3] * v[..., 3])
+
+
+def _tile_dots(W, xs, k0, k1, tile_rows, wG, wOff, q8):
+    """acc for every (row of the given tiles, quarter lane w) over groups [g0, g1): lops.js:63-82 / lops_spec.js:92-112.
+    xs: the staged x, f32, indexed from k0. Returns f32 [rows, 4]."""
+    rows = np.asarray(tile_rows)
+    t, r = rows // 64, rows % 64
+    acc = np.zeros((rows.size, 4), F)
+    wv = np.arange(4)
+    if not q8:
+        g0, g1 = k0 // 32, (k1 + 31) // 32
+        for g in range(g0, g1):
+            rec = wOff + (t * wG + g) * 320
+            q = W[rec[:, None] + r[:, None] * 4 + wv[None, :]]                         # [rows, 4]
+            s, mn = unpack2x16float(W[rec + 256 + r])
+            xb = g * 32 - k0 + wv * 8                                                   # [4]
+            a = np.stack([xs[xb + i] for i in range(4)], -1)[None, :, :]                  # [1, 4, 4]
+            b = np.stack([xs[xb + 4 + i] for i in range(4)], -1)[None, :, :]
+            qa = np.stack([((q >> (4 * i)) & 15) for i in range(4)], -1).astype(F)
+            qb = np.stack([((q >> (16 + 4 * i)) & 15) for i in range(4)], -1).astype(F)
+            one = np.ones(4, F)
+            d1 = dot4(qa, a) + dot4(qb, b)
+            d2 = dot4(a, one) + dot4(b, one)
+            acc = (acc + s[:, None] * d1) + mn[:, None] * d2
+    else:
+        g0, g1 = k0 // 64, (k1 + 63) // 64
+        for g in range(g0, g1):
+            rec = wOff + (t * wG + g) * 1056
+            s2x, s2y = unpack2x16float(W[rec + 1024 + (r >> 1)])
+            sc = np.where((r & 1) == 1, s2y, s2x).astype(F)
+            d = np.zeros((rows.size, 4), F)
+            for u in range(4):
+                q = W[rec[:, None] + r[:, None] * 16 + wv[None, :] * 4 + u]
+                qv = np.stack([((q << (24 - 8 * i)) & 0xFFFFFFFF).astype(np.uint32).view(np.int32) >> 24 for i in range(4)], -1).astype(F)
+                xb = g * 64 - k0 + wv * 16 + u * 4
+                xv = np.stack([xs[xb + i] for i in range(4)], -1)[None, :, :]
+                d = d + dot4(qv, xv)
+            acc = acc + sc[:, None] * d
+    return acc
+
+
+def _quarter_sum(acc):
+    """red[li] + red[li + 1] + red[li + 2] + red[li + 3] (lops.js:86-88)"""
+    return ((acc[:, 0] + acc[:, 1]) + acc[:, 2]) + acc[:, 3]
+
+
+def _softcap_tiles(tot, cap, ntile_rows):
+    """v = cap * tanh(clamp(tot / cap, -15, 15)); per 64-row tile the max and the lowest row holding it"""
+    cap = F(cap)
+    v = (cap * tanhf(np.clip(tot / cap, F(-15.0), F(15.0)).astype(F))).astype(F)
+    vt = v.reshape(-1, 64)
+    mx = vt.max(axis=1)
+    idx = np.array([int(np.nonzero(vt[i] == mx[i])[0][0]) for i in range(vt.shape[0])], np.int64)
+    return v, mx, idx
+
+
+def gemv(Wbytes, X, N, K, *, enc="q4g32a.t64", cols=None, woff=0, rowB=0, kPer=None, pro="raw", epi="store", ldy=None,
+         stat=None, stat_off=0, norm=None, norm_off=0, ev=None, ev_off=0, src=None, cap=30.0, KCH=2048):
+    """lgemv for one token. Returns (Y, MX or None, nsplit) with the reference's output layout."""
+    q8 = enc == "q8g64s.t64"
+    G = 64 if q8 else 32
+    W = words(Wbytes)
+    wG = (cols or K) // G
+    kp = kPer or K
+    nsplit = -(-K // kp)
+    ldy = ldy or N
+    X = np.asarray(X, F)
+    NT = N // 64
+    Y = np.zeros(nsplit * ldy if epi == "store" else N, F)
+    MX = np.zeros(NT * 2, F) if epi == "softcap" else None
+    for split in range(nsplit):
+        k0, k1 = split * kp, min(K, split * kp + kp)
+        k = np.arange(k0, k1)
+        if pro == "raw":
+            xs = X[rowB + k]
+        elif pro == "rms":
+            xs = (X[rowB + k] * F(stat[stat_off])) * np.asarray(norm, F)[norm_off + k]
+        else:
+            ldp, nsrc = src
+            s = np.zeros(k.size, F)
+            for j in range(nsrc):
+                s = s + X[j * ldp + k]
+            xs = s if pro == "sum" else gelu_lops(s) * np.asarray(ev, F)[ev_off + k]
+        xs = np.asarray(xs, F)
+        rows = np.arange(N)
+        tot0 = _quarter_sum(_tile_dots(W, xs, k0, k1, rows, wG, woff // 4, q8))
+        if epi == "store":
+            Y[split * ldy:split * ldy + N] = tot0
+        elif epi == "geglu":
+            tot1 = _quarter_sum(_tile_dots(W, xs, k0, k1, rows + N, wG, woff // 4, q8))
+            Y[:N] = gelu_lops(tot0) * tot1
+        else:
+            v, mx, idx = _softcap_tiles(tot0, cap, NT)
+            Y[:N] = v
+            MX[0::2] = mx
+            MX[1::2] = (np.arange(NT) * 64 + idx).astype(np.uint32).view(F)
+    return Y, MX, nsplit
+
+
+def gemvM(Wbytes, X, M, N, K, *, enc="q4g32a.t64", cols=None, woff=0, rowB=0, ldx=None, kPer=None, pro="raw", epi="store",
+          ldm=None, ldy=None, stat=None, stat_off=0, stat_ld=2, norm=None, norm_off=0, ev=None, ev_off=0, ev_ld=0, src=None,
+          cap=30.0):
+    """lgemvM: per row m the lgemv order with x from row m (x.ldx), rstd ST[statOff + m*statLd], pleg ev per row.
+    Returns (Y, MX or None, nsplit) in lops_spec.js's layout Y[split*ldy + m*ldm + n], MX[(m*ntile + tile)*2]."""
+    q8 = enc == "q8g64s.t64"
+    G = 64 if q8 else 32
+    W = words(Wbytes)
+    wG = (cols or K) // G
+    kp = kPer or K
+    nsplit = -(-K // kp)
+    ldx, ldm = ldx or K, ldm or N
+    ldy = ldy or M * ldm
+    X = np.asarray(X, F)
+    NT = N // 64
+    Y = np.zeros(nsplit * ldy if epi == "store" else M * ldm, F)
+    MX = np.zeros(M * NT * 2, F) if epi == "softcap" else None
+    rows = np.arange(N)
+    for split in range(nsplit):
+        k0, k1 = split * kp, min(K, split * kp + kp)
+        k = np.arange(k0, k1)
+        for m in range(M):
+            if pro == "raw":
+                xs = X[m * ldx + rowB + k]
+            elif pro == "rms":
+                xs = (X[m * ldx + rowB + k] * F(stat[stat_off + m * stat_ld])) * np.asarray(norm, F)[norm_off + k]
+            else:
+                ldp, nsrc = src
+                s = np.zeros(k.size, F)
+                for j in range(nsrc):
+                    s = s + X[j * ldp + m * ldx + k]
+                xs = gelu_lops(s) * np.asarray(ev, F)[ev_off + m * ev_ld + k]
+            xs = np.asarray(xs, F)
+            tot0 = _quarter_sum(_tile_dots(W, xs, k0, k1, rows, wG, woff // 4, q8))
+            if epi == "store":
+                Y[split * ldy + m * ldm:split * ldy + m * ldm + N] = tot0
+            elif epi == "geglu":
+                tot1 = _quarter_sum(_tile_dots(W, xs, k0, k1, rows + N, wG, woff // 4, q8))
+                Y[m * ldm:m * ldm + N] = gelu_lops(tot0) * tot1
+            else:
+                v, mx, idx = _softcap_tiles(tot0, cap, NT)
+                Y[m * ldm:m * ldm + N] = v
+                MX[m * NT * 2:(m + 1) * NT * 2:2] = mx
+                MX[m * NT * 2 + 1:(m + 1) * NT * 2:2] = (np.arange(NT) * 64 + idx).astype(np.uint32).view(F)
+    return Y, MX, nsplit
+
+
+def _h(bits):
+    return np.asarray(bits, np.uint16).view(np.float16).astype(F)
+
+
+def gemm_wtile(Wbytes, rows, k_lo, k_hi, enc, wG, wk0=0):
+    """the fp16 W tile values gemm.js:139-160 builds for weight rows `rows` and k in [k_lo, k_hi): q4 f16(q*s + mn),
+    q8 f16(q*s), as f32 values [rows, k]"""
+    W = words(Wbytes)
+    rows = np.asarray(rows)
+    out = np.zeros((rows.size, k_hi - k_lo), F)
+    rr, tb = rows & 63, rows >> 6
+    for kk in range(k_lo, k_hi):
+        kw = wk0 + kk
+        if enc == "q4g32a.t64":
+            rec = (tb * wG + kw // 32) * 320
+            q = W[rec + rr * 4 + (kw % 32) // 8]
+            cv = ((q >> (4 * (kw % 8))) & 15).astype(F)
+            s, mn = unpack2x16float(W[rec + 256 + rr])
+            out[:, kk - k_lo] = ((cv * s) + mn).astype(np.float16).astype(F)
+        else:
+            rec = (tb * wG + kw // 64) * 1056
+            q = W[rec + rr * 16 + (kw % 64) // 4]
+            cv = ((q << (24 - 8 * (kw % 4))) & 0xFFFFFFFF).astype(np.uint32).view(np.int32) >> 24
+            s2x, s2y = unpack2x16float(W[rec + 1024 + (rr >> 1)])
+            sc = np.where((rr & 1) == 1, s2y, s2x)
+            out[:, kk - k_lo] = (cv.astype(F) * sc).astype(np.float16).astype(F)
+    return out
+
+
+def _f16_round_once(v64):
+    """an exact f64 value rounded once to fp16 (round half to even), as f32"""
+    return np.asarray(v64, np.float64).astype(np.float16).astype(F)
+
+
+def gemm(Wbytes, X16, M, N, K, *, enc="q4g32a.t64", rows=None, cols=None, ldx=None, kx0=0, wr0=0, wr1=0, wk0=0, epi="f16",
+         act="silu", acc="f32", Y=None, ldy=None, ny0=0, ev=None, ev_off=0, bv=None, bv_off=0, bv_up=0, res=False, store=False,
+         post_gelu=False):
+    """gemm.js with the 'f16' x path. X16 fp16 bits [M][ldx]. Returns Y (fp16 bits, or f32 for 'f32' / 'resadd')."""
+    Nw = rows or N
+    G = 64 if enc == "q8g64s.t64" else 32
+    wG = (cols or K) // G
+    ldx, ldy = ldx or K, ldy or N
+    f32y = epi in ("f32", "resadd")
+    if Y is None:
+        Y = np.zeros(M * ldy, F if f32y else np.uint16)
+    Y = Y.copy()
+    ncol = N if epi != "swiglu" else N
+    cc = np.arange(ncol)
+    if epi == "swiglu":
+        wrows = np.where((cc & 1) == 0, wr0, wr1) + (cc >> 1)
+    else:
+        wrows = np.minimum(wr0 + cc, Nw - 1)
+    Wt = gemm_wtile(Wbytes, wrows, 0, K, enc, wG, wk0)               # [N, K] fp16 values
+    Xv = _h(np.asarray(X16, np.uint16).reshape(M, ldx)[:, kx0:kx0 + K])   # [M, K]
+    A = np.zeros((M, ncol), F)
+    for k0 in range(0, K, 32):
+        if acc == "f16":
+            h = np.zeros((M, ncol), F)
+            for k in range(k0, k0 + 32):
+                h = _f16_round_once(Xv[:, k:k + 1].astype(np.float64) * Wt[None, :, k].astype(np.float64) + h.astype(np.float64))
+            A = A + h
+        else:
+            for k in range(k0, k0 + 32):
+                A = A + Xv[:, k:k + 1] * Wt[None, :, k]       # fma: the fp16 x fp16 product is exact in f32
+    Yr = Y.reshape(M, ldy)
+    if epi == "swiglu":
+        gB = np.asarray(bv, F)[bv_off + np.arange(N // 2)] if bv is not None else np.zeros(N // 2, F)
+        uB = np.asarray(bv, F)[bv_off + bv_up + np.arange(N // 2)] if bv is not None else np.zeros(N // 2, F)
+        g = A[:, 0::2] + gB
+        u = A[:, 1::2] + uB
+        a = gelu_gemm(g) if act == "gelu" else silu_gemm(g)
+        Yr[:, ny0:ny0 + N // 2] = (a * u).astype(np.float16).view(np.uint16)
+    elif epi == "f16":
+        Yr[:, ny0:ny0 + N] = A.astype(np.float16).view(np.uint16)
+    elif epi == "f32":
+        Yr[:, ny0:ny0 + N] = A
+    elif epi == "bias":
+        t = A + np.asarray(ev, F)[ev_off + np.arange(N)]
+        if res:
+            t = t + _h(Yr[:, ny0:ny0 + N])
+        h = t.astype(np.float16)
+        if post_gelu:   # misc.js:116 ew 'gelu' on the fp16 result, in f32: 0.5 * x * (1 + tanh(clamp(u, -15, 15)))
+            x = h.astype(F)
+            uu = np.clip(F(0.7978845608) * (x + ((C_GELU2 * x) * x) * x), F(-15.0), F(15.0)).astype(F)
+            h = ((F(0.5) * x) * (F(1.0) + tanhf(uu))).astype(np.float16)
+        Yr[:, ny0:ny0 + N] = h.view(np.uint16)
+    elif epi == "resadd":
+        gte = np.asarray(ev, F)[ev_off + np.arange(N)] if ev is not None else np.ones(N, F)
+        c = np.asarray(bv, F)[bv_off + np.arange(N)] if bv is not None else np.zeros(N, F)
+        t = gte * (A + c)
+        Yr[:, ny0:ny0 + N] = t if store else Yr[:, ny0:ny0 + N] + t
+    return Y

@@ -500,3 +500,95 @@ def test_gemm_xpro_oracle(mode):
     else:
         v = ((x * rstd).astype(f) * pv[4 + kx0:4 + kx0 + K]).astype(f)
     assert np.array_equal(got, ref.f2h(v.astype(np.float64).ravel()))
+
+
+# ---------------------------------------------------------------- the oracle's kernel arithmetic against a second,
+# independent transcription of the WGSL (tests/jsref_kernels.py, numpy), bit for bit on small shapes
+from . import jsref_kernels as jk  # noqa: E402
+
+
+def _bits_equal(a, b):
+    a, b = np.asarray(a), np.asarray(b)
+    assert a.shape == b.shape
+    if a.dtype == np.float32:
+        a, b = a.view(np.uint32), b.view(np.uint32)
+    diff = np.nonzero(a != b)[0]
+    assert diff.size == 0, "%d of %d differ, first at %d: %r vs %r" % (diff.size, a.size, diff[0], a[diff[0]], b[diff[0]])
+
+
+@pytest.mark.parametrize("enc", ["q4g32a.t64", "q8g64s.t64"])
+@pytest.mark.parametrize("pro,epi,kPer", [("raw", "store", None), ("raw", "store", 256), ("rms", "softcap", None), ("rms", "geglu", None),
+                                          ("sum", "store", None), ("pleg", "store", None)])
+def test_gemv_second_transcription(enc, pro, epi, kPer):
+    N, K = 128, 512
+    rows = 2 * N if epi == "geglu" else N
+    W = ref.randn(rows * K, 900, 0.02)
+    b = (ref.pack_q4 if enc == "q4g32a.t64" else ref.pack_q8)(W, rows, K)[0]
+    kw = {}
+    X = ref.randn(2 * K + 64, 901)
+    okw = {}
+    if pro == "rms":
+        # the rstd slot: in the MX buffer past the tile pairs for softcap (lops.js:125), else the stat buffer
+        st = np.zeros(N // 64 * 2 + 4, np.float32)
+        st[N // 64 * 2 + 1] = 0.83
+        kw.update(stat=st.copy(), stat_off=N // 64 * 2 + 1, norm=ref.randn(K + 16, 902, 0.1) + 1, norm_off=16)
+        okw = {"mx": st.copy()} if epi == "softcap" else {"stat_buf": st.copy()}
+        okw.update(stat_off=kw["stat_off"], norm=kw["norm"], norm_off=16)
+    if pro in ("sum", "pleg"):
+        kw.update(src=(K + 32, 2))
+    if pro == "pleg":
+        kw.update(ev=ref.randn(K + 8, 903, 0.5), ev_off=8)
+    if pro in ("sum", "pleg"):
+        okw = {k: v for k, v in kw.items()}
+    rowB = 32 if pro in ("raw", "rms") else 0
+    want_y, want_mx, ns = ref.gemv(b, X, N, K, enc=enc, rowB=rowB, kPer=kPer, pro=pro, epi=epi, **okw)
+    got_y, got_mx, ns2 = jk.gemv(b, X, N, K, enc=enc, rowB=rowB, kPer=kPer, pro=pro, epi=epi, **kw)
+    assert ns == ns2
+    _bits_equal(got_y, want_y[:got_y.size])
+    if epi == "softcap":
+        _bits_equal(got_mx, want_mx[:got_mx.size])
+
+
+@pytest.mark.parametrize("M", [2, 3])
+@pytest.mark.parametrize("pro,epi,kPer", [("raw", "store", 128), ("rms", "softcap", None), ("rms", "geglu", None), ("pleg", "store", None)])
+def test_gemvM_second_transcription(M, pro, epi, kPer):
+    N, K = 128, 256
+    rows = 2 * N if epi == "geglu" else N
+    b, _ = ref.pack_q4(ref.randn(rows * K, 910, 0.02), rows, K)
+    ldx = K + 32
+    X = ref.randn(2 * M * ldx, 911)
+    kw = {}
+    if pro == "rms":
+        kw.update(stat=np.array([0.7, 0, 0.8, 0, 0.9, 0], np.float32), stat_ld=2, norm=ref.randn(K, 912, 0.1) + 1)
+    if pro == "pleg":
+        kw.update(src=(M * ldx, 2), ev=ref.randn(M * K, 913, 0.5), ev_ld=K)
+    want_y, want_mx, ns = ref.gemvM(b, X, M, N, K, ldx=ldx, kPer=kPer, pro=pro, epi=epi, **kw)
+    got_y, got_mx, ns2 = jk.gemvM(b, X, M, N, K, ldx=ldx, kPer=kPer, pro=pro, epi=epi, **kw)
+    assert ns == ns2
+    _bits_equal(got_y, want_y[:got_y.size])
+    if epi == "softcap":
+        _bits_equal(got_mx, want_mx)
+
+
+@pytest.mark.parametrize("enc", ["q4g32a.t64", "q8g64s.t64"])
+@pytest.mark.parametrize("acc", ["f32", "f16"])
+@pytest.mark.parametrize("epi", ["f16", "f32", "bias", "bias_gelu", "resadd", "swiglu_silu", "swiglu_gelu"])
+def test_gemm_second_transcription(enc, acc, epi):
+    M, N, K = 6, 128, 128
+    W = ref.randn(N * K, 920, 0.02)
+    b = (ref.pack_q4 if enc == "q4g32a.t64" else ref.pack_q8)(W, N, K)[0]
+    X = ref.f2h(ref.round_f16(ref.randn(M * K, 921)))
+    kw = {}
+    e = epi
+    if epi.startswith("bias"):
+        e = "bias"
+        kw.update(ev=ref.randn(N + 4, 922, 0.01), ev_off=4, res=True, post_gelu=epi == "bias_gelu",
+                  Y=ref.f2h(ref.randn(M * N, 923, 0.5)))
+    elif epi == "resadd":
+        kw.update(ev=ref.randn(N, 924, 1.0), bv=ref.randn(N, 925, 0.01), Y=ref.randn(M * N, 926))
+    elif epi.startswith("swiglu"):
+        e = "swiglu"
+        kw.update(act=epi.split("_")[1], wr0=0, wr1=N // 2, bv=ref.randn(N, 927, 0.01), bv_up=N // 2)
+    want = ref.gemm(b, X, M, N, K, enc=enc, epi=e, acc=acc, **{k: (v.copy() if isinstance(v, np.ndarray) and k == "Y" else v) for k, v in kw.items()})
+    got = jk.gemm(b, X, M, N, K, enc=enc, epi=e, acc=acc, **kw)
+    _bits_equal(got, want)
