@@ -154,6 +154,31 @@ p0_status p0_gemvM(p0_ctx *ctx, const p0_gemvM_args *a, uint32_t *nsplit);
 #define P0_NOALLOC_COUNTER_BYTES (64u << 10)
 p0_status p0_gemvM_noalloc(p0_ctx *ctx, const p0_gemvM_args *a, uint32_t *nsplit);
 
+/* ---------------------------------------------------------------------------------------------- recorded chains */
+/* The decode loop's dispatch recorder (DecodeRunner, engine/llm/drunner.js:1-8, begin :36): between p0_chain_begin and
+ * p0_chain_end every p0_gemv / p0_gemvM call on the context is checked exactly as it would be (same statuses and
+ * messages) and recorded instead of launched; p0_chain_run enqueues the recorded calls on the context's stream, in
+ * order, with the results they would have had one by one (within the GEMV tolerance: partial sums combine in another
+ * order). Runs of q4 calls with the chain's M (the M of its first q4 call), K per split <= 2048 and at most 4 x SMs
+ * output units run as ONE cooperative kernel: each output unit (64-row tile x k-split) is computed whole by one CTA,
+ * units dealt round-robin over the SMs across calls; every warp streams its share of its CTA's records through a ring
+ * of bulk copies that runs on across calls, and a grid barrier sits only before a call that reads what earlier calls
+ * of the kernel wrote (or writes what they read or wrote), by the byte ranges each call binds. Other calls (the
+ * vocabulary head, q8 weights) run between them on their own kernels. p0_chain_end allocates the chain's device state
+ * (descriptors, barrier words); p0_chain_run allocates nothing. The chain keeps the device addresses of every
+ * buffer its calls bound, so those buffers must outlive it, and the weights must not change while a run is in flight
+ * (they are fetched ahead of the barriers). Runs of one chain on one stream are ordered; two runs of one chain must
+ * not overlap on the GPU (they share the counters). A barrier wait that runs out sets the context's error word
+ * (p0_done reports P0_ETIMEOUT). p0_chain_info reports the recorded calls, those the chain kernel takes, the launches
+ * of a run and the grid barriers. */
+typedef struct p0_chain p0_chain;
+p0_status p0_chain_begin(p0_ctx *ctx);
+p0_status p0_chain_end(p0_ctx *ctx, p0_chain **out);
+p0_status p0_chain_run(p0_ctx *ctx, p0_chain *chain);
+p0_status p0_chain_info(p0_ctx *ctx, const p0_chain *chain, uint32_t *calls, uint32_t *kernel_calls, uint32_t *launches,
+                        uint32_t *barriers);
+p0_status p0_chain_free(p0_ctx *ctx, p0_chain *chain);
+
 /* ---------------------------------------------------------------------------------------------- GEMM */
 enum { P0_GEPI_F16 = 0, P0_GEPI_F32 = 1, P0_GEPI_BIAS = 2, P0_GEPI_RESADD = 3, P0_GEPI_SWIGLU = 4, P0_GEPI_HEADS = 5, P0_GEPI_ONORMGATE = 6 };
 enum { P0_ACT_SILU = 0, P0_ACT_GELU = 1 };

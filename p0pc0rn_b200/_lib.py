@@ -24,7 +24,8 @@ P0_ROPE_INTER, P0_ROPE_HALF = 0, 1
 EXPORTS = ["p0_init", "p0_destroy", "p0_set_stream", "p0_set_overlap", "p0_last_error", "p0_stats", "p0_buffer", "p0_wrap", "p0_upload", "p0_read",
            "p0_free", "p0_done", "p0_device_ptr", "p0_gemv", "p0_gemvM", "p0_gemvM_noalloc", "p0_gemm", "p0_pack_q4", "p0_pack_q8",
            "p0_dequant_f16", "p0_version", "p0_argmaxM", "p0_embed", "p0_normadd", "p0_dhead",
-           "p0_upload_file", "p0_qkrope", "p0_attn_dec", "p0_wait_selftest"]
+           "p0_upload_file", "p0_qkrope", "p0_attn_dec", "p0_wait_selftest",
+           "p0_chain_begin", "p0_chain_end", "p0_chain_run", "p0_chain_info", "p0_chain_free"]
 P0_NOALLOC_SCRATCH_BYTES = 16 << 20   # include/p0mm.h
 P0_OVERLAP_WEIGHTS = 1
 P0_NOALLOC_COUNTER_BYTES = 64 << 10
@@ -134,6 +135,11 @@ def load():
     L.p0_normadd.argtypes = [vp, ctypes.POINTER(p0_normadd_args)]
     L.p0_dhead.argtypes = [vp, ctypes.POINTER(p0_dhead_args)]
     L.p0_wait_selftest.argtypes = [vp, ctypes.c_uint32]
+    L.p0_chain_begin.argtypes = [vp]
+    L.p0_chain_end.argtypes = [vp, ctypes.POINTER(vp)]
+    L.p0_chain_run.argtypes = [vp, vp]
+    L.p0_chain_info.argtypes = [vp, vp] + [ctypes.POINTER(ctypes.c_uint32)] * 4
+    L.p0_chain_free.argtypes = [vp, vp]
     L.p0_version.restype = ctypes.c_char_p
     for name in EXPORTS:
         if name != "p0_version":

@@ -9,7 +9,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libp0mm.so")
-SOURCES = ["context.cu", "gemv.cu", "gemv_v3.cu", "gemv_v4.cu", "gemv_v5.cu", "gemm.cu", "pack.cu", "lops.cu", "io.cu"]
+SOURCES = ["context.cu", "gemv.cu", "gemv_v3.cu", "gemv_v4.cu", "gemv_v5.cu", "chain.cu", "gemm.cu", "pack.cu", "lops.cu", "io.cu"]
 HEADERS = ["internal.h", "tc.cuh", "gemv_common.cuh", os.path.join("..", "..", "include", "p0mm.h")]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

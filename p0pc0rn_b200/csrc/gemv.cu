@@ -550,6 +550,33 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
   uint32_t span = kPer < K ? kPer : K;
   if (xc > span) xc = span;
   p.xc = xc;
+  if (c->chain_rec) {
+    // a chain is being recorded (p0_chain_begin): the checked call is kept, with the byte ranges it reads and
+    // writes, instead of launched
+    ChainIO io{};
+    io.in[0] = {(uintptr_t)rx.base, (uintptr_t)rx.base + xneed};
+    if (pro == P0_PRO_RMS) {
+      io.in[1] = {(uintptr_t)rn.base, (uintptr_t)rn.base + (uint64_t)K * 4};
+      io.in[2] = {(uintptr_t)rs.base, (uintptr_t)rs.base + ((uint64_t)(M - 1) * stat_ld + 1) * 4};
+    }
+    if (pro == P0_PRO_PLEG) io.in[3] = {(uintptr_t)re.base, (uintptr_t)re.base + ((uint64_t)(M - 1) * ev_ld + K) * 4};
+    io.out[0] = {(uintptr_t)ry.base, (uintptr_t)ry.base + yneed};
+    if (epi == P0_EPI_SOFTCAP) io.out[1] = {(uintptr_t)rm.base, (uintptr_t)rm.base + (uint64_t)M * NT * 8};
+    return chain_record(c, op, p, nsplit, io);
+  }
+  return gemv_dispatch(c, op, p, nsplit, noalloc);
+}
+
+}  // namespace
+
+namespace p0gemv {
+// the kernel choice and launch of one checked gemv / gemvM call (also used for the calls of a recorded chain that do
+// not run inside the chain kernel)
+p0_status gemv_dispatch(p0_ctx *c, const char *op, const GemvParams &p, uint32_t nsplit, bool noalloc) {
+  p0_status st;
+  const uint32_t M = p.M, N = p.N, K = p.K, epi = (uint32_t)p.epi;
+  const bool q8 = p.q8 != 0;
+  const uint32_t span = p.kPer < K ? p.kPer : K;
   cudaSetDevice(c->device);
   cudaError_t e;
   // tuning override, read on every call: P0MM_GEMV=v2 | v3 | v4 | v5 runs that kernel wherever it fits
@@ -565,7 +592,7 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
     // q8g64s.t64 weights run on the cluster kernel only
     if (noalloc) return p0_fail(c, P0_EINVAL, "%s: q8g64s.t64 weights are not built for the allocation-free entry point", op);
     if (!v5_plan(p, nsplit, c->sm_count, &p5))
-      return p0_fail(c, P0_EINVAL, "%s: q8g64s.t64 with M %u x K %u (split %u) is not built in this library yet", op, M, K, kPer);
+      return p0_fail(c, P0_EINVAL, "%s: q8g64s.t64 with M %u x K %u (split %u) is not built in this library yet", op, M, K, p.kPer);
     if ((st = p0_cuda(c, launch_v5(p, p5, c->stream), op))) return st;
     return p0_launched(c, op);
   }
@@ -619,8 +646,7 @@ p0_status run_gemv(p0_ctx *c, const char *op, const p0_wview &w, p0_buf xb, uint
   if ((st = p0_cuda(c, e, op))) return st;
   return p0_launched(c, op);
 }
-
-}  // namespace
+}  // namespace p0gemv
 
 // the checks and call of gemvM (lops_spec.js:163-191), shared by p0_gemvM and p0_gemvM_noalloc
 static p0_status gemvM_call(p0_ctx *c, const p0_gemvM_args *a, uint32_t *nsplit_out, bool noalloc) {

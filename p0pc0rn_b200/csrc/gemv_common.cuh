@@ -271,4 +271,17 @@ cudaError_t launch_v5(const GemvParams &p, const V5Plan &pl, cudaStream_t s);
 // device; looked up on a device's first call
 cudaError_t v4_noalloc_scratch(uint8_t **out);
 
+// the kernel choice and launch of one checked gemv / gemvM call (gemv.cu)
+p0_status gemv_dispatch(p0_ctx *c, const char *op, const GemvParams &p, uint32_t nsplit, bool noalloc);
+
+// the byte ranges a recorded call reads (x, norm, stat, ev) and writes (y, mx); {0, 0} = none
+struct ChainRange {
+  uintptr_t lo, hi;
+};
+struct ChainIO {
+  ChainRange in[4], out[2];
+};
+// keeps a checked call in the chain being recorded on the context (chain.cu)
+p0_status chain_record(p0_ctx *c, const char *op, const GemvParams &p, uint32_t nsplit, const ChainIO &io);
+
 }  // namespace p0gemv

@@ -33,6 +33,7 @@ struct p0_ctx {
   // or shrinks while the workspace lives, so one call's scratch never lands on another call's counters.
   void *ws = nullptr;
   size_t ws_bytes = 0, ws_cnt_bytes = 0;
+  void *chain_rec = nullptr;     // p0_chain_begin .. p0_chain_end: gemv / gemvM calls are recorded into this chain
   bool overlap = false;          // p0_set_overlap: weights are static, GEMVs may fetch them before the call ahead ends
   // p0_upload_file: two pinned staging chunks and the events that say when the copy out of each has finished
   void *io_stage[2] = {nullptr, nullptr};

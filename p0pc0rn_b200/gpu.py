@@ -151,6 +151,17 @@ class Gpu:
         records its code; the next done() raises P0Error(P0_ETIMEOUT) and the context stays usable"""
         self._check(self._lib.p0_wait_selftest(self.ctx, int(polls)))
 
+    # -------------------------------------------------------------- recorded chains (engine/llm/drunner.js)
+    def chain_begin(self):
+        """start recording: gemv / gemvM calls on this context are checked and kept, not launched (DecodeRunner.begin)"""
+        self._check(self._lib.p0_chain_begin(self.ctx))
+
+    def chain_end(self):
+        """stop recording; returns the Chain (its device state is allocated here)"""
+        h = ctypes.c_void_p()
+        self._check(self._lib.p0_chain_end(self.ctx, ctypes.byref(h)))
+        return Chain(self, h)
+
     def close(self):
         if self.ctx:
             self._lib.p0_destroy(self.ctx)
@@ -171,3 +182,23 @@ def createGpu(device=0):
 
 def version():
     return L.load().p0_version().decode()
+
+
+class Chain:
+    """a recorded sequence of gemv / gemvM calls (p0_chain_*): run() enqueues them as one persistent kernel where they fit"""
+
+    def __init__(self, g, h):
+        self.g, self.h = g, h
+
+    def run(self):
+        self.g._check(self.g._lib.p0_chain_run(self.g.ctx, self.h))
+
+    def info(self):
+        v = [ctypes.c_uint32() for _ in range(4)]
+        self.g._check(self.g._lib.p0_chain_info(self.g.ctx, self.h, *[ctypes.byref(x) for x in v]))
+        return dict(zip(("calls", "kernel_calls", "launches", "barriers"), (x.value for x in v)))
+
+    def free(self):
+        if self.h:
+            self.g._lib.p0_chain_free(self.g.ctx, self.h)
+            self.h = None
