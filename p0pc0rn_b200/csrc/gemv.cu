@@ -616,11 +616,12 @@ p0_status gemv_dispatch(p0_ctx *c, const char *op, const GemvParams &p, uint32_t
     return p0_launched(c, op);
   }
   const bool v3fit = v3_fits(M, K, nsplit, N / 64, c->sm_count);
+  const bool v3sfit = v3_split_fits(M, K, nsplit, N / 64, c->sm_count, epi == P0_EPI_GEGLU);
   const bool v5fit = v5_plan(p, nsplit, c->sm_count, &p5);
   const bool v4fit = v4_plan(p, nsplit, c->sm_count, &pl, &scratch_bytes);
   bool v3ok, v4ok, v5ok;
   if (pick) {
-    v3ok = pick == 3 && v3fit;
+    v3ok = pick == 3 && (v3fit || v3sfit);
     v4ok = pick == 4 && v4fit;
     v5ok = pick == 5 && v5fit;
   } else {
@@ -628,8 +629,11 @@ p0_status gemv_dispatch(p0_ctx *c, const char *op, const GemvParams &p, uint32_t
     // 2 / 4 / 8 ranks (2048 / 1024 / 512 tiles at K = 2048): at M >= 2 the cluster kernel loses once its units pass two
     // per SM (1024 tiles, M = 4: 68.9 us against v2's 41.2), and from 2048 tiles on the stream-K kernel is the fastest
     // at every M (M = 1: 51.5 us against 90.7)
+    // and for the column-split head shapes (2048 / 1024 / 512 tiles at K = 2048), v3 with tiles cut into k-parts: at
+    // 2048 tiles 50.4 / 50.2 / 49.8 / 57.7 us against stream-K's 51.2 / 55.2 / 62.6 / 70.0 at M = 1 / 2 / 4 / 8; at
+    // 1024 and 512 tiles ahead from M = 2 on (33.4 against 42.1 us at 1024 tiles, M = 2), behind the cluster kernel at M = 1
     const uint32_t ntile_all = N / 64;
-    v3ok = v3fit;
+    v3ok = v3fit || (v3sfit && (M >= 2 || ntile_all >= 2048u));
     v5ok = !v3ok && v5fit && (M == 1 || p.q8 || p5.units <= 2u * (uint32_t)c->sm_count);
     v4ok = !v3ok && !v5ok && v4fit && epi != P0_EPI_GEGLU && ((M >= 5 && pl.R >= 8192u) || ntile_all >= 2048u);
   }

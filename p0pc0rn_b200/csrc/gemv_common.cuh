@@ -233,6 +233,7 @@ __device__ __forceinline__ void rec8_math(float (&acc)[4][4], const Rec8 &q, con
 
 // the v3 (bulk-copy fed, whole tiles per warp) kernels, in gemv_v3.cu
 bool v3_fits(uint32_t M, uint32_t K, uint32_t nsplit, uint32_t ntile, int sms);
+bool v3_split_fits(uint32_t M, uint32_t K, uint32_t nsplit, uint32_t ntile, int sms, bool pair);
 cudaError_t launch_v3(const GemvParams &p, int sms, cudaStream_t s);
 
 // the v4 (stream-K) kernels, in gemv_v4.cu

@@ -1,4 +1,6 @@
 // gemv_v3.cu -- the bulk-copy fed tensor-core GEMV (see the v3 notes below) and its launcher.
+#include <cstdlib>
+
 #include "gemv_common.cuh"
 
 namespace p0gemv {
@@ -73,7 +75,10 @@ __device__ float stage_x_v3(const GemvParams &p, uint32_t G, uint4 *xb, float *x
 }
 
 template <int MT, bool PAIR>
-__global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, const uint32_t gx, const uint32_t nslot) {
+// S > 1 (calls with fewer tiles than warps, e.g. a column-split head on several GPUs): each tile is cut into S k-parts
+// (runs of stages), and the parts are the units dealt to the warps; a warp writes its part's row totals to shared memory
+// and, after the CTA's barrier, the warps sum each tile's parts in part order and run the epilogue.
+__global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, const uint32_t gx, const uint32_t nslot, const uint32_t S) {
   constexpr bool PACK = MT <= 4;
   constexpr int NP = PAIR ? 2 : 1;
   extern __shared__ __align__(128) uint8_t smem8[];
@@ -84,6 +89,7 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
   uint4 *xb = reinterpret_cast<uint4 *>(scratch + 32);                                // [G][MT][4][2]
   const uint32_t G = p.K / 32;
   float *xsum = reinterpret_cast<float *>(xb + (size_t)G * MT * 8);                   // [G][MT]
+  float *pbuf = xsum + (size_t)G * MT;                                                // S > 1: [unit][lane][16] totals
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t g = lane >> 2, c = lane & 3;
   const uint32_t ntile = p.N / 64, spt = PAIR ? G : (G + 1) / 2;   // stages per tile
@@ -91,9 +97,15 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
   // CTA b owns the contiguous tiles [b*ntile/gx, (b+1)*ntile/gx) (27 or 28 of the head's 4096 on 148 SMs), dealt to its
   // warps round-robin: every SM gets the same share of the work
   const uint32_t T0 = (uint32_t)((uint64_t)blockIdx.x * ntile / gx), T1 = (uint32_t)((uint64_t)(blockIdx.x + 1u) * ntile / gx);
-  const uint32_t unit0 = T0 + warp, ustride = kV3Warps;
-  const uint32_t nunits = unit0 < T1 ? (T1 - unit0 + ustride - 1) / ustride : 0;
-  const uint32_t nstage = nunits * spt;
+  // units: (tile, part) for the CTA's tiles, part-minor; part k of a tile runs stages [k*spt/S, (k+1)*spt/S)
+  const uint32_t U0 = T0 * S, U1 = T1 * S;
+  const uint32_t unit0 = U0 + warp, ustride = kV3Warps;
+  const uint32_t nunits = unit0 < U1 ? (U1 - unit0 + ustride - 1) / ustride : 0;
+  uint32_t nstage = 0;
+  for (uint32_t k = 0; k < nunits; k++) {
+    const uint32_t part = (unit0 + k * ustride) % S;
+    nstage += (part + 1u) * spt / S - part * spt / S;
+  }
   uint8_t *myring = ring + (size_t)warp * nslot * kV3Slot;
   uint64_t *myfull = full + warp * kV3MaxSlots;
   if (lane == 0) {
@@ -102,10 +114,16 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
   }
   if (threadIdx.x == 0) *abort_flag = 0u;
   __syncwarp();
-  // the issue side: next stage (tile index ni_t, stage ni_s in it), counted incrementally (lane 0 only uses it)
-  uint32_t ni_t = 0, ni_s = 0, issued = 0;
-  const uint8_t *ni_src = p.W + (size_t)unit0 * tile_bytes;
-  const size_t ustride_bytes = (size_t)ustride * tile_bytes;
+  // the issue side: next stage ni_s (of the tile) of the warp's unit ni_k, which ends at stage ni_e (lane 0 only)
+  uint32_t ni_k = 0, ni_s = 0, ni_e = 0, issued = 0;
+  const uint8_t *ni_src = p.W;
+  auto unit_begin = [&](uint32_t k) {
+    const uint32_t u = unit0 + k * ustride, part = u % S;
+    ni_src = p.W + (size_t)(u / S) * tile_bytes;
+    ni_s = part * spt / S;
+    ni_e = (part + 1u) * spt / S;
+  };
+  if (nunits) unit_begin(0);
   auto issue_next = [&](uint32_t slot) {
     uint8_t *dst = myring + (size_t)slot * kV3Slot;
     if (PAIR) {
@@ -118,7 +136,7 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
       bulk_g2s(dst, ni_src + (size_t)ni_s * 2560u, bytes, &myfull[slot]);
     }
     issued++;
-    if (++ni_s == spt) { ni_s = 0; ni_t++; ni_src += ustride_bytes; }
+    if (++ni_s == ni_e && ++ni_k < nunits) unit_begin(ni_k);
   };
   // the first copies fly while x is staged (and, when the weights are static, while the call ahead finishes)
   if (!p.overlap) pdl_wait();
@@ -136,8 +154,52 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
   const uint32_t xb_lane = xb_s + btok * 128u + c * 32u + bsel * 16u, xs_addr = xsum_s + 2u * c * 4u;
   uint32_t cs = 0, cph = 0, consumed = 0;   // consumed slot and its phase; slots consumed so far
   bool ok = true;
+  // ---- epilogue of a tile from its row totals (same contract as v2); PACK: lanes c < 2 hold the tokens
+  auto tile_epilogue = [&](const uint32_t tile, const float (&tot)[NP][4][4]) {
+    const uint32_t R0 = tile * 64, tk0 = 2u * c, tk1 = 2u * c + 1u;
+    if (p.epi == P0_EPI_SOFTCAP) {
+      float bv0 = -INFINITY, bv1 = -INFINITY;
+      uint32_t bi0 = 0xffffffffu, bi1 = 0xffffffffu;
+#pragma unroll
+      for (int r = 0; r < 4; r++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const uint32_t n = R0 + 16 * r + g + (i >= 2 ? 8 : 0), m = (i & 1) ? tk1 : tk0;
+          const float v = __fmul_rn(p.cap, tanhf(fminf(15.0f, fmaxf(-15.0f, __fdiv_rn(tot[0][r][i], p.cap)))));
+          if (m < MT) p.Y[(size_t)m * p.ldm + n] = v;
+          const uint32_t rr = n & 63u;
+          if (i & 1) { if (v > bv1 || (v == bv1 && rr < bi1)) { bv1 = v; bi1 = rr; } }
+          else { if (v > bv0 || (v == bv0 && rr < bi0)) { bv0 = v; bi0 = rr; } }
+        }
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, bv0, o);
+        uint32_t oi = __shfl_xor_sync(0xffffffffu, bi0, o);
+        if (ov > bv0 || (ov == bv0 && oi < bi0)) { bv0 = ov; bi0 = oi; }
+        ov = __shfl_xor_sync(0xffffffffu, bv1, o);
+        oi = __shfl_xor_sync(0xffffffffu, bi1, o);
+        if (ov > bv1 || (ov == bv1 && oi < bi1)) { bv1 = ov; bi1 = oi; }
+      }
+      if (g == 0) {
+        if (tk0 < MT) { const size_t o = ((size_t)tk0 * p.ntile + tile) * 2; p.MX[o] = bv0; p.MX[o + 1] = __uint_as_float(tile * 64 + bi0); }
+        if (tk1 < MT) { const size_t o = ((size_t)tk1 * p.ntile + tile) * 2; p.MX[o] = bv1; p.MX[o + 1] = __uint_as_float(tile * 64 + bi1); }
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < 4; r++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const uint32_t n = R0 + 16 * r + g + (i >= 2 ? 8 : 0), m = (i & 1) ? tk1 : tk0;
+          if (m >= MT) continue;
+          float v = tot[0][r][i];
+          if (PAIR) v = __fmul_rn(gelu_l(v), tot[NP - 1][r][i]);
+          p.Y[(size_t)m * p.ldm + n] = v;
+        }
+    }
+  };
   for (uint32_t ui = 0; ui < nunits && ok; ui++) {
-    const uint32_t tile = unit0 + ui * ustride;
+    const uint32_t u = unit0 + ui * ustride, tile = u / S, part = u % S;
+    const uint32_t st0 = part * spt / S, st1 = (part + 1u) * spt / S;
     float acc[2][NP][4][4];   // [group parity] -> independent FMA chains for the two groups of a slot
 #pragma unroll
     for (int h = 0; h < 2; h++)
@@ -147,7 +209,7 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
         for (int r = 0; r < 4; r++)
 #pragma unroll
           for (int i = 0; i < 4; i++) acc[h][a][r][i] = 0.0f;
-    for (uint32_t st = 0; st < spt; st++) {
+    for (uint32_t st = st0; st < st1; st++) {
       const bool got = tc::mbar_wait(&myfull[cs], cph, abort_flag, p.err, 0x511u, P0_SPIN_LIMIT);
       if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
       consumed++;
@@ -201,46 +263,14 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
           if (PACK) v += __shfl_xor_sync(0xffffffffu, v, 2);
           tot[a][r][i] = v;
         }
-    // ---- epilogue of the tile (same contract as v2); PACK: lanes c < 2 hold the tokens
-    const uint32_t R0 = tile * 64, tk0 = 2u * c, tk1 = 2u * c + 1u;
-    if (p.epi == P0_EPI_SOFTCAP) {
-      float bv0 = -INFINITY, bv1 = -INFINITY;
-      uint32_t bi0 = 0xffffffffu, bi1 = 0xffffffffu;
-#pragma unroll
-      for (int r = 0; r < 4; r++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const uint32_t n = R0 + 16 * r + g + (i >= 2 ? 8 : 0), m = (i & 1) ? tk1 : tk0;
-          const float v = __fmul_rn(p.cap, tanhf(fminf(15.0f, fmaxf(-15.0f, __fdiv_rn(tot[0][r][i], p.cap)))));
-          if (m < MT) p.Y[(size_t)m * p.ldm + n] = v;
-          const uint32_t rr = n & 63u;
-          if (i & 1) { if (v > bv1 || (v == bv1 && rr < bi1)) { bv1 = v; bi1 = rr; } }
-          else { if (v > bv0 || (v == bv0 && rr < bi0)) { bv0 = v; bi0 = rr; } }
-        }
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, bv0, o);
-        uint32_t oi = __shfl_xor_sync(0xffffffffu, bi0, o);
-        if (ov > bv0 || (ov == bv0 && oi < bi0)) { bv0 = ov; bi0 = oi; }
-        ov = __shfl_xor_sync(0xffffffffu, bv1, o);
-        oi = __shfl_xor_sync(0xffffffffu, bi1, o);
-        if (ov > bv1 || (ov == bv1 && oi < bi1)) { bv1 = ov; bi1 = oi; }
-      }
-      if (g == 0) {
-        if (tk0 < MT) { const size_t o = ((size_t)tk0 * p.ntile + tile) * 2; p.MX[o] = bv0; p.MX[o + 1] = __uint_as_float(tile * 64 + bi0); }
-        if (tk1 < MT) { const size_t o = ((size_t)tk1 * p.ntile + tile) * 2; p.MX[o] = bv1; p.MX[o + 1] = __uint_as_float(tile * 64 + bi1); }
-      }
+    if (S == 1) {
+      tile_epilogue(tile, tot);
     } else {
+      float *pb = pbuf + ((size_t)(u - U0) * 32u + lane) * 16u;
 #pragma unroll
       for (int r = 0; r < 4; r++)
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const uint32_t n = R0 + 16 * r + g + (i >= 2 ? 8 : 0), m = (i & 1) ? tk1 : tk0;
-          if (m >= MT) continue;
-          float v = tot[0][r][i];
-          if (PAIR) v = __fmul_rn(gelu_l(v), tot[NP - 1][r][i]);
-          p.Y[(size_t)m * p.ldm + n] = v;
-        }
+        for (int i = 0; i < 4; i++) pb[r * 4 + i] = tot[0][r][i];
     }
   }
   // copies this warp issued but did not consume (only after a failed wait) land before the CTA exits (bounded)
@@ -252,9 +282,29 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
       if (++slot == nslot) { slot = 0; ph ^= 1u; }
     }
   }
+  if (S > 1) {
+    // every part is in shared memory: each tile's parts summed in part order, then its epilogue (warps take tiles
+    // round-robin). After a failed wait the results are void (the error word reports it), the stores still bounded.
+    __syncthreads();
+    for (uint32_t tile = T0 + warp; tile < T1; tile += kV3Warps) {
+      float tot[NP][4][4];
+#pragma unroll
+      for (int r = 0; r < 4; r++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) tot[0][r][i] = 0.0f;
+      for (uint32_t k = 0; k < S; k++) {
+        const float *pb = pbuf + ((size_t)((tile - T0) * S + k) * 32u + lane) * 16u;
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+#pragma unroll
+          for (int i = 0; i < 4; i++) tot[0][r][i] += pb[r * 4 + i];
+      }
+      tile_epilogue(tile, tot);
+    }
+  }
 }
 
-typedef void (*V3Kernel)(const GemvParams, const uint32_t, const uint32_t);
+typedef void (*V3Kernel)(const GemvParams, const uint32_t, const uint32_t, const uint32_t);
 template <int MT>
 V3Kernel v3_kernel_m(bool pair) { return pair ? gemv_q4_v3<MT, true> : gemv_q4_v3<MT, false>; }
 V3Kernel v3_kernel_for(uint32_t M, bool pair) {
@@ -279,20 +329,55 @@ uint32_t v3_slots(uint32_t M, uint32_t G) {
 }
 }  // namespace
 
-// v3: one split, enough tiles to give every warp of every SM a tile, shared memory for a ring of >= 2 slots
+// the parts per tile: 1 when every warp of the grid gets whole tiles (or for geglu pairs); else enough parts for about
+// 27 units per CTA (whole-tile v3 runs the head at 27-28 tiles per CTA), at most 8 and at most a part per stage
+uint32_t v3_parts(uint32_t K, uint32_t ntile, int sms, bool pair) {
+  const uint32_t spt = (K / 32 + 1) / 2;
+  // tuning override, read on every call: P0MM_V3_PARTS=n (1..8) cuts every non-geglu v3 call's tiles into n parts
+  const char *ov = getenv("P0MM_V3_PARTS");
+  const long nov = ov ? strtol(ov, nullptr, 10) : 0;
+  if (!pair && nov >= 1 && nov <= 8) return (uint32_t)nov < spt ? (uint32_t)nov : spt;
+  if (pair || ntile >= (uint32_t)sms * kV3Warps) return 1;
+  uint32_t S = ((uint32_t)sms * 27u + ntile - 1) / ntile;
+  if (S > 8) S = 8;
+  if (S > spt) S = spt;
+  return S < 1 ? 1 : S;
+}
+size_t v3_pbuf(uint32_t ntile, int sms, uint32_t S) {
+  if (S == 1) return 0;
+  const uint32_t gx = ntile < (uint32_t)sms ? ntile : (uint32_t)sms;
+  return (size_t)((ntile + gx - 1) / gx) * S * 32u * 16u * 4u;
+}
+uint32_t v3_slots_with(uint32_t M, uint32_t G, size_t extra) {
+  for (uint32_t n = kV3MaxSlots; n >= 2; n--)
+    if (v3_smem(M, G, n) + extra <= 220u * 1024u) return n;
+  return 0;
+}
+
+// v3: one split and a ring of >= 2 slots; whole tiles per warp when there are enough tiles for every warp of every SM,
+// else (not geglu, at least one tile per SM) tiles cut into k-parts
 bool v3_fits(uint32_t M, uint32_t K, uint32_t nsplit, uint32_t ntile, int sms) {
   return nsplit == 1 && v3_slots(M, K / 32) >= 2 && ntile >= (uint32_t)sms * kV3Warps;
+}
+bool v3_split_fits(uint32_t M, uint32_t K, uint32_t nsplit, uint32_t ntile, int sms, bool pair) {
+  if (nsplit != 1 || pair || ntile < (uint32_t)sms || ntile >= (uint32_t)sms * kV3Warps) return false;
+  const uint32_t S = v3_parts(K, ntile, sms, pair);
+  return S > 1 && v3_slots_with(M, K / 32, v3_pbuf(ntile, sms, S)) >= 2;
 }
 cudaError_t launch_v3(const GemvParams &p, int sms, cudaStream_t s) {
   const bool pair = p.epi == P0_EPI_GEGLU;
   V3Kernel k = v3_kernel_for(p.M, pair);
-  const uint32_t G = p.K / 32, nslot = v3_slots(p.M, G);
-  const size_t smem = v3_smem(p.M, G, nslot);
+  const uint32_t G = p.K / 32, ntile = p.N / 64;
+  uint32_t S = v3_parts(p.K, ntile, sms, pair);
+  if (S > 1 && v3_slots_with(p.M, G, v3_pbuf(ntile, sms, S)) < 2) S = 1;   // the parts' totals do not fit beside a ring
+  const size_t pb = v3_pbuf(ntile, sms, S);
+  const uint32_t nslot = v3_slots_with(p.M, G, pb);
+  const size_t smem = v3_smem(p.M, G, nslot) + pb;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  const uint32_t ntile = p.N / 64, need = (ntile + kV3Warps - 1) / kV3Warps;
+  const uint32_t need = S == 1 ? (ntile + kV3Warps - 1) / kV3Warps : ntile;
   uint32_t gx = (uint32_t)sms;
   if (gx > need) gx = need;
-  return launch_pdl(k, dim3(gx), dim3(kV3Threads), smem, s, 1, p, gx, nslot);
+  return launch_pdl(k, dim3(gx), dim3(kV3Threads), smem, s, 1, p, gx, nslot, S);
 }
 
 
