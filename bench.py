@@ -418,6 +418,7 @@ def run_ours(args, ws, rank, local):
     config1 = run_config1(g, torch, stream) if rank == 0 else None
     gemm = run_gemm_secondary(args, g, torch, ws, rank, dist)
     decode = run_decode_chain(args, g, torch, stream, dist, ws, rank)
+    decode_step = run_decode_step(args, g, torch, stream) if rank == 0 else None
     res = None
     if rank == 0:
         hbm, tfl, src = peaks()
@@ -442,7 +443,7 @@ def run_ours(args, ws, rank, local):
                          "timing": "event record nodes around this rank's 4 head calls inside every timed step graph; achieved = "
                                    "the head calls' algorithmic bytes / the group's device time", "peak_source": src},
             "e2e": e2e, "gpu_launches": len(sw.calls) * args.steps, "clocks": clocks, "rank_ms": [round(v, 4) for v in rank_ms],
-            "config1": config1, "gemm": gemm, "calls_us": calls_us, "decode": decode,
+            "config1": config1, "gemm": gemm, "calls_us": calls_us, "decode": decode, "decode_step": decode_step,
         }
         res["cpu_baseline"] = cpu_baseline(args) if ws == 1 else None
     if dist:
@@ -761,6 +762,85 @@ def run_decode_chain(args, g, torch, stream, dist=None, ws=1, rank=0):
             "parallelism": "one GPU" if ws == 1 else "FFN and head tensor-parallel x%d (NCCL all-gather of the down partials "
                            "and of the head's max/argmax pairs), QKV and O on every rank" % ws,
             "launch": "one CUDA graph per pass"}
+
+
+# ------------------------------------------------------------------------------------------ whole decode token (secondary)
+def run_decode_step(args, g, torch, stream, ctx_len=1024):
+    """One whole decode token of a random-init Gemma-4-style decoder with config 5's matmul shapes (hidden 2048, 26
+    layers of QKV 2560x2048 / O 2048x2048 / GeGLU 2x8192x2048 / down 2048x8192, the tied 262144x2048 head), 8 query heads
+    of 256 over one KV head, every fifth layer full attention and the others a 512-position sliding window, at position
+    ctx_len - 1 with the caches holding ctx_len (full) or 512 (sliding) earlier keys: p0pc0rn_b200.decode.decode_token
+    (gemma4.js encodeStep without the per-layer embeddings) = embed, per layer QKV -> qkrope -> attnDec -> O -> normadd
+    -> GeGLU -> down -> normadd, then the softcap head and argmax, all library kernels, one CUDA graph per token."""
+    import p0pc0rn_b200 as p0
+    from p0pc0rn_b200 import decode
+    cfg = {"D": CHAIN_D, "layers": CHAIN_LAYERS, "NH": 8, "NKV": 1, "hd": 256, "FF": CHAIN_FF, "vocab": HEAD_N, "window": 512,
+           "kinds": ["full" if l % 5 == 4 else "sliding" for l in range(CHAIN_LAYERS)], "embed_scale": 45.254834, "softcap": 30.0,
+           "eps": 1e-6}
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev)
+    sz = decode.model_sizes(cfg)
+
+    def packed(shape, seed):
+        gen.manual_seed(seed)
+        wf = torch.randn(shape[0], shape[1], generator=gen, device=dev) * 0.02
+        wb = g.wrap(wf.data_ptr(), wf.numel() * 4, "wf")
+        q = p0.pack_q4(g, wb, shape[0], shape[1])
+        g.done()
+        g.free(wb)
+        del wf
+        return q
+
+    rng = np.random.default_rng(9)
+    vec = lambda n: g.upload((1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32))
+    ang = rng.uniform(0, 6.283, ctx_len * 128)
+    rope = np.zeros(2 * ctx_len * 128, np.float32)
+    rope[0::2], rope[1::2] = np.cos(ang), np.sin(ang)
+    rb = g.upload(rope)
+    m = {"embed": packed(sz["head"], 8000), "final_norm": vec(CHAIN_D), "rope": {"full": rb, "sliding": rb}, "layers": []}
+    for l in range(CHAIN_LAYERS):
+        m["layers"].append({"qkv": packed(sz["qkv"], 8100 + 4 * l), "o": packed(sz["o"], 8101 + 4 * l), "gu": packed(sz["gu"], 8102 + 4 * l),
+                            "down": packed(sz["down"], 8103 + 4 * l), "in_norm": vec(CHAIN_D), "qk_norm": vec(512), "post_attn": vec(CHAIN_D),
+                            "pre_ff": vec(CHAIN_D), "post_ff": vec(CHAIN_D)})
+    s = decode.DecodeState(g, cfg, ctx_len)
+    kv = []
+    for c in s.caches:   # earlier keys and values: random fp16
+        for k in ("kc", "vc"):
+            t = (torch.randn(c["len"] * 256, generator=gen, device=dev) * 0.5).half()
+            g.copy(g.wrap(t.data_ptr(), t.numel() * 2, "kv"), 0, c[k], 0, t.numel() * 2)
+            kv.append(t)
+    g.write(s.b["ids"], np.array([1234, 0, 0, 0], np.uint32))
+    pos = ctx_len - 1
+    nk = decode.decode_token(g, m, s, pos)
+    g.done()
+    gr = capture(torch, stream, lambda: decode.decode_token(g, m, s, pos))
+    for _ in range(3):
+        gr.replay()
+    reps = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    arg = g.read(s.b["arg"], 0, 8, np.uint32)
+    del gr
+    wbytes = (CHAIN_LAYERS * (sum(a * b for a, b in (sz["qkv"], sz["o"], sz["gu"], sz["down"]))) + HEAD_N * CHAIN_D) * 0.625
+    kvbytes = sum(2 * min(c["len"], pos + 1) * 256 * 2 for c in s.caches)
+    hbm, _, _ = peaks()
+    for b in list(s.b.values()) + [c[k] for c in s.caches for k in ("kc", "vc")]:
+        g.free(b)
+    for L in m["layers"]:
+        for b in L.values():
+            g.free(b)
+    g.free(m["embed"])
+    g.free(rb)
+    del kv
+    return {"ms_per_token": round(ms, 4), "tok_s": round(1e3 / ms, 1), "context": ctx_len, "kernels_per_token": nk + 1,
+            "GB_s": round((wbytes + kvbytes) / (ms / 1e3) / 1e9, 1), "frac_of_hbm": round((wbytes + kvbytes) / (ms / 1e3) / 1e9 / hbm, 4),
+            "argmax": int(arg[0]), "weights_GB": round(wbytes / 1e9, 3), "kv_MB": round(kvbytes / 1e6, 2),
+            "note": "whole decode token (embed, 26 x [attention + MLP], head, argmax) through p0pc0rn_b200.decode; one CUDA graph"}
 
 
 # ------------------------------------------------------------------------------------------ GEMM (secondary)

@@ -71,6 +71,8 @@ p0_status p0_upload(p0_ctx *ctx, p0_buf buf, size_t dst_off, const void *src, si
  * buf at dst_off, in 16 MiB chunks through two pinned staging buffers (disk reads overlap the copies). Returns with the
  * last copies in flight on the stream; the staging buffers are reused only after their copies have finished. */
 p0_status p0_upload_file(p0_ctx *ctx, p0_buf buf, uint64_t dst_off, const char *path, uint64_t file_off, uint64_t bytes);
+/* Runner.copy(src, srcOff, dst, dstOff, size) (gpu.js:237): device -> device, ordered on the stream */
+p0_status p0_copy(p0_ctx *ctx, p0_buf src, size_t src_off, p0_buf dst, size_t dst_off, size_t n);
 /* Gpu.read(buf, off, n) -> Gpu._readback (gpu.js:118-140): flushes the stream, then device -> host */
 p0_status p0_read(p0_ctx *ctx, p0_buf buf, size_t off, size_t n, void *dst);
 /* Gpu.free (gpu.js:89-94) */

@@ -25,7 +25,7 @@ EXPORTS = ["p0_init", "p0_destroy", "p0_set_stream", "p0_set_overlap", "p0_last_
            "p0_free", "p0_done", "p0_device_ptr", "p0_gemv", "p0_gemvM", "p0_gemvM_noalloc", "p0_gemm", "p0_pack_q4", "p0_pack_q8",
            "p0_dequant_f16", "p0_version", "p0_argmaxM", "p0_embed", "p0_normadd", "p0_dhead",
            "p0_upload_file", "p0_qkrope", "p0_attn_dec", "p0_wait_selftest",
-           "p0_chain_begin", "p0_chain_end", "p0_chain_run", "p0_chain_info", "p0_chain_free"]
+           "p0_chain_begin", "p0_chain_end", "p0_chain_run", "p0_chain_info", "p0_chain_free", "p0_copy"]
 P0_NOALLOC_SCRATCH_BYTES = 16 << 20   # include/p0mm.h
 P0_OVERLAP_WEIGHTS = 1
 P0_NOALLOC_COUNTER_BYTES = 64 << 10
@@ -135,6 +135,7 @@ def load():
     L.p0_normadd.argtypes = [vp, ctypes.POINTER(p0_normadd_args)]
     L.p0_dhead.argtypes = [vp, ctypes.POINTER(p0_dhead_args)]
     L.p0_wait_selftest.argtypes = [vp, ctypes.c_uint32]
+    L.p0_copy.argtypes = [vp, p0_buf, ctypes.c_size_t, p0_buf, ctypes.c_size_t, ctypes.c_size_t]
     L.p0_chain_begin.argtypes = [vp]
     L.p0_chain_end.argtypes = [vp, ctypes.POINTER(vp)]
     L.p0_chain_run.argtypes = [vp, vp]

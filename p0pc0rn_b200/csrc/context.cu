@@ -183,6 +183,16 @@ p0_status p0_upload(p0_ctx *c, p0_buf b, size_t off, const void *src, size_t n) 
   return p0_cuda(c, cudaMemcpyAsync((void *)r.base, src, n, cudaMemcpyHostToDevice, c->stream), "upload");
 }
 
+p0_status p0_copy(p0_ctx *c, p0_buf src, size_t src_off, p0_buf dst, size_t dst_off, size_t n) {
+  if (!c) return P0_EINVAL;
+  P0Range rs, rd;
+  p0_status st = p0_range(c, src, src_off, n, "copy", "src", &rs);
+  if (st) return st;
+  if ((st = p0_range(c, dst, dst_off, n, "copy", "dst", &rd))) return st;
+  if (!n) return P0_OK;
+  return p0_cuda(c, cudaMemcpyAsync((void *)rd.base, rs.base, n, cudaMemcpyDeviceToDevice, c->stream), "copy");
+}
+
 p0_status p0_read(p0_ctx *c, p0_buf b, size_t off, size_t n, void *dst) {
   if (!c) return P0_EINVAL;
   P0Range r;

@@ -632,8 +632,9 @@ p0_status gemv_dispatch(p0_ctx *c, const char *op, const GemvParams &p, uint32_t
     // and for the column-split head shapes (2048 / 1024 / 512 tiles at K = 2048), v3 with tiles cut into k-parts: at
     // 2048 tiles 50.4 / 50.2 / 49.8 / 57.7 us against stream-K's 51.2 / 55.2 / 62.6 / 70.0 at M = 1 / 2 / 4 / 8; at
     // 1024 and 512 tiles ahead from M = 2 on (33.4 against 42.1 us at 1024 tiles, M = 2), behind the cluster kernel at M = 1
+    // and at 256 tiles (N = 16384, M = 2: 17.5 against 11.1 us)
     const uint32_t ntile_all = N / 64;
-    v3ok = v3fit || (v3sfit && (M >= 2 || ntile_all >= 2048u));
+    v3ok = v3fit || (v3sfit && ntile_all >= 512u && (M >= 2 || ntile_all >= 2048u));
     v5ok = !v3ok && v5fit && (M == 1 || p.q8 || p5.units <= 2u * (uint32_t)c->sm_count);
     v4ok = !v3ok && !v5ok && v4fit && epi != P0_EPI_GEGLU && ((M >= 5 && pl.R >= 8192u) || ntile_all >= 2048u);
   }

@@ -92,6 +92,19 @@ __device__ __forceinline__ float prologue(const GemvParams &p, uint32_t m, uint3
   return __fmul_rn(gelu_l(s), p.EV[p.evOff + m * p.evLd + k]);
 }
 
+// packed f32 pairs (a 64-bit register pair) and the two-lane fused multiply-add of sm_100 (fma.rn.f32x2)
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float &a, float &b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 // a pure function of its operands (not volatile): the scheduler may interleave independent MMAs with other work
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
@@ -162,11 +175,21 @@ __device__ __forceinline__ void rec_math(float (&acc)[4][4], const Rec &q, const
     }
     const __half2 h0 = *reinterpret_cast<const __half2 *>(&q.t[r][0]), h1 = *reinterpret_cast<const __half2 *>(&q.t[r][1]);
     const float s0 = __low2float(h0), m0 = __high2float(h0), s1 = __low2float(h1), m1 = __high2float(h1);
-    acc[r][0] = fmaf(s0, d[0], fmaf(m0, xs0, acc[r][0]));
-    acc[r][2] = fmaf(s1, d[2], fmaf(m1, xs0, acc[r][2]));
-    if (MT > 1) {
-      acc[r][1] = fmaf(s0, d[1], fmaf(m0, xs1, acc[r][1]));
-      acc[r][3] = fmaf(s1, d[3], fmaf(m1, xs1, acc[r][3]));
+    // the same fused multiply-adds, two lanes of f32 per instruction (fma.rn.f32x2: each lane rounds as fmaf does)
+    if (MT == 1) {
+      uint64_t a = pk2(acc[r][0], acc[r][2]);
+      a = ffma2(pk2(m0, m1), pk2(xs0, xs0), a);
+      a = ffma2(pk2(s0, s1), pk2(d[0], d[2]), a);
+      upk2(a, acc[r][0], acc[r][2]);
+    } else {
+      const uint64_t xs = pk2(xs0, xs1);
+      uint64_t a = pk2(acc[r][0], acc[r][1]), b = pk2(acc[r][2], acc[r][3]);
+      a = ffma2(pk2(m0, m0), xs, a);
+      b = ffma2(pk2(m1, m1), xs, b);
+      a = ffma2(pk2(s0, s0), pk2(d[0], d[1]), a);
+      b = ffma2(pk2(s1, s1), pk2(d[2], d[3]), b);
+      upk2(a, acc[r][0], acc[r][1]);
+      upk2(b, acc[r][2], acc[r][3]);
     }
   }
 }

@@ -74,11 +74,12 @@ __device__ float stage_x_v3(const GemvParams &p, uint32_t G, uint4 *xb, float *x
   return f;
 }
 
-template <int MT, bool PAIR>
-// S > 1 (calls with fewer tiles than warps, e.g. a column-split head on several GPUs): each tile is cut into S k-parts
+// SPLIT (calls with fewer tiles than warps, e.g. a column-split head on several GPUs): each tile is cut into S k-parts
 // (runs of stages), and the parts are the units dealt to the warps; a warp writes its part's row totals to shared memory
 // and, after the CTA's barrier, the warps sum each tile's parts in part order and run the epilogue.
-__global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, const uint32_t gx, const uint32_t nslot, const uint32_t S) {
+template <int MT, bool PAIR, bool SPLIT>
+__global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, const uint32_t gx, const uint32_t nslot, const uint32_t S_arg) {
+  const uint32_t S = SPLIT ? S_arg : 1u;   // whole tiles fold every part computation away
   constexpr bool PACK = MT <= 4;
   constexpr int NP = PAIR ? 2 : 1;
   extern __shared__ __align__(128) uint8_t smem8[];
@@ -263,7 +264,7 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
           if (PACK) v += __shfl_xor_sync(0xffffffffu, v, 2);
           tot[a][r][i] = v;
         }
-    if (S == 1) {
+    if (!SPLIT) {
       tile_epilogue(tile, tot);
     } else {
       float *pb = pbuf + ((size_t)(u - U0) * 32u + lane) * 16u;
@@ -282,7 +283,7 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
       if (++slot == nslot) { slot = 0; ph ^= 1u; }
     }
   }
-  if (S > 1) {
+  if (SPLIT) {
     // every part is in shared memory: each tile's parts summed in part order, then its epilogue (warps take tiles
     // round-robin). After a failed wait the results are void (the error word reports it), the stores still bounded.
     __syncthreads();
@@ -306,17 +307,19 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
 
 typedef void (*V3Kernel)(const GemvParams, const uint32_t, const uint32_t, const uint32_t);
 template <int MT>
-V3Kernel v3_kernel_m(bool pair) { return pair ? gemv_q4_v3<MT, true> : gemv_q4_v3<MT, false>; }
-V3Kernel v3_kernel_for(uint32_t M, bool pair) {
+V3Kernel v3_kernel_m(bool pair, bool split) {
+  return pair ? gemv_q4_v3<MT, true, false> : split ? gemv_q4_v3<MT, false, true> : gemv_q4_v3<MT, false, false>;
+}
+V3Kernel v3_kernel_for(uint32_t M, bool pair, bool split) {
   switch (M) {
-    case 1: return v3_kernel_m<1>(pair);
-    case 2: return v3_kernel_m<2>(pair);
-    case 3: return v3_kernel_m<3>(pair);
-    case 4: return v3_kernel_m<4>(pair);
-    case 5: return v3_kernel_m<5>(pair);
-    case 6: return v3_kernel_m<6>(pair);
-    case 7: return v3_kernel_m<7>(pair);
-    default: return v3_kernel_m<8>(pair);
+    case 1: return v3_kernel_m<1>(pair, split);
+    case 2: return v3_kernel_m<2>(pair, split);
+    case 3: return v3_kernel_m<3>(pair, split);
+    case 4: return v3_kernel_m<4>(pair, split);
+    case 5: return v3_kernel_m<5>(pair, split);
+    case 6: return v3_kernel_m<6>(pair, split);
+    case 7: return v3_kernel_m<7>(pair, split);
+    default: return v3_kernel_m<8>(pair, split);
   }
 }
 size_t v3_smem(uint32_t M, uint32_t G, uint32_t nslot) {
@@ -366,10 +369,10 @@ bool v3_split_fits(uint32_t M, uint32_t K, uint32_t nsplit, uint32_t ntile, int 
 }
 cudaError_t launch_v3(const GemvParams &p, int sms, cudaStream_t s) {
   const bool pair = p.epi == P0_EPI_GEGLU;
-  V3Kernel k = v3_kernel_for(p.M, pair);
   const uint32_t G = p.K / 32, ntile = p.N / 64;
   uint32_t S = v3_parts(p.K, ntile, sms, pair);
   if (S > 1 && v3_slots_with(p.M, G, v3_pbuf(ntile, sms, S)) < 2) S = 1;   // the parts' totals do not fit beside a ring
+  V3Kernel k = v3_kernel_for(p.M, pair, S > 1);
   const size_t pb = v3_pbuf(ntile, sms, S);
   const uint32_t nslot = v3_slots_with(p.M, G, pb);
   const size_t smem = v3_smem(p.M, G, nslot) + pb;

@@ -125,6 +125,10 @@ class Gpu:
     def write(self, b, data, dst_off=0):
         return self.upload(data, dst=b, dst_off=dst_off)
 
+    def copy(self, src, src_off, dst, dst_off, size):
+        """Runner.copy (gpu.js:237): device -> device, ordered on the stream"""
+        self._check(self._lib.p0_copy(self.ctx, src.handle, int(src_off), dst.handle, int(dst_off), int(size)))
+
     def read(self, b, off=0, size=None, dtype=np.uint8):
         """read size bytes at off (flushes), returned as a numpy array of dtype"""
         size = b.size - off if size is None else int(size)
