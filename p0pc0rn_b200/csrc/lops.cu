@@ -117,23 +117,28 @@ __global__ void __launch_bounds__(kT) embed_kernel(const uint8_t *__restrict__ W
 // mode 1: x = tv; ST = rsqrt(sum x^2 / D + eps). tv is kept in shared memory between the two passes.
 __global__ void __launch_bounds__(kT) normadd_kernel(const float *__restrict__ T, uint32_t nsrc, uint64_t ldp, const float *__restrict__ Wn,
                                                      float *__restrict__ X, float *__restrict__ ST, uint32_t statOff, uint32_t D,
-                                                     uint32_t mode, float eps, float scale) {
-  extern __shared__ float tv[];
+                                                     uint32_t mode, float eps, float scale, bool pre) {
+  extern __shared__ float tv[];   // [D] summed partials; with pre, then [D] x and [D] w read in the same pass
   __shared__ float red[kT / 32];
   const uint32_t m = blockIdx.x;
   const size_t xb = (size_t)m * D;
+  float *xv = tv + D, *wv = tv + 2 * (size_t)D;
   float s = 0.0f;
   for (uint32_t i = threadIdx.x; i < D; i += kT) {
     float v = 0.0f;
     for (uint32_t j = 0; j < nsrc; j++) v = __fadd_rn(v, T[j * ldp + xb + i]);
+    if (pre) {   // x and w do not depend on the sum: their loads fly with the partials'
+      xv[i] = X[xb + i];
+      if (mode == 0) wv[i] = Wn[i];
+    }
     tv[i] = v;
     s = fmaf(v, v, s);
   }
   const float rs = rsqrtf(__fadd_rn(__fdiv_rn(cta_sum(s, red), (float)D), eps));
   float s2 = 0.0f;
   for (uint32_t i = threadIdx.x; i < D; i += kT) {
-    float x = X[xb + i];
-    if (mode == 0) x = __fmul_rn(__fadd_rn(x, __fmul_rn(__fmul_rn(tv[i], rs), Wn[i])), scale);
+    float x = pre ? xv[i] : X[xb + i];
+    if (mode == 0) x = __fmul_rn(__fadd_rn(x, __fmul_rn(__fmul_rn(tv[i], rs), pre ? wv[i] : Wn[i])), scale);
     else x = tv[i];
     X[xb + i] = x;
     s2 = fmaf(x, x, s2);
@@ -338,14 +343,24 @@ __global__ void __launch_bounds__(kT) attn_chunk_kernel(const float *__restrict_
     PT[pb + threadIdx.x] = mh[threadIdx.x];
     PT[pb + nh + threadIdx.x] = l;
   }
-  for (uint32_t dp = threadIdx.x; dp < D / 2; dp += kT) {
-    float2 acc[8];
+  // P.V: the chunk's V rows of one KV head are first staged in shared memory by every thread at once (16-byte loads, all
+  // in flight together), then a thread per dim pair walks the keys from shared memory
+  __half *vs = reinterpret_cast<__half *>(sc + (size_t)nh * 64u);   // [64][D]
+  float2 acc[8];
 #pragma unroll
-    for (int hh = 0; hh < 8; hh++) acc[hh] = make_float2(0.0f, 0.0f);
-    for (uint32_t k = 0; k < nk; k++) {
+  for (int hh = 0; hh < 8; hh++) acc[hh] = make_float2(0.0f, 0.0f);
+  const uint32_t dpa = threadIdx.x;   // this thread's dim pair (D / 2 <= kT)
+  for (uint32_t g = 0; g < nkv; g++) {
+    __syncthreads();   // the previous head's rows are no longer read
+    for (uint32_t i = threadIdx.x; i < nk * (D / 8u); i += kT) {
+      const uint32_t k = i / (D / 8u), e = i - k * (D / 8u);
       const uint32_t row = ring ? (j0 + k) % ring : j0 + k;
-      for (uint32_t g = 0; g < nkv; g++) {
-        const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(VC + ((size_t)g * kvLen + row) * D + 2u * dp));
+      reinterpret_cast<uint4 *>(vs)[(size_t)k * (D / 8u) + e] = *reinterpret_cast<const uint4 *>(VC + ((size_t)g * kvLen + row) * D + 8u * e);
+    }
+    __syncthreads();
+    if (dpa < D / 2) {
+      for (uint32_t k = 0; k < nk; k++) {
+        const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(vs + (size_t)k * D + 2u * dpa));
 #pragma unroll
         for (int hh = 0; hh < 8; hh++)
           if ((uint32_t)hh >= g * hpg && (uint32_t)hh < (g + 1) * hpg) {
@@ -355,9 +370,11 @@ __global__ void __launch_bounds__(kT) attn_chunk_kernel(const float *__restrict_
           }
       }
     }
+  }
+  if (dpa < D / 2) {
 #pragma unroll
     for (int hh = 0; hh < 8; hh++)
-      if ((uint32_t)hh < nh) *reinterpret_cast<float2 *>(PT + pb + 2u * nh + (size_t)hh * D + 2u * dp) = acc[hh];
+      if ((uint32_t)hh < nh) *reinterpret_cast<float2 *>(PT + pb + 2u * nh + (size_t)hh * D + 2u * dpa) = acc[hh];
   }
 }
 
@@ -444,12 +461,13 @@ p0_status p0_normadd(p0_ctx *c, const p0_normadd_args *a) {
   if ((st = p0_range(c, a->x, 0, (uint64_t)M * D * 4, "normadd", "X", &rx))) return st;
   if ((st = p0_range(c, a->st, 0, ((uint64_t)a->st_off + M) * 4, "normadd", "ST", &rs))) return st;
   const float eps = a->eps != 0.0f ? a->eps : 1e-6f;   // lops.js:177 `a.eps || 1e-6`
-  const size_t smem = (size_t)D * 4;
+  const bool pre = (size_t)D * 12 <= 200u * 1024u;   // room for x and w beside the sum: one pass of loads
+  const size_t smem = (size_t)D * (pre ? 12 : 4);
   cudaSetDevice(c->device);
   // above the 48 KB default the kernel opts in (its static reduction array counts against the same limit)
   if (smem > 40u * 1024u) cudaFuncSetAttribute(normadd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   normadd_kernel<<<M, kT, smem, c->stream>>>((const float *)rt.base, nsrc, ldp, a->mode == 0 ? (const float *)rw.base + a->w_off : nullptr,
-                                             (float *)rx.base, (float *)rs.base, a->st_off, D, a->mode, eps, a->scale);
+                                             (float *)rx.base, (float *)rs.base, a->st_off, D, a->mode, eps, a->scale, pre);
   return p0_launched(c, "normadd");
 }
 
@@ -530,9 +548,10 @@ p0_status p0_attn_dec(p0_ctx *c, const p0_attn_dec_args *a) {
   if ((st = p0_range(c, a->vc, 0, (uint64_t)nkv * rows * D * 2, "attnDec", "VC", &rv))) return st;
   if ((st = p0_range(c, a->part, 0, (uint64_t)nchunk * nh * (2 + D) * 4, "attnDec", "part", &rp))) return st;
   if ((st = p0_range(c, a->out, 0, (uint64_t)nh * D * 4, "attnDec", "O", &ro))) return st;
-  const size_t smem = ((size_t)nh * D + (size_t)nh * 64) * 4;
+  const size_t smem = ((size_t)nh * D + (size_t)nh * 64) * 4 + (size_t)64 * D * 2;   // q | scores | a chunk's V rows
   cudaSetDevice(c->device);
   auto go = [&](auto kern) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     kern<<<nchunk, kT, smem, c->stream>>>((const float *)rq.base, (const __half *)rk.base, (const __half *)rv.base, (float *)rp.base, D, nh, nkv,
                                           rows, a->kStart, a->kEnd, a->ring);
   };
