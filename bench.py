@@ -32,7 +32,7 @@ MS = (1, 2, 4, 8)
 NS = (2048, 16384, 262144)
 HEAD_N = 262144
 # DRAM bytes (read + write) of one head GEMV launch (N = 262144, K = 2048, M = 1) from an ncu capture
-HEAD_TRAFFIC = 340.45e6
+HEAD_TRAFFIC = 340.01e6
 
 
 def gemv_bytes(M, N, K, head):
@@ -437,7 +437,7 @@ def run_ours(args, ws, rank, local):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "traffic": HEAD_TRAFFIC * (1.0 / ws) if ws in (1, 2, 4, 8) else None,
                          "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one head launch at M=1 (N=262144) from an ncu "
-                                         "capture (335.7 + 4.7 MB; algorithmic 336.6 MB), scaled by this rank's rows at N>1",
+                                         "capture (335.63 + 4.38 MB; algorithmic 336.6 MB), scaled by this rank's rows at N>1",
                          "kernel": "gemv head (rms+softcap) N=%d/rank K=%d, M=1/2/4/8" % (HEAD_N // ws, K),
                          "launch_us": round(head_launch_us, 2), "launches_timed": len(used) * len(heads),
                          "timing": "event record nodes around this rank's 4 head calls inside every timed step graph; achieved = "
@@ -837,7 +837,7 @@ def run_decode_step(args, g, torch, stream, ctx_len=1024):
     g.free(m["embed"])
     g.free(rb)
     del kv
-    return {"ms_per_token": round(ms, 4), "tok_s": round(1e3 / ms, 1), "context": ctx_len, "kernels_per_token": nk + 1,
+    return {"ms_per_token": round(ms, 4), "tok_s": round(1e3 / ms, 1), "context": ctx_len, "kernels_per_token": nk,
             "GB_s": round((wbytes + kvbytes) / (ms / 1e3) / 1e9, 1), "frac_of_hbm": round((wbytes + kvbytes) / (ms / 1e3) / 1e9 / hbm, 4),
             "argmax": int(arg[0]), "weights_GB": round(wbytes / 1e9, 3), "kv_MB": round(kvbytes / 1e6, 2),
             "note": "whole decode token (embed, 26 x [attention + MLP], head, argmax) through p0pc0rn_b200.decode; one CUDA graph"}
@@ -992,7 +992,9 @@ def run_case(args):
     """One operator on cuda:0: one warm launch, then `--reps` launches timed with CUDA events (the small cases ncu
     captures; back-to-back launches, so a weight matrix below the L2 size is partly L2-resident).
       --case gemv  --M 1 --N 262144 --K 2048 [--head]   (head: rms prologue + softcap epilogue, as the engine's head)
-      --case gemm  --M 4096 --N 9216 --K 3072 [--gelu]  (bias epilogue)"""
+      --case gemm  --M 4096 --N 9216 --K 3072 [--gelu]  (bias epilogue)
+      --case step                                       (one whole decode token, as the line's decode_step key)
+      --case chain --M 1                                (config 5 as a recorded chain, as the line's decode key)"""
     import torch
     import p0pc0rn_b200 as p0
     torch.cuda.set_device(0)
@@ -1000,6 +1002,13 @@ def run_case(args):
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     g.set_stream(stream.cuda_stream)
+    if args.case in ("step", "chain"):
+        g.set_overlap(True)
+        args.steps = 40 * args.reps
+        out = run_decode_step(args, g, torch, stream) if args.case == "step" else run_decode_chain(args, g, torch, stream)
+        g.close()
+        print(json.dumps({"case": args.case, "result": out}))
+        return
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1)
@@ -1055,7 +1064,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--case", default=None, choices=["gemv", "gemm"], help="run one operator (for ncu captures)")
+    ap.add_argument("--case", default=None, choices=["gemv", "gemm", "step", "chain"], help="run one operator or pass (for ncu captures)")
     ap.add_argument("--M", type=int, default=1)
     ap.add_argument("--N", type=int, default=262144)
     ap.add_argument("--K", type=int, default=2048)

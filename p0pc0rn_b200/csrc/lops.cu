@@ -12,6 +12,14 @@ namespace {
 
 constexpr int kT = 256;   // threads per CTA
 
+// Programmatic dependent launch: every operator kernel is launched so that it may start while the kernel ahead of it is
+// still running; it waits for that kernel (griddepcontrol.wait: all prerequisite grids complete, their writes visible)
+// before it reads anything, then lets the kernel after it launch at once. Without such a launch both are no-ops.
+__device__ __forceinline__ void dep_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float h2f(uint32_t h16) { return __half2float(__ushort_as_half((unsigned short)(h16 & 0xffffu))); }
 
 // (value, index) pairs: the larger value wins, ties go to the lower index; NaN never wins
@@ -38,6 +46,7 @@ __device__ __forceinline__ float cta_sum(float v, float *red) {
 
 // ---------------------------------------------------------------- argmaxM: one CTA per row of n (max, bitcast index) pairs
 __global__ void __launch_bounds__(kT) argmax_kernel(const float2 *__restrict__ MX, uint32_t n, uint32_t *__restrict__ out) {
+  dep_enter();
   __shared__ float rv[kT / 32];
   __shared__ uint32_t ri[kT / 32];
   const uint32_t m = blockIdx.x;
@@ -65,6 +74,7 @@ template <bool Q8>
 __global__ void __launch_bounds__(kT) embed_kernel(const uint8_t *__restrict__ W, uint32_t V, const uint32_t *__restrict__ ids,
                                                    uint32_t K, uint32_t wG, float scale, float eps, float *__restrict__ X,
                                                    uint32_t rowOut, float *__restrict__ ST, uint32_t statOff) {
+  dep_enter();
   __shared__ float red[kT / 32];
   const uint32_t m = blockIdx.x, id = ids[m];
   const bool in = id < V;
@@ -118,6 +128,7 @@ __global__ void __launch_bounds__(kT) embed_kernel(const uint8_t *__restrict__ W
 __global__ void __launch_bounds__(kT) normadd_kernel(const float *__restrict__ T, uint32_t nsrc, uint64_t ldp, const float *__restrict__ Wn,
                                                      float *__restrict__ X, float *__restrict__ ST, uint32_t statOff, uint32_t D,
                                                      uint32_t mode, float eps, float scale, bool pre) {
+  dep_enter();
   extern __shared__ float tv[];   // [D] summed partials; with pre, then [D] x and [D] w read in the same pass
   __shared__ float red[kT / 32];
   const uint32_t m = blockIdx.x;
@@ -159,6 +170,7 @@ template <bool Q8>
 __global__ void __launch_bounds__(kT) dhead_kernel(const float *__restrict__ X, const uint8_t *__restrict__ W, uint32_t ntile,
                                                    const float *__restrict__ ST, const float *__restrict__ NW, const uint32_t *__restrict__ SEL,
                                                    uint32_t K, uint32_t wG, uint32_t tPer, float *__restrict__ MX) {
+  dep_enter();
   __shared__ float xs[512];
   __shared__ float rv[kT / 32];
   __shared__ uint32_t ri[kT / 32];
@@ -226,6 +238,7 @@ __global__ void __launch_bounds__(kT) qkrope_kernel(const float *__restrict__ S,
                                                     __half *__restrict__ VC, uint32_t D, uint32_t nq, uint32_t nkv, uint32_t pos, float eps,
                                                     uint32_t qwOff, uint32_t kwOff, uint32_t npairs, uint32_t ropeOff, uint32_t kvRow,
                                                     uint32_t kvLen) {
+  dep_enter();
   extern __shared__ float hv[];
   __shared__ float red[kT / 32];
   const uint32_t h = blockIdx.x, half = D / 2;
@@ -275,6 +288,7 @@ template <int DV>
 __global__ void __launch_bounds__(kT) attn_chunk_kernel(const float *__restrict__ Q, const __half *__restrict__ KC,
                                                         const __half *__restrict__ VC, float *__restrict__ PT, uint32_t D, uint32_t nh,
                                                         uint32_t nkv, uint32_t kvLen, uint32_t kStart, uint32_t kEnd, uint32_t ring) {
+  dep_enter();
   extern __shared__ float sm[];
   float *qs = sm, *sc = sm + (size_t)nh * D;   // q [nh][D] | scores [nh][64]
   __shared__ float mh[8];
@@ -381,6 +395,7 @@ __global__ void __launch_bounds__(kT) attn_chunk_kernel(const float *__restrict_
 // the chunks' merge, one CTA per head: M = max m_c, w_c = exp(m_c - M) / sum_c exp(m_c - M) l_c, O = sum_c w_c acc_c
 __global__ void __launch_bounds__(kT) attn_combine_kernel(const float *__restrict__ PT, float *__restrict__ O, uint32_t D, uint32_t nh,
                                                           uint32_t nchunk) {
+  dep_enter();
   __shared__ float wts[256];
   const uint32_t h = blockIdx.x;
   const size_t st = (size_t)nh * (2u + D);
@@ -403,6 +418,22 @@ __global__ void __launch_bounds__(kT) attn_combine_kernel(const float *__restric
   }
 }
 
+
+// a kernel launch that lets the kernel start before the one ahead of it on the stream finishes (see dep_enter)
+template <typename Kern, typename... Args>
+cudaError_t launch_dep(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
 }  // namespace
 
 extern "C" {
@@ -416,7 +447,7 @@ p0_status p0_argmaxM(p0_ctx *c, p0_buf mx, uint32_t n, uint32_t M, p0_buf out) {
   if ((st = p0_range(c, mx, 0, (uint64_t)M * n * 8, "argmax", "MX", &rm))) return st;
   if ((st = p0_range(c, out, 0, (uint64_t)M * 8, "argmax", "OUT", &ro))) return st;
   cudaSetDevice(c->device);
-  argmax_kernel<<<M, kT, 0, c->stream>>>((const float2 *)rm.base, n, (uint32_t *)ro.base);
+  launch_dep(argmax_kernel, dim3(M), dim3(kT), 0, c->stream, (const float2 *)rm.base, n, (uint32_t *)ro.base);
   return p0_launched(c, "argmax");
 }
 
@@ -439,10 +470,10 @@ p0_status p0_embed(p0_ctx *c, const p0_embed_args *a) {
   const float eps = a->eps != 0.0f ? a->eps : 1e-6f;   // lops.js:364 `a.eps || 1e-6`
   cudaSetDevice(c->device);
   if (q8)
-    embed_kernel<true><<<a->n, kT, 0, c->stream>>>(rw.base, a->w.rows, (const uint32_t *)ri.base, K, wG, a->scale, eps, (float *)rx.base,
+    launch_dep(embed_kernel<true>, dim3(a->n), dim3(kT), 0, c->stream, rw.base, a->w.rows, (const uint32_t *)ri.base, K, wG, a->scale, eps, (float *)rx.base,
                                                     a->rowOut, (float *)rs.base, a->st_off);
   else
-    embed_kernel<false><<<a->n, kT, 0, c->stream>>>(rw.base, a->w.rows, (const uint32_t *)ri.base, K, wG, a->scale, eps, (float *)rx.base,
+    launch_dep(embed_kernel<false>, dim3(a->n), dim3(kT), 0, c->stream, rw.base, a->w.rows, (const uint32_t *)ri.base, K, wG, a->scale, eps, (float *)rx.base,
                                                      a->rowOut, (float *)rs.base, a->st_off);
   return p0_launched(c, "embed");
 }
@@ -466,7 +497,7 @@ p0_status p0_normadd(p0_ctx *c, const p0_normadd_args *a) {
   cudaSetDevice(c->device);
   // above the 48 KB default the kernel opts in (its static reduction array counts against the same limit)
   if (smem > 40u * 1024u) cudaFuncSetAttribute(normadd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  normadd_kernel<<<M, kT, smem, c->stream>>>((const float *)rt.base, nsrc, ldp, a->mode == 0 ? (const float *)rw.base + a->w_off : nullptr,
+  launch_dep(normadd_kernel, dim3(M), dim3(kT), smem, c->stream, (const float *)rt.base, nsrc, ldp, a->mode == 0 ? (const float *)rw.base + a->w_off : nullptr,
                                              (float *)rx.base, (float *)rs.base, a->st_off, D, a->mode, eps, a->scale, pre);
   return p0_launched(c, "normadd");
 }
@@ -493,10 +524,10 @@ p0_status p0_dhead(p0_ctx *c, const p0_dhead_args *a) {
   cudaSetDevice(c->device);
   const float *stp = (const float *)rs.base + a->stat_off, *nw = (const float *)rn.base + a->norm_off;
   if (q8)
-    dhead_kernel<true><<<nblk, kT, 0, c->stream>>>((const float *)rx.base, rw.base, a->w.rows / 64, stp, nw, (const uint32_t *)rsel.base, K,
+    launch_dep(dhead_kernel<true>, dim3(nblk), dim3(kT), 0, c->stream, (const float *)rx.base, rw.base, a->w.rows / 64, stp, nw, (const uint32_t *)rsel.base, K,
                                                     wG, a->tPer, (float *)rm.base);
   else
-    dhead_kernel<false><<<nblk, kT, 0, c->stream>>>((const float *)rx.base, rw.base, a->w.rows / 64, stp, nw, (const uint32_t *)rsel.base, K,
+    launch_dep(dhead_kernel<false>, dim3(nblk), dim3(kT), 0, c->stream, (const float *)rx.base, rw.base, a->w.rows / 64, stp, nw, (const uint32_t *)rsel.base, K,
                                                      wG, a->tPer, (float *)rm.base);
   return p0_launched(c, "dhead");
 }
@@ -525,7 +556,7 @@ p0_status p0_qkrope(p0_ctx *c, const p0_qkrope_args *a) {
   const size_t smem = (size_t)D * 4;
   cudaSetDevice(c->device);
   if (smem > 40u * 1024u) cudaFuncSetAttribute(qkrope_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  qkrope_kernel<<<nh, kT, smem, c->stream>>>((const float *)rs.base, nsrc, ldp, (const float *)rn.base, (const float *)rr.base, (float *)rq.base,
+  launch_dep(qkrope_kernel, dim3(nh), dim3(kT), smem, c->stream, (const float *)rs.base, nsrc, ldp, (const float *)rn.base, (const float *)rr.base, (float *)rq.base,
                                              a->hasKV ? (__half *)rk.base : nullptr, a->hasKV ? (__half *)rv.base : nullptr, D, nq, nkv, a->pos,
                                              eps, a->qw, a->kw, a->npairs, a->rope_off, a->kvRow, a->kvLen);
   return p0_launched(c, "qkrope");
@@ -552,7 +583,7 @@ p0_status p0_attn_dec(p0_ctx *c, const p0_attn_dec_args *a) {
   cudaSetDevice(c->device);
   auto go = [&](auto kern) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<nchunk, kT, smem, c->stream>>>((const float *)rq.base, (const __half *)rk.base, (const __half *)rv.base, (float *)rp.base, D, nh, nkv,
+    launch_dep(kern, dim3(nchunk), dim3(kT), smem, c->stream, (const float *)rq.base, (const __half *)rk.base, (const __half *)rv.base, (float *)rp.base, D, nh, nkv,
                                           rows, a->kStart, a->kEnd, a->ring);
   };
   switch (D / 128) {
@@ -562,7 +593,7 @@ p0_status p0_attn_dec(p0_ctx *c, const p0_attn_dec_args *a) {
     default: go(attn_chunk_kernel<4>); break;
   }
   if ((st = p0_launched(c, "attnDec"))) return st;
-  attn_combine_kernel<<<nh, kT, 0, c->stream>>>((const float *)rp.base, (float *)ro.base, D, nh, nchunk);
+  launch_dep(attn_combine_kernel, dim3(nh), dim3(kT), 0, c->stream, (const float *)rp.base, (float *)ro.base, D, nh, nchunk);
   return p0_launched(c, "attnDec combine");
 }
 

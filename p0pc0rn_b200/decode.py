@@ -57,7 +57,7 @@ def decode_token(g, m, s, pos, token_buf=None):
     """enqueue one decode token at position pos (gemma4.js encodeStep). m: the model's device buffers
     {embed, layers: [{qkv, o, gu, down, in_norm, qk_norm (q at 0, k at hd), post_attn, pre_ff, post_ff}], final_norm,
     rope: {full, sliding} (f32 (cos, sin) pairs per position and pair)}; s: a DecodeState. The token id is read from
-    token_buf (a device buffer) or s.b["ids"]. Returns the number of kernels enqueued."""
+    token_buf (a device buffer) or s.b["ids"]. Returns the number of kernels enqueued (the stat copy is not one)."""
     cfg = s.cfg
     D, NH, NKV, hd, FF, V = cfg["D"], cfg["NH"], cfg["NKV"], cfg["hd"], cfg["FF"], cfg["vocab"]
     eps, b = cfg.get("eps", 1e-6), s.b
@@ -91,7 +91,7 @@ def decode_token(g, m, s, pos, token_buf=None):
         ns_d = ops.gemv(g, {"w": wv(L["down"], sz["down"]), "x": {"buf": b["mbuf"]}, "N": D, "K": FF, "kPer": KP, "y": {"buf": b["tpart"]}})
         ops.normadd(g, {"t": {"buf": b["tpart"], "n": ns_d, "ld": D}, "w": {"buf": L["post_ff"], "off": 0}, "x": {"buf": b["x"]},
                         "st": {"buf": b["st"], "off": 1}, "D": D, "eps": eps, "scale": 1.0})
-        n += 7
+        n += 9   # the two gemv projections, qkrope, attnDec's chunk and combine kernels, two gemv MLP calls, two normadds
     # _headWith: the rms prologue of the softcap head reads its rstd from the MX buffer past the tile slots (lops.js:125)
     stoff = V // 64 * 2
     g.copy(b["st"], 4, b["mx"], stoff * 4, 4)

@@ -93,7 +93,7 @@ def test_decode_tokens_match_oracle(g):
     for pos, tok in enumerate(toks):
         g.write(s.b["ids"], np.array([tok, 0, 0, 0], np.uint32))
         n = decode.decode_token(g, m, s, pos)
-        assert n == 1 + 7 * CFG["layers"] + 2
+        assert n == 1 + 9 * CFG["layers"] + 2
         g.done()
         logits = g.read(s.b["logits"], 0, V * 4, np.float32)
         arg = g.read(s.b["arg"], 0, 8, np.uint32)
