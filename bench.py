@@ -178,6 +178,13 @@ class Sweep:
         self.R = max(ring_copies((c["Nfull"] // ws if c["head"] else c["Nfull"]) * K * 5 // 8) for c in plan)
         self.calls, rings = [], {}
         out_floats = 0
+        # every call's gathered output (Y, or the head's MX pairs and its rstd slot) is a slice of one per-rank buffer,
+        # the all-gather's source: the step needs no copies before the collective. All ranks size it alike.
+        per_rank = max(sum((c["M"] * (c["Nfull"] // ws // 64) * 2 + 8) if c["head"] else c["M"] * c["Nfull"]
+                           for c in plan if c["head"] or c["rank"] == r) for r in range(ws))
+        self.gather_src = torch.zeros(per_rank, dtype=torch.float32, device=dev)
+        self.per_rank = per_rank
+        slice_of = lambda off, n, label: g.wrap(self.gather_src.data_ptr() + off * 4, n * 4, label)
         for pc in plan:
             if not (pc["head"] or pc["rank"] == rank):
                 continue
@@ -203,17 +210,17 @@ class Sweep:
             NT = Nr // 64
             c = {"M": M, "N": Nr, "Nfull": N, "head": head, "ring": ring, "i": ring_offset(pc["j"], len(ring)), "x": x, "xb": xb,
                  "bytes": gemv_bytes(M, Nr, K, head), "out_off": out_floats}
-            c["y"] = g.buffer(M * Nr * 4, "y")
             if head:
+                c["y"] = g.buffer(M * Nr * 4, "y")       # the logits stay on the rank; the MX pairs are gathered
                 nw = (1.0 + 0.1 * rng.standard_normal(K)).astype(np.float32)
                 c["nw"] = g.upload(nw, "nw")
-                mx = np.zeros(M * NT * 2 + 8, np.float32)
-                c["mxb"] = g.upload(mx, "mx")
+                c["mxb"] = slice_of(out_floats, M * NT * 2 + 8, "mx")
                 c["st"] = g.upload(np.full(8, 0.9, np.float32), "st")
                 c["stat_off"] = M * NT * 2              # the rstd slot past the tile slots (gemma4.js:504)
                 g.write(c["mxb"], np.full(1, 0.9, np.float32), dst_off=c["stat_off"] * 4)
-                out_floats += M * NT * 2
+                out_floats += M * NT * 2 + 8
             else:
+                c["y"] = slice_of(out_floats, M * Nr, "y")
                 out_floats += M * Nr
             self.calls.append(c)
         self.out_floats = out_floats
@@ -311,12 +318,9 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize()
     # the weights are packed and synchronised: GEMVs may fetch them while the call ahead finishes (p0_set_overlap)
     g.set_overlap(True)
-    # one gather buffer per rank of equal size (ranks own different call sets): every call's outputs of this rank,
-    # concatenated; one all-gather per step
-    per_rank = max(sum((c["M"] * (c["Nfull"] // ws // 64) * 2) if c["head"] else c["M"] * c["Nfull"]
-                       for c in plan_calls(ws) if c["head"] or c["rank"] == r) for r in range(ws))
-    gather_src = torch.zeros(per_rank, dtype=torch.float32, device="cuda")
-    gather_dst = torch.empty(per_rank * ws, dtype=torch.float32, device="cuda")
+    # the all-gather: every rank's output slices (equal sizes) into one buffer per step
+    gather_src = sw.gather_src
+    gather_dst = torch.empty(sw.per_rank * ws, dtype=torch.float32, device="cuda")
     outs = []
     for c in sw.calls:
         buf = c["mxb"] if c["head"] else c["y"]
@@ -324,8 +328,11 @@ def run_ours(args, ws, rank, local):
         outs.append((c["out_off"], n, buf.ptr))
 
     def copies(ptrs=None):
+        """outputs written elsewhere (the e2e loop's second buffer set) into their slices; the first set writes there"""
         for i, (off, n, ptr) in enumerate(outs):
-            _memcpy_d2d(gather_src.data_ptr() + off * 4, ptrs[i] if ptrs else ptr, n * 4, stream.cuda_stream)
+            src = ptrs[i] if ptrs else ptr
+            if src != gather_src.data_ptr() + off * 4:
+                _memcpy_d2d(gather_src.data_ptr() + off * 4, src, n * 4, stream.cuda_stream)
 
     def gather(ptrs=None):
         """every call's outputs of this rank (at ptrs, default the first buffer set) -> one buffer -> one NCCL

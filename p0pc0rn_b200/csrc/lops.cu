@@ -135,6 +135,7 @@ __global__ void __launch_bounds__(kT) normadd_kernel(const float *__restrict__ T
   const size_t xb = (size_t)m * D;
   float *xv = tv + D, *wv = tv + 2 * (size_t)D;
   float s = 0.0f;
+#pragma unroll 8
   for (uint32_t i = threadIdx.x; i < D; i += kT) {
     float v = 0.0f;
     for (uint32_t j = 0; j < nsrc; j++) v = __fadd_rn(v, T[j * ldp + xb + i]);
@@ -147,6 +148,7 @@ __global__ void __launch_bounds__(kT) normadd_kernel(const float *__restrict__ T
   }
   const float rs = rsqrtf(__fadd_rn(__fdiv_rn(cta_sum(s, red), (float)D), eps));
   float s2 = 0.0f;
+#pragma unroll 8
   for (uint32_t i = threadIdx.x; i < D; i += kT) {
     float x = pre ? xv[i] : X[xb + i];
     if (mode == 0) x = __fmul_rn(__fadd_rn(x, __fmul_rn(__fmul_rn(tv[i], rs), pre ? wv[i] : Wn[i])), scale);
