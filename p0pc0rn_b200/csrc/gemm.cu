@@ -49,6 +49,7 @@ using Cfg1 = GemmCfg<16, 5, 256, 1>;
 using Cfg2 = GemmCfg<8, 4, 128, 2>;
 using Cfg3 = GemmCfg<16, 6, 256, 1>;   // Cfg1 with a sixth stage (223 KB of shared memory, 448 TMEM columns)
 using CfgH = GemmCfg<16, 4, 256, 1>;   // fp16 weights: 16 KB of weights per stage, so four stages fit
+using Cfg4 = GemmCfg<24, 5, 256, 1>;   // Cfg1 with a third dequantiser parity (every third stage per warp; 832 threads)
 constexpr int kDqPerStage = 8;  // dequant warps that fill one stage
 // weights of a stage: q4 2 row tiles x 2 groups of 1280 B; q8 2 row tiles x 1 group of 4224 B (= the gathered layout's
 // 128 rows x 2 halves x 32 code bytes + 128 scales x 2 B + 256 B)
@@ -504,9 +505,9 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
         gB = p.BV[p.bvOff + o];
         uB = p.BV[p.bvOff + p.bvUp + o];
       }
-      // warp: quarter q of the lanes, columns [e*cpw, (e+1)*cpw) of BT / (warps / 4)
-      const uint32_t e = d >> 2, cpw = BT / (kDqWarps / 4);
-      for (uint32_t c0 = e * cpw; c0 < (e + 1) * cpw; c0 += 16) {
+      // warp: quarter q of the lanes, every (warps / 4)-th 16-column chunk of BT from chunk e
+      const uint32_t e = d >> 2;
+      for (uint32_t c0 = e * 16u; c0 < BT; c0 += (kDqWarps / 4) * 16u) {
         uint32_t r[16];
         tc::tmem_ld16(tq + c0, r);
         tc::tmem_wait_ld();
@@ -746,7 +747,7 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   // Cfg1 everywhere: measured on B200 (configs 3 and 4), Cfg2's overlapped epilogue does not pay for halving the tokens
   // each dequantised stage feeds (804-899 against 937-1067 TFLOP/s). P0MM_GEMM=2 selects Cfg2 (tuning and tests).
   const char *gv = getenv("P0MM_GEMM");
-  const bool cfg2 = gv && gv[0] == '2', cfg3 = gv && gv[0] == '3';
+  const bool cfg2 = gv && gv[0] == '2', cfg3 = gv && gv[0] == '3', cfg4 = gv && gv[0] == '4';
   const uint32_t BT = M <= 64 ? 64u : (M <= 128 || cfg2) ? 128u : 256u;
   auto enc_fn = tensor_map_encoder();
   if (!enc_fn) return p0_fail(c, P0_EDEVICE, "gemm: cuTensorMapEncodeTiled is unavailable");
@@ -805,6 +806,10 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
     const size_t smem = Cfg3::kRingBytes + (size_t)Cfg3::kStages * kWStage + 1024 + 256;
     cudaFuncSetAttribute(gemm_q4_tc<Cfg3, kWQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     gemm_q4_tc<Cfg3, kWQ4><<<grid, Cfg3::kThreads, smem, c->stream>>>(tm, p);
+  } else if (cfg4) {
+    const size_t smem = Cfg4::kRingBytes + (size_t)Cfg4::kStages * kWStage + 1024 + 256;
+    cudaFuncSetAttribute(gemm_q4_tc<Cfg4, kWQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    gemm_q4_tc<Cfg4, kWQ4><<<grid, Cfg4::kThreads, smem, c->stream>>>(tm, p);
   } else if (cfg2) {
     const size_t smem = Cfg2::kRingBytes + (size_t)Cfg2::kStages * kWStage + 1024 + 256;
     cudaFuncSetAttribute(gemm_q4_tc<Cfg2, kWQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
