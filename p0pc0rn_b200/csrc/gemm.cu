@@ -31,9 +31,13 @@ constexpr int kBK = 64;         // k per stage
 // Two shapes of the kernel, one source. Cfg1: 16 dequantiser warps (two stage parities), 5 stages, tiles of up to 256
 // tokens, one CTA per SM, 512 TMEM columns. Cfg2: 8 dequantiser warps, 4 stages, tiles of up to 128 tokens, two CTAs
 // per SM with 256 TMEM columns each, so that one CTA's epilogue runs while the other's main loop keeps the tensor
-// cores busy.
-template <int DQW, int STAGES, uint32_t MAXBT, int MINB>
+// cores busy. PAIR = 2: a CTA pair (a 2-CTA cluster) runs one tcgen05.mma.cta_group::2 of M = 256 weight rows: each
+// CTA dequantises its own 128 rows into its tensor memory and loads half of the token tile's X (BT / 2 rows), and the
+// even CTA's elected thread issues the pair's MMAs, which leave each CTA's 128 rows x BT tokens in its own tensor
+// memory. Per SM that is the same dequantisation and MMA work per stage for half the X bytes out of L2.
+template <int DQW, int STAGES, uint32_t MAXBT, int MINB, int PAIR = 1>
 struct GemmCfg {
+  static constexpr int kPair = PAIR;
   static constexpr int kDqWarps = DQW;                 // warps 2 .. 2+DQW-1: (lane quarter) x (32-k half) x (parity)
   static constexpr int kPar = DQW / 8;                 // stage parities the dequantisers alternate over
   static constexpr int kStages = STAGES;
@@ -42,7 +46,7 @@ struct GemmCfg {
   static constexpr uint32_t kMaxBT = MAXBT;
   static constexpr uint32_t kAcol = MAXBT;             // first TMEM column of the weight (A) stages; D holds [0, BT)
   static constexpr uint32_t kTmemCols = MAXBT + 32u * STAGES <= 256u ? 256u : 512u;
-  static constexpr size_t kXStage = (size_t)MAXBT * kBK * 2;   // X slot (1024-aligned); the ring is also the staging
+  static constexpr size_t kXStage = (size_t)MAXBT / PAIR * kBK * 2;   // X slot (1024-aligned); the ring is also the staging
   static constexpr size_t kRingBytes = (size_t)STAGES * kXStage;
 };
 using Cfg1 = GemmCfg<16, 5, 256, 1>;
@@ -50,6 +54,7 @@ using Cfg2 = GemmCfg<8, 4, 128, 2>;
 using Cfg3 = GemmCfg<16, 6, 256, 1>;   // Cfg1 with a sixth stage (223 KB of shared memory, 448 TMEM columns)
 using CfgH = GemmCfg<16, 4, 256, 1>;   // fp16 weights: 16 KB of weights per stage, so four stages fit
 using Cfg4 = GemmCfg<24, 5, 256, 1>;   // Cfg1 with a third dequantiser parity (every third stage per warp; 832 threads)
+using Cfg5 = GemmCfg<16, 8, 256, 1, 2>;   // CTA pairs: 16 KB X slots, so 8 stages (the ring still stages [256][128] f32)
 constexpr int kDqPerStage = 8;  // dequant warps that fill one stage
 // weights of a stage: q4 2 row tiles x 2 groups of 1280 B; q8 2 row tiles x 1 group of 4224 B (= the gathered layout's
 // 128 rows x 2 halves x 32 code bytes + 128 scales x 2 B + 256 B)
@@ -300,15 +305,19 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
   uint32_t *tmem_slot = (uint32_t *)(accf + 1);
   volatile uint32_t *abort_flag = tmem_slot + 1;
 
+  constexpr bool PR = C::kPair == 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t BT = p.BT, nk = p.nk, nB = blockIdx.x * kBW, m0 = blockIdx.y * BT;
-  const uint32_t xbytes = BT * kBK * 2;
+  // pairs: the CTA's rank in its cluster (= blockIdx.x & 1) picks its half of the token tile
+  const uint32_t crank = PR ? tc::cluster_rank() : 0u, xrows = BT / C::kPair;
+  const uint32_t xbytes = xrows * kBK * 2;
+  const int32_t xm0 = (int32_t)(m0 + crank * xrows);
   const uint32_t g0 = p.wk0 / (Q8 ? 64u : 32u);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; s++) {
       tc::mbar_init(&full[s], 1);
-      tc::mbar_init(&full_a[s], kDqPerStage);
+      tc::mbar_init(&full_a[s], kDqPerStage * C::kPair);   // pairs: the even CTA's barrier counts both CTAs' warps
       tc::mbar_init(&empty[s], 1);
     }
     tc::mbar_init(accf, 1);
@@ -316,11 +325,17 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
     tc::fence_mbar_init();
   }
   if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, kTmemCols);
-    tc::tmem_relinquish();
+    if (PR) {
+      tc::tmem_alloc_pair(tmem_slot, kTmemCols);
+      tc::tmem_relinquish_pair();
+    } else {
+      tc::tmem_alloc(tmem_slot, kTmemCols);
+      tc::tmem_relinquish();
+    }
   }
   tc::fence_before();
-  __syncthreads();
+  if (PR) tc::cluster_sync();   // both CTAs' barriers are initialised before either arrives on the other's
+  else __syncthreads();
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -350,19 +365,19 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
         __syncwarp();
         if (lane == 0) {
           tc::mbar_expect_tx(&full[slot], xbytes);
-          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), (int32_t)m0);
+          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), xm0);
         }
       } else if (p.wtma && Q8) {
         if (lane == 0) {   // one q8 record of each row tile: the stage's 64 k
           tc::mbar_expect_tx(&full[slot], xbytes + 2u * 4224u);
-          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), (int32_t)m0);
+          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), xm0);
           bulk_g2s(ws, p.W + ((size_t)t0 * p.wG + g0 + s) * 4224u, 4224u, &full[slot]);
           bulk_g2s(ws + 4224u, p.W + ((size_t)t1 * p.wG + g0 + s) * 4224u, 4224u, &full[slot]);
         }
       } else if (p.wtma) {
         if (lane == 0) {
           tc::mbar_expect_tx(&full[slot], xbytes + 2u * ng * 1280u);
-          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), (int32_t)m0);
+          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), xm0);
           bulk_g2s(ws, p.W + ((size_t)t0 * p.wG + g0 + 2u * s) * 1280u, ng * 1280u, &full[slot]);
           bulk_g2s(ws + 2560u, p.W + ((size_t)t1 * p.wG + g0 + 2u * s) * 1280u, ng * 1280u, &full[slot]);
         }
@@ -381,7 +396,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
         __syncwarp();
         if (lane == 0) {
           tc::mbar_expect_tx(&full[slot], xbytes);
-          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), (int32_t)m0);
+          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), xm0);
         }
       } else {
         // rows that are not whole tiles: the warp gathers them into lane order ([h][lane] 16-byte codes, then tails)
@@ -397,7 +412,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
         __syncwarp();
         if (lane == 0) {
           tc::mbar_expect_tx(&full[slot], xbytes);
-          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), (int32_t)m0);
+          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), xm0);
         }
       }
       issued++;
@@ -410,19 +425,26 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = tc::idesc_f16_f32(kBW, BT);
+    if (lane == 0 && crank == 0u) {   // pairs: the even CTA issues for both
+      const uint32_t idesc = tc::idesc_f16_f32(kBW * C::kPair, BT);
       for (uint32_t s = 0; s < nk; s++) {
         const uint32_t slot = s % kStages, ph = (s / kStages) & 1u;
-        if (!tc::mbar_wait(&full_a[slot], ph, abort_flag, p.err, 0x202u, P0_SPIN_LIMIT)) break;   // implies X landed
+        // implies X landed (in both CTAs: each CTA's dequantisers waited for its stage before arriving)
+        const bool got = PR ? tc::mbar_wait_cluster(&full_a[slot], ph, abort_flag, p.err, 0x202u, P0_SPIN_LIMIT)
+                            : tc::mbar_wait(&full_a[slot], ph, abort_flag, p.err, 0x202u, P0_SPIN_LIMIT);
+        if (!got) break;
         tc::fence_after();
         const uint32_t xs = tc::smem_u32(xring + (size_t)slot * kXStage);
 #pragma unroll
-        for (uint32_t kk = 0; kk < kBK / 16; kk++)
-          tc::mma_ts_f16(tmem, tmem + kAcol + slot * 32u + kk * 8u, tc::desc_sw128(xs + kk * 32u), idesc, (s | kk) != 0u);
-        tc::mma_commit(&empty[slot]);
+        for (uint32_t kk = 0; kk < kBK / 16; kk++) {
+          if (PR) tc::mma_ts_f16_pair(tmem, tmem + kAcol + slot * 32u + kk * 8u, tc::desc_sw128(xs + kk * 32u), idesc, (s | kk) != 0u);
+          else tc::mma_ts_f16(tmem, tmem + kAcol + slot * 32u + kk * 8u, tc::desc_sw128(xs + kk * 32u), idesc, (s | kk) != 0u);
+        }
+        if (PR) tc::mma_commit_pair(&empty[slot]);   // frees the slot in both CTAs
+        else tc::mma_commit(&empty[slot]);
       }
-      tc::mma_commit(accf);
+      if (PR) tc::mma_commit_pair(accf);
+      else tc::mma_commit(accf);
       // the accumulator is complete (or the loop gave up) before TMEM can be released
       volatile uint32_t never = 0;
       tc::mbar_wait(accf, 0, &never, p.err, 0x203u, P0_SPIN_LIMIT);
@@ -480,7 +502,10 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
       tc::tmem_wait_st();
       tc::fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&full_a[slot]);
+      if (lane == 0) {
+        if (PR) tc::mbar_arrive_rank(&full_a[slot], 0u);   // the even CTA's barrier, which its MMA thread waits on
+        else tc::mbar_arrive(&full_a[slot]);
+      }
     }
     // ---- epilogue. Every epilogue thread passes both named barriers whatever happened (the loops above are
     // bounded), and the work between them is skipped warp-uniformly after a failed wait.
@@ -533,7 +558,9 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
       }
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kDqWarps * 32) : "memory");
-    if (go && !*abort_flag && (p.epi == P0_GEPI_HEADS || p.epi == P0_GEPI_ONORMGATE)) {
+    if (nB >= p.N) {
+      // a pair's odd CTA past the last weight row: nothing of its tile is stored
+    } else if (go && !*abort_flag && (p.epi == P0_GEPI_HEADS || p.epi == P0_GEPI_ONORMGATE)) {
       store_red128(p, stg, nB, m0, BT, (threadIdx.x - 64u) >> 5, kDqWarps, lane);
     } else if (go && !*abort_flag) {
       // coalesced stores: 4 consecutive columns per thread per step (the reference's vec4 granularity)
@@ -580,11 +607,14 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
     }
   }
   // ---------------------------------------------------------------- teardown
+  // (pairs: neither CTA frees its tensor memory or exits while the other may still arrive on its barriers or read it)
   tc::fence_before();
-  __syncthreads();
+  if (PR) tc::cluster_sync();
+  else __syncthreads();
   if (warp == 1) {
     tc::fence_after();
-    tc::tmem_dealloc(tmem, kTmemCols);
+    if (PR) tc::tmem_dealloc_pair(tmem, kTmemCols);
+    else tc::tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -749,6 +779,9 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   const char *gv = getenv("P0MM_GEMM");
   const bool cfg2 = gv && gv[0] == '2', cfg3 = gv && gv[0] == '3', cfg4 = gv && gv[0] == '4';
   const uint32_t BT = M <= 64 ? 64u : (M <= 128 || cfg2) ? 128u : 256u;
+  // CTA pairs (Cfg5, P0MM_GEMM=5) for q4 weights in 256-token tiles: half the X bytes per SM, measured at ~0.8x Cfg1
+  // on the config-3/4 shapes (the pair's per-stage hand-off spans two SMs), so not the default
+  const bool pair = gv && gv[0] == '5' && BT == 256u && !f16w && !q8;
   auto enc_fn = tensor_map_encoder();
   if (!enc_fn) return p0_fail(c, P0_EDEVICE, "gemm: cuTensorMapEncodeTiled is unavailable");
   // the fp16 X the GEMM reads: x itself, or the prologue pass's output in the context workspace
@@ -771,7 +804,7 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   CUtensorMap tm;
   cuuint64_t dims[2] = {K, M};
   cuuint64_t strides[1] = {(cuuint64_t)xld * 2};
-  cuuint32_t box[2] = {(cuuint32_t)kBK, BT};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, pair ? BT / 2u : BT};   // pairs: each CTA loads half of the token tile
   cuuint32_t estr[2] = {1, 1};
   CUresult cr = enc_fn(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)xbase, dims, strides, box, estr,
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -802,6 +835,22 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
     const size_t smem = Cfg1::kRingBytes + (size_t)Cfg1::kStages * w_stage<true>() + 1024 + 256;
     cudaFuncSetAttribute(gemm_q4_tc<Cfg1, kWQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     gemm_q4_tc<Cfg1, kWQ8><<<grid, Cfg1::kThreads, smem, c->stream>>>(tm, p);
+  } else if (pair) {
+    const size_t smem = Cfg5::kRingBytes + (size_t)Cfg5::kStages * kWStage + 1024 + 256;
+    cudaFuncSetAttribute(gemm_q4_tc<Cfg5, kWQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((grid.x + 1u) & ~1u, grid.y);   // whole pairs: an odd CTA past the last row tile stores nothing
+    lc.blockDim = dim3(Cfg5::kThreads);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = c->stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    cudaLaunchKernelEx(&lc, gemm_q4_tc<Cfg5, kWQ4>, tm, p);
   } else if (cfg3) {
     const size_t smem = Cfg3::kRingBytes + (size_t)Cfg3::kStages * kWStage + 1024 + 256;
     cudaFuncSetAttribute(gemm_q4_tc<Cfg3, kWQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -40,6 +40,46 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
   return false;
 }
 
+// ---- CTA pairs (a 2-CTA cluster sharing one tcgen05.mma.cta_group::2)
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// every thread of both CTAs: orders each CTA's earlier shared-memory writes (barrier inits included) before the peer's
+// later accesses
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// arrive (release at cluster scope) on the mbarrier at the same shared offset in CTA `rank` of the cluster
+__device__ __forceinline__ void mbar_arrive_rank(uint64_t *bar, uint32_t rank) {
+  asm volatile(
+      "{\n .reg .b32 ra;\n mapa.shared::cluster.u32 ra, %0, %1;\n mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n}" ::"r"(
+          smem_u32(bar)),
+      "r"(rank)
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_cluster(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// mbar_wait for a phase completed by arrivals from the peer CTA as well (acquire at cluster scope)
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, volatile uint32_t *abort, uint32_t *err, uint32_t code,
+                                                  uint32_t limit) {
+  for (uint32_t i = 0; i < limit; i++) {
+    if (mbar_try_cluster(bar, parity)) return true;
+    if (*abort) return false;
+  }
+  *abort = 1u;
+  atomicOr(err, code);
+  return false;
+}
+
 // 2D TMA tile load (no multicast) into shared memory, completing bytes on an mbarrier
 __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, uint64_t *bar, int32_t c0, int32_t c1) {
   asm volatile(
@@ -71,6 +111,33 @@ __device__ __forceinline__ void mma_ts_f16(uint32_t d_tmem, uint32_t a_tmem, uin
 // arrive on an mbarrier once every tcgen05.mma this thread issued so far has completed
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// The same for a CTA pair. Both CTAs allocate (one warp each, the same warp), both free after a cluster barrier.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D (+)= A * B on the pair, issued by one thread of the even CTA: M = 256 rows (rows 0-127 from the even CTA's tensor
+// memory, 128-255 from the odd CTA's, at the same address), N columns of B (columns [0, N/2) from the even CTA's
+// shared memory, [N/2, N) from the odd CTA's, at the same descriptor), each CTA's D = its 128 rows x N
+__device__ __forceinline__ void mma_ts_f16_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive on the mbarrier at this shared offset in both CTAs of the pair once the pair's MMAs issued so far completed
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "h"((uint16_t)3)
+               : "memory");
 }
 
 // 16 consecutive 32-bit columns of this thread's lane (warp = one 32-lane quarter)
