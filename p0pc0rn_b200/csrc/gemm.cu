@@ -16,6 +16,9 @@
 //                stage the same warps are the epilogue: tcgen05.ld -> bias / activation -> shared staging ->
 //                coalesced vector stores.
 // Orientation: D = Wdq . X^T, so TMEM lane = output column n and TMEM column = token m.
+// A persistent form of the same GEMM (gemm_q4_ps, below) serves q4 calls with a store epilogue and short K: one CTA
+// per SM walks the tiles with two accumulators in tensor memory and the dequantised weights in shared memory, so a
+// tile's epilogue runs under the next tile's main loop.
 #include <cuda.h>
 #include <cstdlib>
 #include <cuda_fp16.h>
@@ -618,6 +621,240 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
   }
 }
 
+// ================================================================================================ persistent form
+// gemm_q4_ps: the same GEMM for q4 weights in whole 64-row tiles (the bulk-copy path) with the store epilogues
+// (f16 / f32 / bias (+res, +post_gelu) / resadd / swiglu), as a persistent kernel: one CTA per SM walks the tiles
+// t = blockIdx.x, blockIdx.x + gridDim.x, ... (row tile fastest, so the CTAs running at once share one or two token
+// tiles' X in L2), its roles streaming through one ring across tile boundaries:
+//   warp 0       producer: per stage the X tile by TMA and the two row tiles' q4 records by cp.async.bulk
+//   warp 1       TMEM (512 columns: two accumulators of up to 256 tokens) and the MMA thread: tile i accumulates in
+//                buffer i & 1, tcgen05.mma kind::f16 with A (the dequantised weights) and B (X) both from shared
+//                memory, M = 128, N = BT
+//   warps 2..17  dequantisers: f16(q*s + mn) of their row's 32 k into the stage's A slot, 128-byte swizzled K-major
+//                (the layout TMA gives the X tile), then a proxy fence and an arrive
+//   warps 18..25 epilogue: two per TMEM lane quarter, alternate 32-token chunks; waits for tile i's accumulator,
+//                reads it 32 tokens at a time, applies the epilogue and stores straight to Y (a warp's 32 rows = 32
+//                consecutive columns of Y per token), then frees the buffer for tile i + 2. Tile i's epilogue runs
+//                under tile i + 1's main loop.
+// Per tile the prologue (barrier set-up, TMEM allocation, pipeline fill) is paid once per CTA instead of per tile, and
+// no epilogue leaves the tensor pipe idle.
+constexpr int kPsStages = 4;
+constexpr int kPsDq = 16;
+constexpr int kPsEpi = 8;
+constexpr int kPsThreads = 32 * (2 + kPsDq + kPsEpi);
+constexpr size_t kPsX = (size_t)256 * kBK * 2;   // X slot: up to 256 tokens x 64 k fp16
+constexpr size_t kPsA = (size_t)kBW * kBK * 2;   // A slot: 128 rows x 64 k fp16
+constexpr size_t kPsW = 2u * 2u * 1280u;         // two row tiles x two q4 groups
+constexpr size_t kPsSmem = (size_t)kPsStages * (kPsX + kPsA + kPsW) + 1024 + 256;
+
+__global__ void __launch_bounds__(kPsThreads, 1) gemm_q4_ps(const __grid_constant__ CUtensorMap tmx, const GemmParams p, const uint32_t nrt,
+                                                           const uint32_t ntiles) {
+  constexpr int S = kPsStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t *xring = smem;
+  uint8_t *aring = xring + S * kPsX;
+  uint8_t *wring = aring + S * kPsA;
+  uint64_t *full = (uint64_t *)(wring + S * kPsW);
+  uint64_t *full_a = full + S;
+  uint64_t *empty = full_a + S;
+  uint64_t *acc_full = empty + S;     // [2]
+  uint64_t *acc_empty = acc_full + 2; // [2]
+  uint64_t *mdone = acc_empty + 2;
+  uint32_t *tmem_slot = (uint32_t *)(mdone + 1);
+  volatile uint32_t *abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t BT = p.BT, nk = p.nk, xbytes = BT * kBK * 2, g0 = p.wk0 / 32u;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; s++) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&full_a[s], kDqPerStage);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      tc::mbar_init(&acc_full[b], 1);
+      tc::mbar_init(&acc_empty[b], kPsEpi);
+    }
+    tc::mbar_init(mdone, 1);
+    *abort_flag = 0u;
+    tc::fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, 512);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) tc::prefetch_tmap(&tmx);
+    uint32_t gs = 0;
+    bool ok = true;
+    for (uint32_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      const uint32_t nB = (t % nrt) * kBW, m0 = (t / nrt) * BT;
+      uint32_t t0 = 0, t1 = 0;
+      cta_tiles(p, nB, t0, t1);
+      for (uint32_t s = 0; s < nk; s++, gs++) {
+        const uint32_t slot = gs % S, ph = (gs / S) & 1u;
+        bool got = true;
+        if (lane == 0) got = tc::mbar_wait(&empty[slot], ph ^ 1u, abort_flag, p.err, 0x111u, P0_SPIN_LIMIT);
+        if (!__shfl_sync(0xffffffffu, (int)got, 0)) { ok = false; break; }
+        if (lane == 0) {
+          const uint32_t ng = min(2u, (p.K - s * kBK) / 32u);
+          uint8_t *ws = wring + (size_t)slot * kPsW;
+          tc::mbar_expect_tx(&full[slot], xbytes + 2u * ng * 1280u);
+          tc::tma_load_2d(xring + (size_t)slot * kPsX, &tmx, &full[slot], (int32_t)(s * kBK), (int32_t)m0);
+          bulk_g2s(ws, p.W + ((size_t)t0 * p.wG + g0 + 2u * s) * 1280u, ng * 1280u, &full[slot]);
+          bulk_g2s(ws + 2560u, p.W + ((size_t)t1 * p.wG + g0 + 2u * s) * 1280u, ng * 1280u, &full[slot]);
+        }
+      }
+    }
+    // every issued copy has landed before the CTA can exit (bounded; copies always finish)
+    if (lane == 0) {
+      volatile uint32_t never = 0;
+      for (uint32_t g = gs > (uint32_t)S ? gs - S : 0; g < gs; g++)
+        tc::mbar_wait(&full[g % S], (g / S) & 1u, &never, p.err, 0x112u, P0_SPIN_LIMIT);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_f16_f32(kBW, BT);
+      uint32_t gs = 0, i = 0;
+      bool ok = true;
+      for (uint32_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, i++) {
+        const uint32_t b = i & 1u, u = i >> 1;
+        // the epilogue has read this buffer's previous tile (the first use of each buffer passes at once)
+        if (!tc::mbar_wait(&acc_empty[b], (u & 1u) ^ 1u, abort_flag, p.err, 0x211u, P0_SPIN_LIMIT)) break;
+        tc::fence_after();
+        const uint32_t dt = tmem + b * 256u;
+        for (uint32_t s = 0; s < nk; s++, gs++) {
+          const uint32_t slot = gs % S, ph = (gs / S) & 1u;
+          if (!tc::mbar_wait(&full_a[slot], ph, abort_flag, p.err, 0x212u, P0_SPIN_LIMIT)) { ok = false; break; }   // implies X landed
+          tc::fence_after();
+          const uint32_t xs = tc::smem_u32(xring + (size_t)slot * kPsX), as = tc::smem_u32(aring + (size_t)slot * kPsA);
+#pragma unroll
+          for (uint32_t kk = 0; kk < kBK / 16; kk++)
+            tc::mma_ss_f16(dt, tc::desc_sw128(as + kk * 32u), tc::desc_sw128(xs + kk * 32u), idesc, (s | kk) != 0u);
+          tc::mma_commit(&empty[slot]);
+        }
+        if (ok) tc::mma_commit(&acc_full[b]);
+      }
+      // every MMA has completed before TMEM can be released
+      tc::mma_commit(mdone);
+      volatile uint32_t never = 0;
+      tc::mbar_wait(mdone, 0, &never, p.err, 0x213u, P0_SPIN_LIMIT);
+    }
+  } else if (warp < 2 + kPsDq) {
+    // ---------------------------------------------------------------- dequantisers
+    const uint32_t d = (uint32_t)warp - 2u, q = (uint32_t)warp & 3u, h = (d >> 2) & 1u, par = d >> 3;
+    const uint32_t nl = q * 32u + lane;   // this thread's weight row of the tile
+    // its record tile and row (swiglu: even rows from the gate tile, odd rows from the up tile)
+    const bool swi = p.epi == P0_GEPI_SWIGLU;
+    const uint32_t ts = swi ? (nl & 1u) : (nl >> 6), rr = swi ? (nl >> 1) : (nl & 63u);
+    const uint32_t code_off = ts * 2560u + h * 1280u + rr * 16u, tail_off = ts * 2560u + h * 1280u + 1024u + rr * 4u;
+    const uint32_t arow = (nl >> 3) * 1024u + (nl & 7u) * 128u;   // the row's 128-byte line in the swizzled A slot
+    uint32_t gs = 0;
+    bool ok = true;
+    for (uint32_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      for (uint32_t s = 0; s < nk; s++, gs++) {
+        if ((gs & 1u) != par) continue;   // this warp fills every other stage of the ring's sequence
+        const uint32_t slot = gs % S, ph = (gs / S) & 1u;
+        const bool got = tc::mbar_wait(&full[slot], ph, abort_flag, p.err, 0x311u, P0_SPIN_LIMIT);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        uint32_t r[16];
+        if (s * kBK + h * 32u < p.K) {
+          const uint8_t *ws = wring + (size_t)slot * kPsW;
+          deq_row16(*reinterpret_cast<const uint4 *>(ws + code_off), *reinterpret_cast<const uint32_t *>(ws + tail_off), r);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; j++) r[j] = 0u;   // k beyond K: zero weights (X is zero-filled there as well)
+        }
+        uint8_t *as = aring + (size_t)slot * kPsA + arow;
+#pragma unroll
+        for (uint32_t j = 0; j < 4; j++)   // 16-byte chunk 4h + j of the row at chunk position (4h + j) ^ (row % 8)
+          *reinterpret_cast<uint4 *>(as + (((4u * h + j) ^ (nl & 7u)) * 16u)) = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the generic writes before the MMA's reads
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&full_a[slot]);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const uint32_t q = (uint32_t)warp & 3u, nl = q * 32u + lane, e = ((uint32_t)warp - 2u - kPsDq) >> 2;
+    const bool swi = p.epi == P0_GEPI_SWIGLU, f32y = p.epi == P0_GEPI_F32 || p.epi == P0_GEPI_RESADD;
+    uint32_t i = 0;
+    for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, i++) {
+      const uint32_t b = i & 1u, u = i >> 1;
+      const bool got = tc::mbar_wait(&acc_full[b], u & 1u, abort_flag, p.err, 0x411u, P0_SPIN_LIMIT);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc::fence_after();
+      const uint32_t nB = (t % nrt) * kBW, m0 = (t / nrt) * BT, n = nB + nl;
+      float pre_a = 1.0f, pre_b = 0.0f, gB = 0.0f, uB = 0.0f;   // per-row epilogue constants
+      if (p.epi == P0_GEPI_BIAS) pre_b = n < p.N ? p.EV[p.evOff + n] : 0.0f;
+      if (p.epi == P0_GEPI_RESADD && n < p.N) {
+        pre_a = p.gate ? p.EV[p.evOff + n] : 1.0f;
+        pre_b = p.bias ? p.BV[p.bvOff + n] : 0.0f;
+      }
+      const uint32_t o = (nB >> 1) + (nl >> 1);
+      if (swi && p.bias && nB + (nl & ~1u) < p.N) {
+        gB = p.BV[p.bvOff + o];
+        uB = p.BV[p.bvOff + p.bvUp + o];
+      }
+      const bool col_ok = swi ? ((nl & 1u) == 0u && n < p.N) : n < p.N;
+      const size_t col = swi ? (size_t)p.ny0 + o : (size_t)p.ny0 + n;
+      const uint32_t dt = tmem + ((q * 32u) << 16) + b * 256u;
+      for (uint32_t c0 = e * 32u; c0 < BT; c0 += 32u * (kPsEpi / 4)) {
+        uint32_t r[32];
+        tc::tmem_ld32(dt + c0, r);
+        tc::tmem_wait_ld();
+        if (c0 + 32u * (kPsEpi / 4) >= BT) {   // this warp's last chunk   // the accumulator is read: tile i + 2 may use it while these values are stored
+          tc::fence_before();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < 32; j++) {
+          const float v = __uint_as_float(r[j]);
+          const uint32_t m = m0 + c0 + j;
+          float w = v;
+          if (swi) {
+            const float up = __shfl_down_sync(0xffffffffu, v, 1);
+            const float g = __fadd_rn(v, gB), uu = __fadd_rn(up, uB);
+            w = __fmul_rn(p.act == P0_ACT_GELU ? gelu_g(g) : silu_g(g), uu);
+          } else if (p.epi == P0_GEPI_BIAS) {
+            w = __fadd_rn(v, pre_b);
+          } else if (p.epi == P0_GEPI_RESADD) {
+            w = __fmul_rn(pre_a, __fadd_rn(v, pre_b));
+          }
+          if (m >= p.M || !col_ok) continue;
+          const size_t e = (size_t)m * p.ldy + col;
+          if (f32y) {
+            float *yp = reinterpret_cast<float *>(p.Y) + e;
+            *yp = (p.epi == P0_GEPI_RESADD && !p.store) ? __fadd_rn(*yp, w) : w;
+          } else {
+            __half *yp = reinterpret_cast<__half *>(p.Y) + e;
+            if (p.epi == P0_GEPI_BIAS && p.res) w = __fadd_rn(w, __half2float(*yp));
+            __half hv = __float2half_rn(w);
+            if (p.epi == P0_GEPI_BIAS && p.post_gelu) hv = __float2half_rn(gelu_m(__half2float(hv)));
+            *yp = hv;
+          }
+        }
+      }
+    }
+  }
+  // ---------------------------------------------------------------- teardown
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
 // the dequantiser of the GEMM, dumped: out[row][k] = f16(q*s + mn) for a q4 view (bit-exactness checks)
 __global__ void deq_dump_q4(const uint8_t *W, uint32_t rows, uint32_t cols, uint32_t wG, uint16_t *out) {
   const uint32_t G = cols / 32;
@@ -826,6 +1063,13 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   p.wtma = swi ? (a->wr0 % 64 == 0 && a->wr1 % 64 == 0 && (N / 2) % 64 == 0) : (a->wr0 % 64 == 0);
   cudaSetDevice(c->device);
   dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
+  // The persistent form for q4 weights in whole row tiles with a store epilogue, when the CTAs get more than one tile
+  // and K is at most 96 stages: measured on B200 (configs 3 and 4) it gains 1-10 % on the K = 2240 / 3072 shapes,
+  // where the per-tile fixed cost is a large share, and loses 4-7 % on the K = 8960 / 12288 ones, where its 4-stage
+  // ring (the A slots take shared memory) costs more than the fixed part it hides. P0MM_GEMM=1..5 selects the
+  // one-tile-per-CTA forms, P0MM_GEMM=6 the persistent form wherever it applies (tuning and tests).
+  const bool ps_ok = !f16w && !q8 && p.wtma && a->epi != P0_GEPI_HEADS && a->epi != P0_GEPI_ONORMGATE;
+  const bool persistent = ps_ok && (gv ? gv[0] == '6' : (p.nk <= 96u && grid.x * grid.y > (uint32_t)c->sm_count));
   if (f16w) {   // fp16 weights: four stages
     p.wtma = 0;
     const size_t smem = CfgH::kRingBytes + (size_t)CfgH::kStages * w_stage_e<kWF16>() + 1024 + 256;
@@ -835,6 +1079,11 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
     const size_t smem = Cfg1::kRingBytes + (size_t)Cfg1::kStages * w_stage<true>() + 1024 + 256;
     cudaFuncSetAttribute(gemm_q4_tc<Cfg1, kWQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     gemm_q4_tc<Cfg1, kWQ8><<<grid, Cfg1::kThreads, smem, c->stream>>>(tm, p);
+  } else if (persistent) {
+    cudaFuncSetAttribute(gemm_q4_ps, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPsSmem);
+    const uint32_t nrt = grid.x, ntiles = grid.x * grid.y;
+    const uint32_t nctas = ntiles < (uint32_t)c->sm_count ? ntiles : (uint32_t)c->sm_count;
+    gemm_q4_ps<<<nctas, kPsThreads, kPsSmem, c->stream>>>(tm, p, nrt, ntiles);
   } else if (pair) {
     const size_t smem = Cfg5::kRingBytes + (size_t)Cfg5::kStages * kWStage + 1024 + 256;
     cudaFuncSetAttribute(gemm_q4_tc<Cfg5, kWQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
