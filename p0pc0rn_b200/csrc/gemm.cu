@@ -38,9 +38,12 @@ constexpr int kBK = 64;         // k per stage
 // CTA dequantises its own 128 rows into its tensor memory and loads half of the token tile's X (BT / 2 rows), and the
 // even CTA's elected thread issues the pair's MMAs, which leave each CTA's 128 rows x BT tokens in its own tensor
 // memory. Per SM that is the same dequantisation and MMA work per stage for half the X bytes out of L2.
-template <int DQW, int STAGES, uint32_t MAXBT, int MINB, int PAIR = 1>
+// KS = 128: stages of 128 k (two 64-k X boxes, four q4 groups per row tile; q4 records by bulk copy only), so each
+// stage hand-off carries twice the work.
+template <int DQW, int STAGES, uint32_t MAXBT, int MINB, int PAIR = 1, int KS = 64>
 struct GemmCfg {
   static constexpr int kPair = PAIR;
+  static constexpr uint32_t kKS = KS;                  // k per stage
   static constexpr int kDqWarps = DQW;                 // warps 2 .. 2+DQW-1: (lane quarter) x (32-k half) x (parity)
   static constexpr int kPar = DQW / 8;                 // stage parities the dequantisers alternate over
   static constexpr int kStages = STAGES;
@@ -48,8 +51,8 @@ struct GemmCfg {
   static constexpr int kThreads = 32 * (2 + DQW);
   static constexpr uint32_t kMaxBT = MAXBT;
   static constexpr uint32_t kAcol = MAXBT;             // first TMEM column of the weight (A) stages; D holds [0, BT)
-  static constexpr uint32_t kTmemCols = MAXBT + 32u * STAGES <= 256u ? 256u : 512u;
-  static constexpr size_t kXStage = (size_t)MAXBT / PAIR * kBK * 2;   // X slot (1024-aligned); the ring is also the staging
+  static constexpr uint32_t kTmemCols = MAXBT + (KS / 2u) * STAGES <= 256u ? 256u : 512u;
+  static constexpr size_t kXStage = (size_t)MAXBT / PAIR * KS * 2;   // X slot (1024-aligned); the ring is also the staging
   static constexpr size_t kRingBytes = (size_t)STAGES * kXStage;
 };
 using Cfg1 = GemmCfg<16, 5, 256, 1>;
@@ -57,7 +60,8 @@ using Cfg2 = GemmCfg<8, 4, 128, 2>;
 using Cfg3 = GemmCfg<16, 6, 256, 1>;   // Cfg1 with a sixth stage (223 KB of shared memory, 448 TMEM columns)
 using CfgH = GemmCfg<16, 4, 256, 1>;   // fp16 weights: 16 KB of weights per stage, so four stages fit
 using Cfg4 = GemmCfg<24, 5, 256, 1>;   // Cfg1 with a third dequantiser parity (every third stage per warp; 832 threads)
-using Cfg5 = GemmCfg<16, 8, 256, 1, 2>;   // CTA pairs: 16 KB X slots, so 8 stages (the ring still stages [256][128] f32)
+using Cfg5 = GemmCfg<16, 8, 256, 1, 2>;
+using Cfg7 = GemmCfg<16, 3, 256, 1, 1, 128>;   // 128-k stages: 3 x (64 KB X + 10 KB records), 448 TMEM columns   // CTA pairs: 16 KB X slots, so 8 stages (the ring still stages [256][128] f32)
 constexpr int kDqPerStage = 8;  // dequant warps that fill one stage
 // weights of a stage: q4 2 row tiles x 2 groups of 1280 B; q8 2 row tiles x 1 group of 4224 B (= the gathered layout's
 // 128 rows x 2 halves x 32 code bytes + 128 scales x 2 B + 256 B)
@@ -292,7 +296,9 @@ template <class C, int WE>
 __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const __grid_constant__ CUtensorMap tmx, const GemmParams p) {
   constexpr bool Q8 = WE == kWQ8, F16 = WE == kWF16;
   constexpr int kStages = C::kStages, kDqWarps = C::kDqWarps;
-  constexpr uint32_t kWStage = w_stage_e<WE>();
+  constexpr uint32_t kSK = C::kKS, kAC = kSK / 2u, kGS = kSK / 32u;   // k, TMEM A columns and q4 groups per stage
+  static_assert(kSK == 64 || WE == kWQ4, "128-k stages are built for q4 records only");
+  constexpr uint32_t kWStage = WE == kWQ4 ? 2u * kGS * 1280u : w_stage_e<WE>();
   constexpr uint32_t kAcol = C::kAcol, kTmemCols = C::kTmemCols;
   constexpr size_t kXStage = C::kXStage, kRingBytes = C::kRingBytes;
   static_assert((size_t)C::kMaxBT * 128 * 4 <= C::kRingBytes, "the epilogue stages [BT][128] f32 in the X ring");
@@ -313,7 +319,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
   const uint32_t BT = p.BT, nk = p.nk, nB = blockIdx.x * kBW, m0 = blockIdx.y * BT;
   // pairs: the CTA's rank in its cluster (= blockIdx.x & 1) picks its half of the token tile
   const uint32_t crank = PR ? tc::cluster_rank() : 0u, xrows = BT / C::kPair;
-  const uint32_t xbytes = xrows * kBK * 2;
+  const uint32_t xbytes = xrows * kSK * 2;
   const int32_t xm0 = (int32_t)(m0 + crank * xrows);
   const uint32_t g0 = p.wk0 / (Q8 ? 64u : 32u);
 
@@ -377,12 +383,15 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
           bulk_g2s(ws, p.W + ((size_t)t0 * p.wG + g0 + s) * 4224u, 4224u, &full[slot]);
           bulk_g2s(ws + 4224u, p.W + ((size_t)t1 * p.wG + g0 + s) * 4224u, 4224u, &full[slot]);
         }
-      } else if (p.wtma) {
+      } else if (p.wtma || kSK != 64) {
         if (lane == 0) {
-          tc::mbar_expect_tx(&full[slot], xbytes + 2u * ng * 1280u);
-          tc::tma_load_2d(xring + (size_t)slot * kXStage, &tmx, &full[slot], (int32_t)(s * kBK), xm0);
-          bulk_g2s(ws, p.W + ((size_t)t0 * p.wG + g0 + 2u * s) * 1280u, ng * 1280u, &full[slot]);
-          bulk_g2s(ws + 2560u, p.W + ((size_t)t1 * p.wG + g0 + 2u * s) * 1280u, ng * 1280u, &full[slot]);
+          const uint32_t ngs = min(kGS, (p.K - s * kSK) / 32u);   // groups in this stage (the last may hold fewer)
+          tc::mbar_expect_tx(&full[slot], xbytes + 2u * ngs * 1280u);
+#pragma unroll
+          for (uint32_t bx = 0; bx < kSK / 64u; bx++)   // 64-k boxes (one 128-byte swizzle span each), stacked
+            tc::tma_load_2d(xring + (size_t)slot * kXStage + bx * xrows * 128u, &tmx, &full[slot], (int32_t)(s * kSK + bx * 64u), xm0);
+          bulk_g2s(ws, p.W + ((size_t)t0 * p.wG + g0 + kGS * s) * 1280u, ngs * 1280u, &full[slot]);
+          bulk_g2s(ws + kGS * 1280u, p.W + ((size_t)t1 * p.wG + g0 + kGS * s) * 1280u, ngs * 1280u, &full[slot]);
         }
       } else if (Q8) {
         // q8 rows that are not whole tiles: [h][lane] 32 code bytes, then one scale per row
@@ -439,9 +448,10 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
         tc::fence_after();
         const uint32_t xs = tc::smem_u32(xring + (size_t)slot * kXStage);
 #pragma unroll
-        for (uint32_t kk = 0; kk < kBK / 16; kk++) {
-          if (PR) tc::mma_ts_f16_pair(tmem, tmem + kAcol + slot * 32u + kk * 8u, tc::desc_sw128(xs + kk * 32u), idesc, (s | kk) != 0u);
-          else tc::mma_ts_f16(tmem, tmem + kAcol + slot * 32u + kk * 8u, tc::desc_sw128(xs + kk * 32u), idesc, (s | kk) != 0u);
+        for (uint32_t kk = 0; kk < kSK / 16; kk++) {
+          const uint64_t bd = tc::desc_sw128(xs + (kk >> 2) * xrows * 128u + (kk & 3u) * 32u);   // box kk / 4, k16 step kk % 4
+          if (PR) tc::mma_ts_f16_pair(tmem, tmem + kAcol + slot * kAC + kk * 8u, bd, idesc, (s | kk) != 0u);
+          else tc::mma_ts_f16(tmem, tmem + kAcol + slot * kAC + kk * 8u, bd, idesc, (s | kk) != 0u);
         }
         if (PR) tc::mma_commit_pair(&empty[slot]);   // frees the slot in both CTAs
         else tc::mma_commit(&empty[slot]);
@@ -470,10 +480,11 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
         code_off = (h * 128u + nl) * 32u;
         tail_off = 8192u + nl * 2u;
       }
-    } else if (p.wtma) {
+    } else if (p.wtma || kSK != 64) {
+      // this thread's groups of a stage: h * kGS / 2 + j (j < kGS / 2), records 1280 bytes apart
       const uint32_t ts = p.epi == P0_GEPI_SWIGLU ? (nl & 1u) : (nl >> 6), r = p.epi == P0_GEPI_SWIGLU ? (nl >> 1) : (nl & 63u);
-      code_off = ts * 2560u + h * 1280u + r * 16u;
-      tail_off = ts * 2560u + h * 1280u + 1024u + r * 4u;
+      code_off = ts * kGS * 1280u + h * (kGS / 2u) * 1280u + r * 16u;
+      tail_off = ts * kGS * 1280u + h * (kGS / 2u) * 1280u + 1024u + r * 4u;
     } else {
       code_off = (h * 128u + nl) * 16u;
       tail_off = 4096u + (h * 128u + nl) * 4u;
@@ -483,25 +494,29 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
       const uint32_t slot = s % kStages, ph = (s / kStages) & 1u;
       const bool got = tc::mbar_wait(&full[slot], ph, abort_flag, p.err, 0x301u, P0_SPIN_LIMIT);
       if (!__all_sync(0xffffffffu, got)) { ok = false; break; }   // warp-uniform: tcgen05.st is .sync.aligned
-      uint32_t r[16];
-      if (s * kBK + h * 32u < p.K) {
-        const uint8_t *ws = wring + (size_t)slot * kWStage;
-        if (F16) {
 #pragma unroll
-          for (int j = 0; j < 4; j++) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(ws + code_off + j * 2048u);
-            r[4 * j] = v.x; r[4 * j + 1] = v.y; r[4 * j + 2] = v.z; r[4 * j + 3] = v.w;
-          }
-        } else if (Q8)
-          deq_row16_q8(*reinterpret_cast<const uint4 *>(ws + code_off), *reinterpret_cast<const uint4 *>(ws + code_off + 16u),
-                       *reinterpret_cast<const uint16_t *>(ws + tail_off), r);
-        else
-          deq_row16(*reinterpret_cast<const uint4 *>(ws + code_off), *reinterpret_cast<const uint32_t *>(ws + tail_off), r);
-      } else {
+      for (uint32_t j = 0; j < kGS / 2u; j++) {   // 64-k stages: one group (j = 0)
+        const uint32_t gi = h * (kGS / 2u) + j;   // the group of the stage
+        uint32_t r[16];
+        if (s * kSK + gi * 32u < p.K) {
+          const uint8_t *ws = wring + (size_t)slot * kWStage;
+          if (F16) {
 #pragma unroll
-        for (int i = 0; i < 16; i++) r[i] = 0u;   // k beyond K: zero weights (X is zero-filled there as well)
+            for (int jj = 0; jj < 4; jj++) {
+              const uint4 v = *reinterpret_cast<const uint4 *>(ws + code_off + jj * 2048u);
+              r[4 * jj] = v.x; r[4 * jj + 1] = v.y; r[4 * jj + 2] = v.z; r[4 * jj + 3] = v.w;
+            }
+          } else if (Q8)
+            deq_row16_q8(*reinterpret_cast<const uint4 *>(ws + code_off), *reinterpret_cast<const uint4 *>(ws + code_off + 16u),
+                         *reinterpret_cast<const uint16_t *>(ws + tail_off), r);
+          else
+            deq_row16(*reinterpret_cast<const uint4 *>(ws + code_off + j * 1280u), *reinterpret_cast<const uint32_t *>(ws + tail_off + j * 1280u), r);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; i++) r[i] = 0u;   // k beyond K: zero weights (X is zero-filled there as well)
+        }
+        tc::tmem_st16(tq + kAcol + slot * kAC + gi * 16u, r);
       }
-      tc::tmem_st16(tq + kAcol + slot * 32u + h * 16u, r);
       tc::tmem_wait_st();
       tc::fence_before();
       __syncwarp();
@@ -1015,7 +1030,13 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   // each dequantised stage feeds (804-899 against 937-1067 TFLOP/s). P0MM_GEMM=2 selects Cfg2 (tuning and tests).
   const char *gv = getenv("P0MM_GEMM");
   const bool cfg2 = gv && gv[0] == '2', cfg3 = gv && gv[0] == '3', cfg4 = gv && gv[0] == '4';
-  const uint32_t BT = M <= 64 ? 64u : (M <= 128 || cfg2) ? 128u : 256u;
+  uint32_t BT = M <= 64 ? 64u : (M <= 128 || cfg2) ? 128u : 256u;
+  // tuning override, read on every call: P0MM_GEMM_BT=64|128|256 sets the token tile
+  const char *btv = getenv("P0MM_GEMM_BT");
+  if (btv && !cfg2) {
+    const long b = strtol(btv, nullptr, 10);
+    if (b == 64 || b == 128 || b == 256) BT = (uint32_t)b;
+  }
   // CTA pairs (Cfg5, P0MM_GEMM=5) for q4 weights in 256-token tiles: half the X bytes per SM, measured at ~0.8x Cfg1
   // on the config-3/4 shapes (the pair's per-stage hand-off spans two SMs), so not the default
   const bool pair = gv && gv[0] == '5' && BT == 256u && !f16w && !q8;
@@ -1063,13 +1084,20 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   p.wtma = swi ? (a->wr0 % 64 == 0 && a->wr1 % 64 == 0 && (N / 2) % 64 == 0) : (a->wr0 % 64 == 0);
   cudaSetDevice(c->device);
   dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
-  // The persistent form for q4 weights in whole row tiles with a store epilogue, when the CTAs get more than one tile
-  // and K is at most 96 stages: measured on B200 (configs 3 and 4) it gains 1-10 % on the K = 2240 / 3072 shapes,
-  // where the per-tile fixed cost is a large share, and loses 4-7 % on the K = 8960 / 12288 ones, where its 4-stage
-  // ring (the A slots take shared memory) costs more than the fixed part it hides. P0MM_GEMM=1..5 selects the
-  // one-tile-per-CTA forms, P0MM_GEMM=6 the persistent form wherever it applies (tuning and tests).
-  const bool ps_ok = !f16w && !q8 && p.wtma && a->epi != P0_GEPI_HEADS && a->epi != P0_GEPI_ONORMGATE;
-  const bool persistent = ps_ok && (gv ? gv[0] == '6' : (p.nk <= 96u && grid.x * grid.y > (uint32_t)c->sm_count));
+  // Which form (measured on B200, configs 3 and 4; the main loop of every form costs ~0.4-0.5 us per stage whatever
+  // the stage's work, so the forms differ in work per stage and in per-tile fixed cost):
+  //  * Cfg7, 128-k stages, for q4 records by bulk copy in 256-token tiles: +13-17 % over Cfg1 on all six shapes
+  //    (1043-1097 against 957-968 TFLOP/s aggregate in the same runs);
+  //  * else the persistent form for q4 records by bulk copy with a store epilogue, when the CTAs get more than one
+  //    tile and K is at most 96 stages (it hides the per-tile fixed cost; its 4-stage ring loses on long K);
+  //  * else Cfg1.
+  // P0MM_GEMM=1..7 forces a form where it applies (tuning and tests): 1 Cfg1, 2..4 variants of it, 5 the CTA pair,
+  // 6 the persistent form, 7 Cfg7.
+  const bool q4bulk = !f16w && !q8 && p.wtma;
+  const bool k128 = q4bulk && BT == 256u && (gv ? gv[0] == '7' : true);
+  const bool ps_ok = q4bulk && a->epi != P0_GEPI_HEADS && a->epi != P0_GEPI_ONORMGATE;
+  const bool persistent = !k128 && ps_ok && (gv ? gv[0] == '6' : (p.nk <= 96u && grid.x * grid.y > (uint32_t)c->sm_count));
+  if (k128) p.nk = (K + 127u) / 128u;
   if (f16w) {   // fp16 weights: four stages
     p.wtma = 0;
     const size_t smem = CfgH::kRingBytes + (size_t)CfgH::kStages * w_stage_e<kWF16>() + 1024 + 256;
@@ -1079,6 +1107,10 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
     const size_t smem = Cfg1::kRingBytes + (size_t)Cfg1::kStages * w_stage<true>() + 1024 + 256;
     cudaFuncSetAttribute(gemm_q4_tc<Cfg1, kWQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     gemm_q4_tc<Cfg1, kWQ8><<<grid, Cfg1::kThreads, smem, c->stream>>>(tm, p);
+  } else if (k128) {
+    const size_t smem = Cfg7::kRingBytes + (size_t)Cfg7::kStages * 2u * 4u * 1280u + 1024 + 256;
+    cudaFuncSetAttribute(gemm_q4_tc<Cfg7, kWQ4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    gemm_q4_tc<Cfg7, kWQ4><<<grid, Cfg7::kThreads, smem, c->stream>>>(tm, p);
   } else if (persistent) {
     cudaFuncSetAttribute(gemm_q4_ps, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPsSmem);
     const uint32_t nrt = grid.x, ntiles = grid.x * grid.y;

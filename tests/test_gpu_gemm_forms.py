@@ -1,14 +1,14 @@
-"""GPU parity of the GEMM's forms against the CPU oracle, through ops.gemm. The library picks the form per call: the
-persistent form (one CTA per SM walking the tiles, two tensor-memory accumulators, dequantised weights in shared
-memory) for q4 weights in whole row tiles with a store epilogue when the CTAs get more than one tile and K is at most
-96 stages; otherwise Cfg1 (one 128-row x 256-token tile per CTA, dequantised weights in tensor memory), which the
-other GEMM tests mostly reach (small grids, long K, heads / onormgate, q8, fp16 weights). P0MM_GEMM forces a form:
-6 = persistent wherever it applies, 5 = Cfg5, the CTA pair (a 2-CTA cluster on one tcgen05.mma.cta_group::2 of 256
-weight rows, each CTA loading half of the 256-token tile's X; measured on B200 at about 0.8x Cfg1 on the config-3/4
-shapes, so never chosen by default). The cases cover a token count that is not a multiple of 256, an odd count of
-128-row tiles (a pair's odd CTA past the last weight row stores nothing), K with a one-group last stage, and the
-bias (+ GELU), f32, resadd, swiglu and heads epilogues (engine/ops/gemm.js:187-250); the many-tile cases make every
-persistent CTA walk several tiles, so both accumulators and the ring are reused across tiles."""
+"""GPU parity of the GEMM's forms against the CPU oracle, through ops.gemm. The library picks the form per call
+(measured on B200, configs 3 and 4): Cfg7 (one 128-row x 256-token tile per CTA, 128-k stages, dequantised weights in
+tensor memory) for q4 records by bulk copy in 256-token tiles; else the persistent form (one CTA per SM walking the
+tiles, two tensor-memory accumulators, dequantised weights in shared memory) for q4 records by bulk copy with a store
+epilogue when the CTAs get more than one tile and K is at most 96 stages; else Cfg1 (64-k stages: q8 and fp16
+weights, gathered rows, tiles of fewer tokens). P0MM_GEMM forces a form: 7 = Cfg7, 6 = persistent, 5 = the CTA pair
+(a 2-CTA cluster on one tcgen05.mma.cta_group::2 of 256 weight rows, each CTA loading half of the token tile's X;
+about 0.8x Cfg1, never chosen by default), 1 = Cfg1. The cases cover a token count that is not a multiple of 256,
+an odd count of 128-row tiles (a pair's odd CTA past the last weight row stores nothing), K with a one-group last
+stage, and the bias (+ GELU), f32, resadd, swiglu and heads epilogues (engine/ops/gemm.js:187-250); the many-tile
+cases make every persistent CTA walk several tiles, so both accumulators and the ring are reused across tiles."""
 import numpy as np
 import pytest
 
@@ -20,13 +20,13 @@ from .test_gpu_parity import assert_close, run_gemm
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["6", "5"], ids=["persistent", "pair"])
+@pytest.fixture(params=["7", "6", "5", "1"], ids=["k128", "persistent", "pair", "cfg1"])
 def form(request, monkeypatch):
     monkeypatch.setenv("P0MM_GEMM", request.param)
     return request.param
 
 
-@pytest.mark.parametrize("M,N,K", [(300, 384, 352), (600, 640, 1024), (257, 128, 64)])
+@pytest.mark.parametrize("M,N,K", [(300, 384, 352), (400, 384, 512), (257, 128, 64)])
 def test_form_f16(g, form, M, N, K):
     b, _ = ref.pack_q4(ref.randn(N * K, 190 + M, 0.02), N, K)
     X = ref.f2h(ref.round_f16(ref.randn(M * K, 191)))
@@ -35,7 +35,7 @@ def test_form_f16(g, form, M, N, K):
 
 
 def test_form_bias_gelu(g, form):
-    M, N, K = 700, 640, 1024
+    M, N, K = 300, 384, 512
     b, _ = ref.pack_q4(ref.randn(N * K, 192, 0.02), N, K)
     X = ref.f2h(ref.round_f16(ref.randn(M * K, 193)))
     bias = ref.randn(N, 194, 0.01)
@@ -83,10 +83,11 @@ def test_form_heads(g, form):
 
 
 # ---------------------------------------------------------------- the default (persistent) form over many tiles per CTA
-@pytest.mark.parametrize("M,N,K", [(2048, 20480, 64), (1500, 9216, 96), (100, 40960, 128)])
+@pytest.mark.parametrize("M,N,K", [(200, 57344, 32), (130, 38400, 96), (100, 40960, 64)])
 def test_persistent_many_tiles(g, monkeypatch, M, N, K):
     monkeypatch.setenv("P0MM_GEMM", "6")
-    # thousands of tiles: every CTA walks several, so both accumulators are reused and the ring runs across tiles
+    # 300-448 tiles on 148 SMs: every CTA walks two or three, so both accumulators are reused and the ring runs across
+    # tiles (one-stage tiles; two stages with a one-group last stage; 128-token tiles)
     b, _ = ref.pack_q4(ref.randn(N * K, 210 + K, 0.02), N, K)
     X = ref.f2h(ref.round_f16(ref.randn(M * K, 211)))
     bias = ref.randn(N, 212, 0.01)
@@ -96,7 +97,7 @@ def test_persistent_many_tiles(g, monkeypatch, M, N, K):
 
 def test_persistent_many_tiles_swiglu_resadd(g, monkeypatch):
     monkeypatch.setenv("P0MM_GEMM", "6")
-    M, N, K = 1024, 16384, 128
+    M, N, K = 130, 40960, 64
     b, _ = ref.pack_q4(ref.randn(N * K, 213, 0.02), N, K)
     X = ref.f2h(ref.round_f16(ref.randn(M * K, 214)))
     bv = ref.randn(N, 215, 0.01)
