@@ -84,6 +84,8 @@ struct GemmParams {
   int rope_half;
   int epi, act, res, store, gate, bias, post_gelu;
   uint32_t BT, nk;
+  uint32_t nkz;       // k split: stages per split (0: none); split z = blockIdx.z runs stages [z * nkz, (z + 1) * nkz)
+  size_t zstride;     // k split: elements between the splits' f32 partial outputs
   int wtma;           // 1: the CTA's 128 rows are two whole 64-row tiles -> records arrive by bulk copy
   uint32_t *err;
 };
@@ -322,6 +324,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
   const uint32_t xbytes = xrows * kSK * 2;
   const int32_t xm0 = (int32_t)(m0 + crank * xrows);
   const uint32_t g0 = p.wk0 / (Q8 ? 64u : 32u);
+  // this CTA's stages: all of them, or its split's range (slots and phases count from the range's start)
+  const uint32_t s0 = p.nkz ? blockIdx.z * p.nkz : 0u, nloc = p.nkz ? min(nk, s0 + p.nkz) - s0 : nk;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; s++) {
@@ -354,8 +358,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
     cta_tiles(p, nB, t0, t1);
     if (lane == 0) tc::prefetch_tmap(&tmx);
     uint32_t issued = 0;
-    for (uint32_t s = 0; s < nk; s++) {
-      const uint32_t slot = s % kStages, ph = (s / kStages) & 1u;
+    for (uint32_t sl = 0; sl < nloc; sl++) {
+      const uint32_t s = s0 + sl, slot = sl % kStages, ph = (sl / kStages) & 1u;
       bool got = true;
       if (lane == 0) got = tc::mbar_wait(&empty[slot], ph ^ 1u, abort_flag, p.err, 0x101u, P0_SPIN_LIMIT);
       if (!__shfl_sync(0xffffffffu, (int)got, 0)) break;
@@ -439,8 +443,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0 && crank == 0u) {   // pairs: the even CTA issues for both
       const uint32_t idesc = tc::idesc_f16_f32(kBW * C::kPair, BT);
-      for (uint32_t s = 0; s < nk; s++) {
-        const uint32_t slot = s % kStages, ph = (s / kStages) & 1u;
+      for (uint32_t sl = 0; sl < nloc; sl++) {
+        const uint32_t slot = sl % kStages, ph = (sl / kStages) & 1u;
         // implies X landed (in both CTAs: each CTA's dequantisers waited for its stage before arriving)
         const bool got = PR ? tc::mbar_wait_cluster(&full_a[slot], ph, abort_flag, p.err, 0x202u, P0_SPIN_LIMIT)
                             : tc::mbar_wait(&full_a[slot], ph, abort_flag, p.err, 0x202u, P0_SPIN_LIMIT);
@@ -450,8 +454,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
 #pragma unroll
         for (uint32_t kk = 0; kk < kSK / 16; kk++) {
           const uint64_t bd = tc::desc_sw128(xs + (kk >> 2) * xrows * 128u + (kk & 3u) * 32u);   // box kk / 4, k16 step kk % 4
-          if (PR) tc::mma_ts_f16_pair(tmem, tmem + kAcol + slot * kAC + kk * 8u, bd, idesc, (s | kk) != 0u);
-          else tc::mma_ts_f16(tmem, tmem + kAcol + slot * kAC + kk * 8u, bd, idesc, (s | kk) != 0u);
+          if (PR) tc::mma_ts_f16_pair(tmem, tmem + kAcol + slot * kAC + kk * 8u, bd, idesc, (sl | kk) != 0u);
+          else tc::mma_ts_f16(tmem, tmem + kAcol + slot * kAC + kk * 8u, bd, idesc, (sl | kk) != 0u);
         }
         if (PR) tc::mma_commit_pair(&empty[slot]);   // frees the slot in both CTAs
         else tc::mma_commit(&empty[slot]);
@@ -490,8 +494,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
       tail_off = 4096u + (h * 128u + nl) * 4u;
     }
     bool ok = true;
-    for (uint32_t s = par; s < nk; s += C::kPar) {   // this warp fills every kPar-th stage
-      const uint32_t slot = s % kStages, ph = (s / kStages) & 1u;
+    for (uint32_t sl = par; sl < nloc; sl += C::kPar) {   // this warp fills every kPar-th stage
+      const uint32_t s = s0 + sl, slot = sl % kStages, ph = (sl / kStages) & 1u;
       const bool got = tc::mbar_wait(&full[slot], ph, abort_flag, p.err, 0x301u, P0_SPIN_LIMIT);
       if (!__all_sync(0xffffffffu, got)) { ok = false; break; }   // warp-uniform: tcgen05.st is .sync.aligned
 #pragma unroll
@@ -590,7 +594,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks) gemm_q4_tc(const _
         const uint32_t colw = swi ? nB + cq * 8u : nB + cq * 4u;   // the ws column the vec4 starts at
         if (m >= p.M || colw >= p.N) continue;
         const float4 t = *reinterpret_cast<const float4 *>(stg + ml * OC + cq * 4u);
-        const size_t e = (size_t)m * p.ldy + p.ny0 + nOut0 + cq * 4u;
+        const size_t e = (size_t)m * p.ldy + p.ny0 + nOut0 + cq * 4u + blockIdx.z * p.zstride;
         if (f32y) {
           float4 *yp = reinterpret_cast<float4 *>(p.Y + e * 4);
           float4 o = t;
@@ -870,6 +874,62 @@ __global__ void __launch_bounds__(kPsThreads, 1) gemm_q4_ps(const __grid_constan
   }
 }
 
+// k split: the S f32 partial products P[z][m][n] of a call, summed in split order, then the call's store epilogue
+// (f16 / bias (+res, +post_gelu) / f32 / resadd, the same arithmetic as the GEMM's store pass), 4 columns per thread
+__global__ void gemm_ksplit_epilogue(const float *__restrict__ P, uint32_t S, size_t zstride, const GemmParams p) {
+  const uint32_t q4 = p.N / 4u;
+  const size_t total = (size_t)p.M * q4;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const uint32_t m = (uint32_t)(i / q4), n = (uint32_t)(i - (size_t)m * q4) * 4u;
+    float4 t = *reinterpret_cast<const float4 *>(P + (size_t)m * p.N + n);
+    for (uint32_t z = 1; z < S; z++) {
+      const float4 u = *reinterpret_cast<const float4 *>(P + z * zstride + (size_t)m * p.N + n);
+      t = make_float4(__fadd_rn(t.x, u.x), __fadd_rn(t.y, u.y), __fadd_rn(t.z, u.z), __fadd_rn(t.w, u.w));
+    }
+    float v[4] = {t.x, t.y, t.z, t.w};
+    const size_t e = (size_t)m * p.ldy + p.ny0 + n;
+    if (p.epi == P0_GEPI_F32 || p.epi == P0_GEPI_RESADD) {
+      float4 *yp = reinterpret_cast<float4 *>(p.Y + e * 4);
+      if (p.epi == P0_GEPI_RESADD) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float pa = p.gate ? p.EV[p.evOff + n + j] : 1.0f, pb = p.bias ? p.BV[p.bvOff + n + j] : 0.0f;
+          v[j] = __fmul_rn(pa, __fadd_rn(v[j], pb));
+        }
+        if (!p.store) {
+          const float4 y0 = *yp;
+          v[0] = __fadd_rn(y0.x, v[0]); v[1] = __fadd_rn(y0.y, v[1]); v[2] = __fadd_rn(y0.z, v[2]); v[3] = __fadd_rn(y0.w, v[3]);
+        }
+      }
+      *yp = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+      uint2 *yp = reinterpret_cast<uint2 *>(p.Y + e * 2);
+      if (p.epi == P0_GEPI_BIAS) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) v[j] = __fadd_rn(v[j], p.EV[p.evOff + n + j]);
+        if (p.res) {
+          const uint2 y0 = *yp;
+          const __half2 a = *reinterpret_cast<const __half2 *>(&y0.x), b = *reinterpret_cast<const __half2 *>(&y0.y);
+          v[0] = __fadd_rn(v[0], __low2float(a));
+          v[1] = __fadd_rn(v[1], __high2float(a));
+          v[2] = __fadd_rn(v[2], __low2float(b));
+          v[3] = __fadd_rn(v[3], __high2float(b));
+        }
+      }
+      __half hv[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        hv[j] = __float2half_rn(v[j]);
+        if (p.epi == P0_GEPI_BIAS && p.post_gelu) hv[j] = __float2half_rn(gelu_m(__half2float(hv[j])));
+      }
+      uint2 o;
+      o.x = (uint32_t)__half_as_ushort(hv[0]) | ((uint32_t)__half_as_ushort(hv[1]) << 16);
+      o.y = (uint32_t)__half_as_ushort(hv[2]) | ((uint32_t)__half_as_ushort(hv[3]) << 16);
+      *yp = o;
+    }
+  }
+}
+
 // the dequantiser of the GEMM, dumped: out[row][k] = f16(q*s + mn) for a q4 view (bit-exactness checks)
 __global__ void deq_dump_q4(const uint8_t *W, uint32_t rows, uint32_t cols, uint32_t wG, uint16_t *out) {
   const uint32_t G = cols / 32;
@@ -1040,15 +1100,58 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   // CTA pairs (Cfg5, P0MM_GEMM=5) for q4 weights in 256-token tiles: half the X bytes per SM, measured at ~0.8x Cfg1
   // on the config-3/4 shapes (the pair's per-stage hand-off spans two SMs), so not the default
   const bool pair = gv && gv[0] == '5' && BT == 256u && !f16w && !q8;
+  // bulk-copy weight path: every CTA's 128 lanes read two whole 64-row tiles
+  const bool wtma = !f16w && (swi ? (a->wr0 % 64 == 0 && a->wr1 % 64 == 0 && (N / 2) % 64 == 0) : (a->wr0 % 64 == 0));
+  dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
+  // Which form (measured on B200, configs 3 and 4; the main loop of every form costs ~0.4-0.5 us per stage whatever
+  // the stage's work, so the forms differ in work per stage and in per-tile fixed cost):
+  //  * Cfg7, 128-k stages, for q4 records by bulk copy in 256-token tiles: +13-17 % over Cfg1 on all six shapes
+  //    (1043-1097 against 957-968 TFLOP/s aggregate in the same runs);
+  //  * else the persistent form for q4 records by bulk copy with a store epilogue, when the CTAs get more than one
+  //    tile and K is at most 96 stages (it hides the per-tile fixed cost; its 4-stage ring loses on long K);
+  //  * else Cfg1.
+  // P0MM_GEMM=1..7 forces a form where it applies (tuning and tests): 1 Cfg1, 2..4 variants of it, 5 the CTA pair,
+  // 6 the persistent form, 7 Cfg7.
+  const bool q4bulk = !f16w && !q8 && wtma;
+  const bool k128 = q4bulk && BT == 256u && (gv ? gv[0] == '7' : true);
+  const bool ps_ok = q4bulk && a->epi != P0_GEPI_HEADS && a->epi != P0_GEPI_ONORMGATE;
+  const uint32_t nk64 = (K + kBK - 1) / kBK, nk = k128 ? (K + 127u) / 128u : nk64;
+  const bool persistent = !k128 && ps_ok && (gv ? gv[0] == '6' : (nk64 <= 96u && grid.x * grid.y > (uint32_t)c->sm_count));
+  // k split, for grids that fill at most half the SMs (a row shard of few tokens; c3 down at 8 ranks is 48 CTAs):
+  // split z runs stages [z * nkz, (z + 1) * nkz) and stores its f32 partial product to the workspace, a second pass
+  // sums the splits in order and applies the store epilogue. P0MM_GEMM_KSPLIT=1..8 sets the split count (tuning, tests).
+  uint32_t S = 1, nkz = 0;
+  const bool split_epi = a->epi == P0_GEPI_F16 || a->epi == P0_GEPI_BIAS || a->epi == P0_GEPI_F32 || a->epi == P0_GEPI_RESADD;
+  if (split_epi && !pair && !persistent) {
+    const char *ksv = getenv("P0MM_GEMM_KSPLIT");
+    const long want = ksv ? strtol(ksv, nullptr, 10) : 0;
+    const uint32_t ctas = grid.x * grid.y, sms = (uint32_t)c->sm_count;
+    if (want >= 1 && want <= 8) S = (uint32_t)want;
+    else if (ctas * 2u <= sms && nk >= 16u) S = min(min(8u, sms / ctas), nk / 4u);
+    if (S > nk) S = nk;
+    if (S > 1u) {
+      nkz = (nk + S - 1u) / S;
+      S = (nk + nkz - 1u) / nkz;   // no empty split
+    }
+    if (S <= 1u) { S = 1u; nkz = 0u; }
+  }
   auto enc_fn = tensor_map_encoder();
   if (!enc_fn) return p0_fail(c, P0_EDEVICE, "gemm: cuTensorMapEncodeTiled is unavailable");
+  // the context workspace holds the prologue pass's fp16 X and the splits' partial products
+  const size_t xws = xmode != P0_XPRO_F16 ? ((size_t)M * K * 2 + 255) / 256 * 256 : 0;
+  const size_t pws = S > 1u ? (size_t)S * M * N * 4 : 0;
+  uint8_t *wsp = nullptr;
+  if (xws + pws) {
+    uint32_t *unused_cnt = nullptr;
+    void *scratch = nullptr;
+    if ((st = p0_workspace(c, 0, xws + pws, &unused_cnt, &scratch))) return st;
+    wsp = (uint8_t *)scratch;
+  }
   // the fp16 X the GEMM reads: x itself, or the prologue pass's output in the context workspace
   const uint8_t *xbase = rx.base + 2ull * a->x_k0;
   uint32_t xld = ldx;
   if (xmode != P0_XPRO_F16) {
-    uint32_t *unused_cnt = nullptr;
-    void *scratch = nullptr;
-    if ((st = p0_workspace(c, 0, (size_t)M * K * 2, &unused_cnt, &scratch))) return st;
+    void *scratch = wsp;
     cudaSetDevice(c->device);
     const uint64_t n8 = (uint64_t)M * (K / 8);
     const unsigned blocks = (unsigned)((n8 + 255) / 256 < (uint64_t)c->sm_count * 8 ? (n8 + 255) / 256 : (uint64_t)c->sm_count * 8);
@@ -1079,27 +1182,19 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
   p.Ltot = a->h_Ltot; p.Hq = a->h_Hq; p.Hkv = a->h_Hkv; p.rowOff = a->h_rowOff;
   p.eps = a->h_eps != 0.0f ? a->h_eps : 1e-6f;   // gemm.js:309 `h.eps || 1e-6`
   p.rope_half = a->h_rope_mode == P0_ROPE_HALF;
-  p.BT = BT; p.nk = (K + kBK - 1) / kBK; p.err = c->d_err;
-  // bulk-copy weight path: every CTA's 128 lanes read two whole 64-row tiles
-  p.wtma = swi ? (a->wr0 % 64 == 0 && a->wr1 % 64 == 0 && (N / 2) % 64 == 0) : (a->wr0 % 64 == 0);
+  p.BT = BT; p.nk = nk; p.err = c->d_err;
+  p.wtma = wtma;
+  const GemmParams pe = p;   // the call's epilogue, for the k split's second pass
+  if (S > 1u) {              // the splits store raw f32 partials [z][m][n]
+    p.nkz = nkz;
+    p.zstride = (size_t)M * N;
+    p.Y = wsp + xws;
+    p.epi = P0_GEPI_F32;
+    p.ldy = N; p.ny0 = 0; p.res = 0; p.store = 1; p.post_gelu = 0;
+    grid.z = S;
+  }
   cudaSetDevice(c->device);
-  dim3 grid((N + kBW - 1) / kBW, (M + BT - 1) / BT);
-  // Which form (measured on B200, configs 3 and 4; the main loop of every form costs ~0.4-0.5 us per stage whatever
-  // the stage's work, so the forms differ in work per stage and in per-tile fixed cost):
-  //  * Cfg7, 128-k stages, for q4 records by bulk copy in 256-token tiles: +13-17 % over Cfg1 on all six shapes
-  //    (1043-1097 against 957-968 TFLOP/s aggregate in the same runs);
-  //  * else the persistent form for q4 records by bulk copy with a store epilogue, when the CTAs get more than one
-  //    tile and K is at most 96 stages (it hides the per-tile fixed cost; its 4-stage ring loses on long K);
-  //  * else Cfg1.
-  // P0MM_GEMM=1..7 forces a form where it applies (tuning and tests): 1 Cfg1, 2..4 variants of it, 5 the CTA pair,
-  // 6 the persistent form, 7 Cfg7.
-  const bool q4bulk = !f16w && !q8 && p.wtma;
-  const bool k128 = q4bulk && BT == 256u && (gv ? gv[0] == '7' : true);
-  const bool ps_ok = q4bulk && a->epi != P0_GEPI_HEADS && a->epi != P0_GEPI_ONORMGATE;
-  const bool persistent = !k128 && ps_ok && (gv ? gv[0] == '6' : (p.nk <= 96u && grid.x * grid.y > (uint32_t)c->sm_count));
-  if (k128) p.nk = (K + 127u) / 128u;
   if (f16w) {   // fp16 weights: four stages
-    p.wtma = 0;
     const size_t smem = CfgH::kRingBytes + (size_t)CfgH::kStages * w_stage_e<kWF16>() + 1024 + 256;
     cudaFuncSetAttribute(gemm_q4_tc<CfgH, kWF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     gemm_q4_tc<CfgH, kWF16><<<grid, CfgH::kThreads, smem, c->stream>>>(tm, p);
@@ -1150,6 +1245,12 @@ p0_status p0_gemm(p0_ctx *c, const p0_gemm_args *a, double *flops) {
     gemm_q4_tc<Cfg1, kWQ4><<<grid, Cfg1::kThreads, smem, c->stream>>>(tm, p);
   }
   if ((st = p0_launched(c, "gemm"))) return st;
+  if (S > 1u) {
+    const uint64_t n4 = (uint64_t)M * (N / 4);
+    const unsigned blocks = (unsigned)((n4 + 255) / 256 < (uint64_t)c->sm_count * 8 ? (n4 + 255) / 256 : (uint64_t)c->sm_count * 8);
+    gemm_ksplit_epilogue<<<blocks, 256, 0, c->stream>>>((const float *)(wsp + xws), S, (size_t)M * N, pe);
+    if ((st = p0_launched(c, "gemm k-split epilogue"))) return st;
+  }
   if (flops) *flops = 2.0 * M * N * K;
   return P0_OK;
 }

@@ -15,6 +15,7 @@ import pytest
 from oracle import ref
 
 from .test_gpu_gemm_heads import rope_table, run_heads
+from .test_gpu_gemm_xpro import _case as xpro_case
 from .test_gpu_parity import assert_close, run_gemm
 
 pytestmark = pytest.mark.gpu
@@ -108,3 +109,40 @@ def test_persistent_many_tiles_swiglu_resadd(g, monkeypatch):
     r0 = ref.randn(M * N, 217)
     y2 = run_gemm(g, b, X, M, N, K, y_init=r0.copy(), epi="resadd", ev=(gate, 0), bv=(bv, 0), store=False)
     assert_close(y2, ref.gemm(b, X, M, N, K, epi="resadd", ev=gate, bv=bv, store=False, Y=r0.copy(), threads=0))
+
+
+# ---------------------------------------------------------------- k split (grids that fill at most half the SMs)
+@pytest.mark.parametrize("ks", ["auto", "3"])
+@pytest.mark.parametrize("gemm_form", ["7", "1"], ids=["k128", "cfg1"])
+def test_ksplit_epilogues(g, monkeypatch, gemm_form, ks):
+    # 130 tokens x 512 rows = 4 CTAs: the library splits K (2080 = 16.25 x 128: the last split ends on a one-group
+    # stage); each split stores f32 partials, a second pass sums them in order and applies the epilogue
+    monkeypatch.setenv("P0MM_GEMM", gemm_form)
+    if ks != "auto":
+        monkeypatch.setenv("P0MM_GEMM_KSPLIT", ks)
+    M, N, K = 130, 512, 2080
+    b, _ = ref.pack_q4(ref.randn(N * K, 220, 0.02), N, K)
+    X = ref.f2h(ref.round_f16(ref.randn(M * K, 221)))
+    bias, gate = ref.randn(N, 222, 0.01), ref.randn(N, 223, 1.0)
+    y = run_gemm(g, b, X, M, N, K)
+    assert_close(ref.h2f(y), ref.h2f(ref.gemm(b, X, M, N, K, threads=0)))
+    y0 = ref.f2h(ref.randn(M * N, 224, 0.5))
+    y = run_gemm(g, b, X, M, N, K, y_init=y0.copy(), epi="bias", ev=(bias, 0), res=True, post_gelu=True)
+    want = ref.gemm(b, X, M, N, K, epi="bias", ev=bias, res=True, post_gelu=True, Y=y0.copy(), threads=0)
+    assert_close(ref.h2f(y), ref.h2f(want))
+    r0 = ref.randn(M * N, 225)
+    y = run_gemm(g, b, X, M, N, K, y_init=r0.copy(), epi="resadd", ev=(gate, 0), bv=(bias, 0), store=False)
+    assert_close(y, ref.gemm(b, X, M, N, K, epi="resadd", ev=gate, bv=bias, store=False, Y=r0.copy(), threads=0))
+    yf = run_gemm(g, b, X, M, N, K, y_bytes=M * N * 4, epi="f32")
+    assert_close(yf, ref.gemm(b, X, M, N, K, epi="f32", threads=0))
+
+
+def test_ksplit_with_x_prologue(g, monkeypatch):
+    # the workspace holds the lnmod prologue's fp16 X and the splits' partials side by side
+    monkeypatch.setenv("P0MM_GEMM_KSPLIT", "4")
+    M, N, K = 40, 256, 1024
+    b, _ = ref.pack_q4(ref.randn(N * K, 226, 0.02), N, K)
+    X, st, pv = xpro_case(M, K, 227, K, 0, 0, 0, K)
+    y = run_gemm(g, b, X, M, N, K, x={"mode": "lnmod"}, _stats=(st, 0), _pv=(pv, 0, K))
+    X16 = ref.gemm_xpro("lnmod", X, M, K, stats=st, pv=pv, pv_stride=K)
+    assert_close(ref.h2f(y), ref.h2f(ref.gemm(b, X16, M, N, K, threads=0)))
