@@ -492,9 +492,9 @@ def _memcpy_d2d(dst, src, nbytes, stream):
 def run_e2e(args, sw, g, torch, dist, gather):
     """the same sweep through the public API with host buffers: every step, x from pinned host memory -> device, the
     12 calls, results device -> pinned host; wall-clock over the steps (max over ranks). Run as a serving loop runs it:
-    two sets of device inputs / outputs and pinned outputs alternate, the copies go on a second stream (the copy
-    engines) so that step s's downloads and step s+1's uploads overlap the kernels, and the host waits for step s-2's
-    results before it enqueues step s (two steps in flight). Events order each buffer's reuse: an upload waits for the compute two steps
+    two sets of device inputs / outputs and pinned outputs alternate, uploads and downloads go on two more streams (the
+    two copy engines) so that step s's downloads and step s+1's uploads overlap the kernels and neither waits behind
+    the other, and the host waits for step s-2's results before it enqueues step s (two steps in flight). Events order each buffer's reuse: an upload waits for the compute two steps
     back that read its buffer, a compute waits for its upload and for the download two steps back of its outputs."""
     h2d = d2h = 0
     pin_in, pin_out = [], [[], []]
@@ -517,7 +517,7 @@ def run_e2e(args, sw, g, torch, dist, gather):
                     g.write(mxb, np.full(1, 0.9, np.float32), dst_off=c["stat_off"] * 4)
             sets[b].append((c, xb.ptr, (mxb if c["head"] else yb).ptr, xb, yb, mxb))
     comp = torch.cuda.current_stream()
-    cps = torch.cuda.Stream()
+    ups, downs = torch.cuda.Stream(), torch.cuda.Stream()   # uploads and downloads on their own copy engines
 
     def use(b):
         for c, _, _, xb, yb, mxb in sets[b]:
@@ -541,19 +541,19 @@ def run_e2e(args, sw, g, torch, dist, gather):
     def step(s):
         b = s & 1
         d2h_done[b].synchronize()                     # step s - 2's results are on the host (its pinned set is free)
-        cps.wait_event(comp_done[b])                 # the compute two steps back has read these inputs
+        ups.wait_event(comp_done[b])                 # the compute two steps back has read these inputs
         for (c, xp, _, _, _, _), t in zip(sets[b], pin_in):
-            _memcpy_h2d(xp, t.data_ptr(), t.numel() * 4, cps.cuda_stream)
-        h2d_done[b].record(cps)
+            _memcpy_h2d(xp, t.data_ptr(), t.numel() * 4, ups.cuda_stream)
+        h2d_done[b].record(ups)
         comp.wait_event(h2d_done[b])
         comp.wait_event(d2h_done[b])                 # the download two steps back has read these outputs
         graphs[s % len(graphs)].replay()
         gather([op for _, _, op, _, _, _ in sets[b]])
         comp_done[b].record(comp)
-        cps.wait_event(comp_done[b])
+        downs.wait_event(comp_done[b])
         for (c, _, op, _, _, _), o in zip(sets[b], pin_out[b]):
-            _memcpy_d2h(o.data_ptr(), op, o.numel() * 4, cps.cuda_stream)
-        d2h_done[b].record(cps)
+            _memcpy_d2h(o.data_ptr(), op, o.numel() * 4, downs.cuda_stream)
+        d2h_done[b].record(downs)
 
     steps = max(20, args.steps)
     for s in range(len(graphs) + 4):               # every graph replayed once (its first launch uploads it)
@@ -576,7 +576,8 @@ def run_e2e(args, sw, g, torch, dist, gather):
     return {"value": round(val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": round(dt / steps * 1e3, 4),
             "path": "p0pc0rn_b200.gemv/gemvM (ctypes -> libp0mm.so C ABI) recorded as one CUDA graph per step; "
-                    "pinned host x in, outputs out every step; copies on a second stream, two buffer sets, two steps in flight"}
+                    "pinned host x in, outputs out every step; uploads and downloads on their own streams, two buffer sets, two steps "
+                    "in flight"}
 
 
 def _memcpy_h2d(dst, src, nbytes, stream):
