@@ -22,6 +22,10 @@ constexpr int kV3Warps = 16;
 constexpr int kV3Threads = 32 * kV3Warps;
 constexpr uint32_t kV3Slot = 2560;
 constexpr uint32_t kV3MaxSlots = 4;
+// G4 (M = 1, whole tiles, no geglu pair): a slot holds four consecutive groups of a tile, each record 1312 bytes after
+// the previous one (1280 + 32: the four records' rows then fall in different shared-memory banks)
+constexpr uint32_t kG4Rec = 1312;
+constexpr uint32_t kG4Slot = 4u * kG4Rec;
 
 // x staging (v2's): B fragments of x * sigma as fp16 hi / lo in the permuted k order, and per (group, token) sum(x) / f
 // in f32. Returns f = 2^24 / sigma.
@@ -77,14 +81,23 @@ __device__ float stage_x_v3(const GemvParams &p, uint32_t G, uint4 *xb, float *x
 // SPLIT (calls with fewer tiles than warps, e.g. a column-split head on several GPUs): each tile is cut into S k-parts
 // (runs of stages), and the parts are the units dealt to the warps; a warp writes its part's row totals to shared memory
 // and, after the CTA's barrier, the warps sum each tile's parts in part order and run the epilogue.
-template <int MT, bool PAIR, bool SPLIT>
+//
+// G4: the M = 1 form with one group per lane of a quad. The MMA's 16 k slots hold four groups (the slots of lane c,
+// 2c, 2c+1, 2c+8, 2c+9, carry group c's codes, four per MMA), and B's column n holds group n / 2's x (hi for even n,
+// lo for odd n) in the slots of that group and zeros elsewhere, so D's columns 2c, 2c+1 are group c's hi and lo sums
+// for the lane's two rows: each lane converts only its own group's (s, mn) and scales only its own sums (a quarter of
+// the generic form's conversions and FMAs at M = 1, where six of the eight D columns are empty). Eight MMAs per row
+// block walk the group's four code words; the row totals are summed over the quad's lanes at the end of the tile.
+template <int MT, bool PAIR, bool SPLIT, bool G4 = false>
 __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, const uint32_t gx, const uint32_t nslot, const uint32_t S_arg) {
+  static_assert(!G4 || (MT == 1 && !PAIR && !SPLIT), "G4 is the whole-tile M = 1 form");
+  constexpr uint32_t kSlotB = G4 ? kG4Slot : kV3Slot;
   const uint32_t S = SPLIT ? S_arg : 1u;   // whole tiles fold every part computation away
   constexpr bool PACK = MT <= 4;
   constexpr int NP = PAIR ? 2 : 1;
   extern __shared__ __align__(128) uint8_t smem8[];
   uint8_t *ring = smem8;                                                              // [warp][slot] x 2560 B
-  uint64_t *full = reinterpret_cast<uint64_t *>(ring + (size_t)kV3Warps * nslot * kV3Slot);
+  uint64_t *full = reinterpret_cast<uint64_t *>(ring + (size_t)kV3Warps * nslot * kSlotB);
   float *scratch = reinterpret_cast<float *>(full + kV3Warps * kV3MaxSlots);          // 32 floats
   volatile uint32_t *abort_flag = reinterpret_cast<volatile uint32_t *>(scratch + 24);
   uint4 *xb = reinterpret_cast<uint4 *>(scratch + 32);                                // [G][MT][4][2]
@@ -93,7 +106,7 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
   float *pbuf = xsum + (size_t)G * MT;                                                // S > 1: [unit][lane][16] totals
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t g = lane >> 2, c = lane & 3;
-  const uint32_t ntile = p.N / 64, spt = PAIR ? G : (G + 1) / 2;   // stages per tile
+  const uint32_t ntile = p.N / 64, spt = G4 ? (G + 3) / 4 : PAIR ? G : (G + 1) / 2;   // stages per tile
   const size_t tile_bytes = (size_t)p.wG * 1280u, pair_off = (size_t)ntile * tile_bytes;
   // CTA b owns the contiguous tiles [b*ntile/gx, (b+1)*ntile/gx) (27 or 28 of the head's 4096 on 148 SMs), dealt to its
   // warps round-robin: every SM gets the same share of the work
@@ -107,7 +120,7 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
     const uint32_t part = (unit0 + k * ustride) % S;
     nstage += (part + 1u) * spt / S - part * spt / S;
   }
-  uint8_t *myring = ring + (size_t)warp * nslot * kV3Slot;
+  uint8_t *myring = ring + (size_t)warp * nslot * kSlotB;
   uint64_t *myfull = full + warp * kV3MaxSlots;
   if (lane == 0) {
     for (uint32_t i = 0; i < nslot; i++) tc::mbar_init(&myfull[i], 1);
@@ -126,8 +139,12 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
   };
   if (nunits) unit_begin(0);
   auto issue_next = [&](uint32_t slot) {
-    uint8_t *dst = myring + (size_t)slot * kV3Slot;
-    if (PAIR) {
+    uint8_t *dst = myring + (size_t)slot * kSlotB;
+    if (G4) {
+      const uint32_t gs = 4u * ni_s, cnt = G - gs < 4u ? G - gs : 4u;
+      tc::mbar_expect_tx(&myfull[slot], cnt * 1280u);
+      for (uint32_t i = 0; i < cnt; i++) bulk_g2s(dst + i * kG4Rec, ni_src + (size_t)(gs + i) * 1280u, 1280u, &myfull[slot]);
+    } else if (PAIR) {
       tc::mbar_expect_tx(&myfull[slot], 2560u);
       bulk_g2s(dst, ni_src + (size_t)ni_s * 1280u, 1280u, &myfull[slot]);
       bulk_g2s(dst + 1280u, ni_src + pair_off + (size_t)ni_s * 1280u, 1280u, &myfull[slot]);
@@ -198,80 +215,173 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
         }
     }
   };
-  for (uint32_t ui = 0; ui < nunits && ok; ui++) {
-    const uint32_t u = unit0 + ui * ustride, tile = u / S, part = u % S;
-    const uint32_t st0 = part * spt / S, st1 = (part + 1u) * spt / S;
-    float acc[2][NP][4][4];   // [group parity] -> independent FMA chains for the two groups of a slot
+  if constexpr (G4) {
+    // ---- G4 main loop (M = 1): lane (g, c) takes group 4 * st + c of every stage, rows 16r + 8j + g of the tile
+    const uint32_t rec_off = c * kG4Rec;
+    const bool bcol = c == (g >> 1u);      // this lane's B column n = g belongs to its own group: x (hi / lo), else 0
+    const uint32_t blo = g & 1u;
+    for (uint32_t ui = 0; ui < nunits && ok; ui++) {
+      const uint32_t tile = unit0 + ui * ustride;
+      float acc[4][2];
 #pragma unroll
-    for (int h = 0; h < 2; h++)
-#pragma unroll
-      for (int a = 0; a < NP; a++)
+      for (int r = 0; r < 4; r++) acc[r][0] = acc[r][1] = 0.0f;
+      for (uint32_t st = 0; st < spt; st++) {
+        const bool got = tc::mbar_wait(&myfull[cs], cph, abort_flag, p.err, 0x511u, P0_SPIN_LIMIT);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        consumed++;
+        const uint32_t gg = 4u * st + c;
+        const bool live = gg < G;          // the tile's last stage may hold fewer than four groups
+        const uint32_t rec = ring_s + cs * kSlotB + rec_off;
+        uint4 cw[4][2];
+        uint32_t tl[4][2];
 #pragma unroll
         for (int r = 0; r < 4; r++)
 #pragma unroll
-          for (int i = 0; i < 4; i++) acc[h][a][r][i] = 0.0f;
-    for (uint32_t st = st0; st < st1; st++) {
-      const bool got = tc::mbar_wait(&myfull[cs], cph, abort_flag, p.err, 0x511u, P0_SPIN_LIMIT);
-      if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
-      consumed++;
-      const uint32_t sl = ring_s + cs * kV3Slot;
-      const bool two = PAIR || 2u * st + 1u < G;   // PAIR: gate and up records of one group; else two groups
-      const uint32_t gg0 = PAIR ? st : 2u * st, gg1 = PAIR ? st : gg0 + 1u;
-      // all shared loads of the slot first
-      Rec q0, q1;
-      rec_load(q0, sl, lane_row16, tail_off);
-      if (two) rec_load(q1, sl + 1280u, lane_row16, tail_off);
-      uint4 bh0 = make_uint4(0, 0, 0, 0), bl0 = bh0, bh1 = bh0, bl1 = bh0;
-      float x00 = 0.0f, x01 = 0.0f, x10 = 0.0f, x11 = 0.0f;
-      if (tok_ok) {
-        bh0 = lds128(xb_lane + gg0 * MT * 128u);
-        if (!PACK) bl0 = lds128(xb_lane + gg0 * MT * 128u + 16u);
-        if (!PAIR && two) {
-          bh1 = lds128(xb_lane + gg1 * MT * 128u);
-          if (!PACK) bl1 = lds128(xb_lane + gg1 * MT * 128u + 16u);
+          for (int j = 0; j < 2; j++) {
+            const uint32_t row = 16u * r + 8u * j + g;
+            cw[r][j] = lds128(rec + row * 16u);
+            tl[r][j] = lds32(rec + 1024u + row * 4u);
+          }
+        uint4 bx[4];
+        float xs = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 4; w++) bx[w] = make_uint4(0, 0, 0, 0);
+        if (live) {
+          xs = __uint_as_float(lds32(xsum_s + gg * 4u));
+          if (bcol) {
+#pragma unroll
+            for (int w = 0; w < 4; w++) bx[w] = lds128(xb_s + ((gg * 4u + w) * 2u + blo) * 16u);
+          }
+        }
+        // every lane has read the slot: lane 0 refills it with the stage nslot ahead
+        __syncwarp();
+        if (lane == 0 && issued < nstage) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issue_next(cs);
+        }
+        if (++cs == nslot) { cs = 0; cph ^= 1u; }
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+          float d0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          const uint32_t wa[4] = {cw[r][0].x, cw[r][0].y, cw[r][0].z, cw[r][0].w};
+          const uint32_t wb[4] = {cw[r][1].x, cw[r][1].y, cw[r][1].z, cw[r][1].w};
+#pragma unroll
+          for (int w = 0; w < 4; w++) {
+            const uint32_t a = wa[w], b = wb[w];
+            const uint32_t as = __umulhi(a, 1u << 24), bs = __umulhi(b, 1u << 24);   // >> 8 on the multiplier pipe
+            const uint32_t A0[4] = {a & 0x000F000Fu, b & 0x000F000Fu, a & 0x00F000F0u, b & 0x00F000F0u};
+            const uint32_t A1[4] = {as & 0x000F000Fu, bs & 0x000F000Fu, as & 0x00F000F0u, bs & 0x00F000F0u};
+            if (w & 1) {
+              mma16816(d1, A0, bx[w].x, bx[w].y);
+              mma16816(d1, A1, bx[w].z, bx[w].w);
+            } else {
+              mma16816(d0, A0, bx[w].x, bx[w].y);
+              mma16816(d0, A1, bx[w].z, bx[w].w);
+            }
+          }
+          if (live) {
+            // D columns 2c, 2c+1: this group's hi and lo sums for rows g (d[0], d[1]) and g + 8 (d[2], d[3])
+            const float vg = __fadd_rn(__fadd_rn(d0[0], d1[0]), __fadd_rn(d0[1], d1[1]));
+            const float vg8 = __fadd_rn(__fadd_rn(d0[2], d1[2]), __fadd_rn(d0[3], d1[3]));
+            const __half2 h0 = *reinterpret_cast<const __half2 *>(&tl[r][0]), h1 = *reinterpret_cast<const __half2 *>(&tl[r][1]);
+            uint64_t av = pk2(acc[r][0], acc[r][1]);
+            av = ffma2(pk2(__high2float(h0), __high2float(h1)), pk2(xs, xs), av);
+            av = ffma2(pk2(__low2float(h0), __low2float(h1)), pk2(vg, vg8), av);
+            upk2(av, acc[r][0], acc[r][1]);
+          }
         }
       }
-      if (xs_lane) {
-        if (2 * c < MT) { x00 = __uint_as_float(lds32(xs_addr + gg0 * MT * 4u)); x10 = __uint_as_float(lds32(xs_addr + gg1 * MT * 4u)); }
-        if (2 * c + 1 < MT) { x01 = __uint_as_float(lds32(xs_addr + gg0 * MT * 4u + 4u)); x11 = __uint_as_float(lds32(xs_addr + gg1 * MT * 4u + 4u)); }
-      }
-      // every lane has read the slot: lane 0 refills it with the stage nslot ahead (generic reads before the
-      // async-proxy write: warp sync, then a proxy fence); the math below uses registers only
-      __syncwarp();
-      if (lane == 0 && issued < nstage) {
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        issue_next(cs);
-      }
-      if (++cs == nslot) { cs = 0; cph ^= 1u; }
-      if (PAIR) {
-        rec_math<MT, PACK>(acc[0][0], q0, bh0, bl0, x00, x01);
-        rec_math<MT, PACK>(acc[1][NP - 1], q1, bh0, bl0, x00, x01);
-      } else {
-        rec_math<MT, PACK>(acc[0][0], q0, bh0, bl0, x00, x01);
-        if (two) rec_math<MT, PACK>(acc[1][0], q1, bh1, bl1, x10, x11);
-      }
-    }
-    if (!ok) break;
-    // row totals: f * (the two parities' sums); PACK: add the x-lo lanes c = 2, 3
-    float tot[NP][4][4];
-#pragma unroll
-    for (int a = 0; a < NP; a++)
+      if (!ok) break;
+      // row totals: the quad's four groups (lanes c), then f; the epilogue reads token 0 from lanes c = 0
+      float tot[NP][4][4];
 #pragma unroll
       for (int r = 0; r < 4; r++)
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-          float v = PAIR ? acc[a][a][r][i] * f : (acc[0][a][r][i] + acc[1][a][r][i]) * f;
-          if (PACK) v += __shfl_xor_sync(0xffffffffu, v, 2);
-          tot[a][r][i] = v;
+        for (int j = 0; j < 2; j++) {
+          float v = acc[r][j];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          tot[0][r][2 * j] = v * f;
+          tot[0][r][2 * j + 1] = 0.0f;
         }
-    if (!SPLIT) {
       tile_epilogue(tile, tot);
-    } else {
-      float *pb = pbuf + ((size_t)(u - U0) * 32u + lane) * 16u;
-#pragma unroll
-      for (int r = 0; r < 4; r++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) pb[r * 4 + i] = tot[0][r][i];
+    }
+  } else {
+    for (uint32_t ui = 0; ui < nunits && ok; ui++) {
+      const uint32_t u = unit0 + ui * ustride, tile = u / S, part = u % S;
+      const uint32_t st0 = part * spt / S, st1 = (part + 1u) * spt / S;
+      float acc[2][NP][4][4];   // [group parity] -> independent FMA chains for the two groups of a slot
+  #pragma unroll
+      for (int h = 0; h < 2; h++)
+  #pragma unroll
+        for (int a = 0; a < NP; a++)
+  #pragma unroll
+          for (int r = 0; r < 4; r++)
+  #pragma unroll
+            for (int i = 0; i < 4; i++) acc[h][a][r][i] = 0.0f;
+      for (uint32_t st = st0; st < st1; st++) {
+        const bool got = tc::mbar_wait(&myfull[cs], cph, abort_flag, p.err, 0x511u, P0_SPIN_LIMIT);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        consumed++;
+        const uint32_t sl = ring_s + cs * kV3Slot;
+        const bool two = PAIR || 2u * st + 1u < G;   // PAIR: gate and up records of one group; else two groups
+        const uint32_t gg0 = PAIR ? st : 2u * st, gg1 = PAIR ? st : gg0 + 1u;
+        // all shared loads of the slot first
+        Rec q0, q1;
+        rec_load(q0, sl, lane_row16, tail_off);
+        if (two) rec_load(q1, sl + 1280u, lane_row16, tail_off);
+        uint4 bh0 = make_uint4(0, 0, 0, 0), bl0 = bh0, bh1 = bh0, bl1 = bh0;
+        float x00 = 0.0f, x01 = 0.0f, x10 = 0.0f, x11 = 0.0f;
+        if (tok_ok) {
+          bh0 = lds128(xb_lane + gg0 * MT * 128u);
+          if (!PACK) bl0 = lds128(xb_lane + gg0 * MT * 128u + 16u);
+          if (!PAIR && two) {
+            bh1 = lds128(xb_lane + gg1 * MT * 128u);
+            if (!PACK) bl1 = lds128(xb_lane + gg1 * MT * 128u + 16u);
+          }
+        }
+        if (xs_lane) {
+          if (2 * c < MT) { x00 = __uint_as_float(lds32(xs_addr + gg0 * MT * 4u)); x10 = __uint_as_float(lds32(xs_addr + gg1 * MT * 4u)); }
+          if (2 * c + 1 < MT) { x01 = __uint_as_float(lds32(xs_addr + gg0 * MT * 4u + 4u)); x11 = __uint_as_float(lds32(xs_addr + gg1 * MT * 4u + 4u)); }
+        }
+        // every lane has read the slot: lane 0 refills it with the stage nslot ahead (generic reads before the
+        // async-proxy write: warp sync, then a proxy fence); the math below uses registers only
+        __syncwarp();
+        if (lane == 0 && issued < nstage) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issue_next(cs);
+        }
+        if (++cs == nslot) { cs = 0; cph ^= 1u; }
+        if (PAIR) {
+          rec_math<MT, PACK>(acc[0][0], q0, bh0, bl0, x00, x01);
+          rec_math<MT, PACK>(acc[1][NP - 1], q1, bh0, bl0, x00, x01);
+        } else {
+          rec_math<MT, PACK>(acc[0][0], q0, bh0, bl0, x00, x01);
+          if (two) rec_math<MT, PACK>(acc[1][0], q1, bh1, bl1, x10, x11);
+        }
+      }
+      if (!ok) break;
+      // row totals: f * (the two parities' sums); PACK: add the x-lo lanes c = 2, 3
+      float tot[NP][4][4];
+  #pragma unroll
+      for (int a = 0; a < NP; a++)
+  #pragma unroll
+        for (int r = 0; r < 4; r++)
+  #pragma unroll
+          for (int i = 0; i < 4; i++) {
+            float v = PAIR ? acc[a][a][r][i] * f : (acc[0][a][r][i] + acc[1][a][r][i]) * f;
+            if (PACK) v += __shfl_xor_sync(0xffffffffu, v, 2);
+            tot[a][r][i] = v;
+          }
+      if (!SPLIT) {
+        tile_epilogue(tile, tot);
+      } else {
+        float *pb = pbuf + ((size_t)(u - U0) * 32u + lane) * 16u;
+  #pragma unroll
+        for (int r = 0; r < 4; r++)
+  #pragma unroll
+          for (int i = 0; i < 4; i++) pb[r * 4 + i] = tot[0][r][i];
+      }
     }
   }
   // copies this warp issued but did not consume (only after a failed wait) land before the CTA exits (bounded)
@@ -306,6 +416,7 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
 }
 
 typedef void (*V3Kernel)(const GemvParams, const uint32_t, const uint32_t, const uint32_t);
+V3Kernel v3_kernel_g4() { return gemv_q4_v3<1, false, false, true>; }
 template <int MT>
 V3Kernel v3_kernel_m(bool pair, bool split) {
   return pair ? gemv_q4_v3<MT, true, false> : split ? gemv_q4_v3<MT, false, true> : gemv_q4_v3<MT, false, false>;
@@ -322,8 +433,8 @@ V3Kernel v3_kernel_for(uint32_t M, bool pair, bool split) {
     default: return v3_kernel_m<8>(pair, split);
   }
 }
-size_t v3_smem(uint32_t M, uint32_t G, uint32_t nslot) {
-  return (size_t)kV3Warps * nslot * kV3Slot + kV3Warps * kV3MaxSlots * 8 + 32 * 4 + (size_t)G * M * 128 + (size_t)G * M * 4;
+size_t v3_smem(uint32_t M, uint32_t G, uint32_t nslot, uint32_t slotb = kV3Slot) {
+  return (size_t)kV3Warps * nslot * slotb + kV3Warps * kV3MaxSlots * 8 + 32 * 4 + (size_t)G * M * 128 + (size_t)G * M * 4;
 }
 uint32_t v3_slots(uint32_t M, uint32_t G) {
   for (uint32_t n = kV3MaxSlots; n >= 2; n--)
@@ -374,8 +485,16 @@ cudaError_t launch_v3(const GemvParams &p, int sms, cudaStream_t s) {
   if (S > 1 && v3_slots_with(p.M, G, v3_pbuf(ntile, sms, S)) < 2) S = 1;   // the parts' totals do not fit beside a ring
   V3Kernel k = v3_kernel_for(p.M, pair, S > 1);
   const size_t pb = v3_pbuf(ntile, sms, S);
-  const uint32_t nslot = v3_slots_with(p.M, G, pb);
-  const size_t smem = v3_smem(p.M, G, nslot) + pb;
+  uint32_t nslot = v3_slots_with(p.M, G, pb);
+  size_t smem = v3_smem(p.M, G, nslot) + pb;
+  // M = 1 whole tiles: the one-group-per-lane form (two 4-group slots per warp, the same bytes in flight) when it fits;
+  // P0MM_V3_G4=0, a tuning override read on every call, keeps the generic form
+  const char *g4v = getenv("P0MM_V3_G4");
+  if (p.M == 1 && !pair && S == 1 && !(g4v && g4v[0] == '0') && v3_smem(1, G, 2, kG4Slot) <= 220u * 1024u) {
+    k = v3_kernel_g4();
+    nslot = 2;
+    smem = v3_smem(1, G, 2, kG4Slot);
+  }
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const uint32_t need = S == 1 ? (ntile + kV3Warps - 1) / kV3Warps : ntile;
   uint32_t gx = (uint32_t)sms;
