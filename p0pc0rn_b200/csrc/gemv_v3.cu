@@ -88,9 +88,13 @@ __device__ float stage_x_v3(const GemvParams &p, uint32_t G, uint4 *xb, float *x
 // for the lane's two rows: each lane converts only its own group's (s, mn) and scales only its own sums (a quarter of
 // the generic form's conversions and FMAs at M = 1, where six of the eight D columns are empty). Eight MMAs per row
 // block walk the group's four code words; the row totals are summed over the quad's lanes at the end of the tile.
+// At M = 2 (G2) an MMA holds two groups: lanes c = 0, 1 carry group 2p's code words 0-1 and 2-3, lanes 2, 3 group
+// 2p + 1's; B's column n is token (n / 2) % 2 of group n / 4 (hi / lo by n's parity). D's columns 2c, 2c+1 are then
+// group c / 2's hi and lo sums for token c % 2: a lane converts and scales one group and token per MMA pair (half of
+// the generic form's work); per tile, the token's total is the sum of lanes c and c ^ 2.
 template <int MT, bool PAIR, bool SPLIT, bool G4 = false>
 __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, const uint32_t gx, const uint32_t nslot, const uint32_t S_arg) {
-  static_assert(!G4 || (MT == 1 && !PAIR && !SPLIT), "G4 is the whole-tile M = 1 form");
+  static_assert(!G4 || ((MT == 1 || MT == 2) && !PAIR && !SPLIT), "G4 is the whole-tile form for M = 1 and 2");
   constexpr uint32_t kSlotB = G4 ? kG4Slot : kV3Slot;
   const uint32_t S = SPLIT ? S_arg : 1u;   // whole tiles fold every part computation away
   constexpr bool PACK = MT <= 4;
@@ -215,7 +219,99 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
         }
     }
   };
-  if constexpr (G4) {
+  if constexpr (G4 && MT == 2) {
+    // ---- G2 main loop (M = 2): per stage, pairs p = 0, 1 of groups; lane (g, c) takes group 4 * st + 2p + c / 2,
+    // its code words 2 (c % 2) and 2 (c % 2) + 1, token c % 2; rows 16r + 8j + g of the tile
+    const uint32_t half = c >> 1u, tk = c & 1u, wofs = 8u * (c & 1u);   // word pair of the lane: bytes 8 (c % 2)
+    // B: this lane supplies column g for its own slots, nonzero when column g's group (g / 4) is the lane's (c / 2)
+    const bool bcol = half == (g >> 2u);
+    const uint32_t btk = (g >> 1u) & 1u, blo = g & 1u;
+    for (uint32_t ui = 0; ui < nunits && ok; ui++) {
+      const uint32_t tile = unit0 + ui * ustride;
+      float acc[4][2];
+#pragma unroll
+      for (int r = 0; r < 4; r++) acc[r][0] = acc[r][1] = 0.0f;
+      for (uint32_t st = 0; st < spt; st++) {
+        const bool got = tc::mbar_wait(&myfull[cs], cph, abort_flag, p.err, 0x511u, P0_SPIN_LIMIT);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        consumed++;
+        uint2 cw[2][4][2];
+        uint32_t tl[2][4][2];
+        uint4 bx[2][2];
+        float xs[2] = {0.0f, 0.0f};
+        bool live[2];
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+          const uint32_t ri = 2u * q + half, gg = 4u * st + ri;
+          live[q] = gg < G;
+          const uint32_t rec = ring_s + cs * kSlotB + ri * kG4Rec;
+#pragma unroll
+          for (int r = 0; r < 4; r++)
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+              const uint32_t row = 16u * r + 8u * j + g;
+              asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(cw[q][r][j].x), "=r"(cw[q][r][j].y) : "r"(rec + row * 16u + wofs));
+              tl[q][r][j] = lds32(rec + 1024u + row * 4u);
+            }
+          bx[q][0] = bx[q][1] = make_uint4(0, 0, 0, 0);
+          if (live[q]) {
+            xs[q] = __uint_as_float(lds32(xsum_s + (gg * 2u + tk) * 4u));
+            const uint32_t gb = 4u * st + 2u * q + (g >> 2u);   // column g's group
+            if (bcol) {
+#pragma unroll
+              for (int w = 0; w < 2; w++) bx[q][w] = lds128(xb_s + ((gb * 8u + btk * 4u + 2u * (c & 1u) + w) * 2u + blo) * 16u);
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0 && issued < nstage) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issue_next(cs);
+        }
+        if (++cs == nslot) { cs = 0; cph ^= 1u; }
+#pragma unroll
+        for (int q = 0; q < 2; q++)
+#pragma unroll
+          for (int r = 0; r < 4; r++) {
+            float d0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const uint32_t wa[2] = {cw[q][r][0].x, cw[q][r][0].y}, wb[2] = {cw[q][r][1].x, cw[q][r][1].y};
+#pragma unroll
+            for (int w = 0; w < 2; w++) {
+              const uint32_t a = wa[w], b = wb[w];
+              const uint32_t as = __umulhi(a, 1u << 24), bs = __umulhi(b, 1u << 24);
+              const uint32_t A0[4] = {a & 0x000F000Fu, b & 0x000F000Fu, a & 0x00F000F0u, b & 0x00F000F0u};
+              const uint32_t A1[4] = {as & 0x000F000Fu, bs & 0x000F000Fu, as & 0x00F000F0u, bs & 0x00F000F0u};
+              float(&dd)[4] = w ? d1 : d0;
+              mma16816(dd, A0, bx[q][w].x, bx[q][w].y);
+              mma16816(dd, A1, bx[q][w].z, bx[q][w].w);
+            }
+            if (live[q]) {
+              const float vg = __fadd_rn(__fadd_rn(d0[0], d1[0]), __fadd_rn(d0[1], d1[1]));
+              const float vg8 = __fadd_rn(__fadd_rn(d0[2], d1[2]), __fadd_rn(d0[3], d1[3]));
+              const __half2 h0 = *reinterpret_cast<const __half2 *>(&tl[q][r][0]), h1 = *reinterpret_cast<const __half2 *>(&tl[q][r][1]);
+              uint64_t av = pk2(acc[r][0], acc[r][1]);
+              av = ffma2(pk2(__high2float(h0), __high2float(h1)), pk2(xs[q], xs[q]), av);
+              av = ffma2(pk2(__low2float(h0), __low2float(h1)), pk2(vg, vg8), av);
+              upk2(av, acc[r][0], acc[r][1]);
+            }
+          }
+      }
+      if (!ok) break;
+      // token totals: lanes c and c ^ 2 hold the two halves of the groups; lane c = 0 takes token 0 and token 1 (lane 1)
+      float tot[NP][4][4];
+#pragma unroll
+      for (int r = 0; r < 4; r++)
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+          float v = acc[r][j];
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          const float o = __shfl_xor_sync(0xffffffffu, v, 1);
+          tot[0][r][2 * j] = v * f;
+          tot[0][r][2 * j + 1] = o * f;
+        }
+      tile_epilogue(tile, tot);
+    }
+  } else if constexpr (G4) {
     // ---- G4 main loop (M = 1): lane (g, c) takes group 4 * st + c of every stage, rows 16r + 8j + g of the tile
     const uint32_t rec_off = c * kG4Rec;
     const bool bcol = c == (g >> 1u);      // this lane's B column n = g belongs to its own group: x (hi / lo), else 0
@@ -416,7 +512,7 @@ __global__ void __launch_bounds__(kV3Threads, 1) gemv_q4_v3(const GemvParams p, 
 }
 
 typedef void (*V3Kernel)(const GemvParams, const uint32_t, const uint32_t, const uint32_t);
-V3Kernel v3_kernel_g4() { return gemv_q4_v3<1, false, false, true>; }
+V3Kernel v3_kernel_g4(uint32_t M) { return M == 1 ? gemv_q4_v3<1, false, false, true> : gemv_q4_v3<2, false, false, true>; }
 template <int MT>
 V3Kernel v3_kernel_m(bool pair, bool split) {
   return pair ? gemv_q4_v3<MT, true, false> : split ? gemv_q4_v3<MT, false, true> : gemv_q4_v3<MT, false, false>;
@@ -487,13 +583,13 @@ cudaError_t launch_v3(const GemvParams &p, int sms, cudaStream_t s) {
   const size_t pb = v3_pbuf(ntile, sms, S);
   uint32_t nslot = v3_slots_with(p.M, G, pb);
   size_t smem = v3_smem(p.M, G, nslot) + pb;
-  // M = 1 whole tiles: the one-group-per-lane form (two 4-group slots per warp, the same bytes in flight) when it fits;
+  // M = 1 / 2 whole tiles: the grouped forms (two 4-group slots per warp, the same bytes in flight) when they fit;
   // P0MM_V3_G4=0, a tuning override read on every call, keeps the generic form
   const char *g4v = getenv("P0MM_V3_G4");
-  if (p.M == 1 && !pair && S == 1 && !(g4v && g4v[0] == '0') && v3_smem(1, G, 2, kG4Slot) <= 220u * 1024u) {
-    k = v3_kernel_g4();
+  if (p.M <= 2 && !pair && S == 1 && !(g4v && g4v[0] == '0') && v3_smem(p.M, G, 2, kG4Slot) <= 220u * 1024u) {
+    k = v3_kernel_g4(p.M);
     nslot = 2;
-    smem = v3_smem(1, G, 2, kG4Slot);
+    smem = v3_smem(p.M, G, 2, kG4Slot);
   }
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const uint32_t need = S == 1 ? (ntile + kV3Warps - 1) / kV3Warps : ntile;

@@ -1,8 +1,9 @@
 """GPU parity of the wide-projection GEMV (the vocabulary-head kernel, whole 64-row tiles per warp from each CTA's
 contiguous share) on a shape whose tiles do not divide evenly over the CTAs and warps (2432 tiles: 16-17 per CTA on
 148 SMs) with an odd group count (65 groups: a half stage at each tile's end), store and softcap epilogues, against the
-CPU oracle (lops.js:30-106, lops_spec.js:44-157 restated). At M = 1 this is the one-group-per-lane form, whose last
-stage of each tile holds one group here; P0MM_V3_G4=0 runs the generic form on the same cases."""
+CPU oracle (lops.js:30-106, lops_spec.js:44-157 restated). At M = 1 and 2 this is the grouped form (one or two groups
+per MMA lane pair), whose last stage of each tile holds one group here; P0MM_V3_G4=0 runs the generic form on the same
+cases."""
 import numpy as np
 import pytest
 
@@ -22,7 +23,7 @@ def weights():
     return _W["b"]
 
 
-@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("M", [1, 2, 3, 8])
 def test_wide_store(g, M):
     b = weights()
     X = ref.randn(M * K, 601 + M)
@@ -47,7 +48,7 @@ def test_wide_softcap(g, M):
         check_mx(mx[m * NT * 2:(m + 1) * NT * 2], wmx[m * NT * 2:(m + 1) * NT * 2], wy[m * N:(m + 1) * N], NT)
 
 
-@pytest.mark.parametrize("M", [1, 4])
+@pytest.mark.parametrize("M", [1, 2, 4])
 def test_wide_repeat_bit_identical(g, M):
     # every tile is summed by one warp in a fixed order: the same call gives the same bits
     b = weights()
