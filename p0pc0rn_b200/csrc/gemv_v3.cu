@@ -539,15 +539,21 @@ uint32_t v3_slots(uint32_t M, uint32_t G) {
 }
 }  // namespace
 
-// the parts per tile: 1 when every warp of the grid gets whole tiles (or for geglu pairs); else enough parts for about
-// 27 units per CTA (whole-tile v3 runs the head at 27-28 tiles per CTA), at most 8 and at most a part per stage
-uint32_t v3_parts(uint32_t K, uint32_t ntile, int sms, bool pair) {
+// whole tiles per warp: when every warp of the grid gets one, or, for M <= 4, from 13 tiles per SM (measured on B200 at
+// 2048 tiles, the 2-rank column-split head, whole tiles against k-parts: 37.8 / 44.7 / 45.2 against 48.8 / 46.7 / 46.4 us
+// at M = 1 / 2 / 4, M = 8 even (56.4 against 55.8); at 1024 tiles the k-parts lead by 10 us from M = 2 on)
+bool v3_whole(uint32_t M, uint32_t ntile, int sms) {
+  return ntile >= (uint32_t)sms * kV3Warps || (M <= 4u && ntile >= (uint32_t)sms * 13u);
+}
+// the parts per tile: 1 for whole tiles (or for geglu pairs); else enough parts for about 27 units per CTA (whole-tile
+// v3 runs the head at 27-28 tiles per CTA), at most 8 and at most a part per stage
+uint32_t v3_parts(uint32_t K, uint32_t ntile, int sms, bool pair, uint32_t M) {
   const uint32_t spt = (K / 32 + 1) / 2;
   // tuning override, read on every call: P0MM_V3_PARTS=n (1..8) cuts every non-geglu v3 call's tiles into n parts
   const char *ov = getenv("P0MM_V3_PARTS");
   const long nov = ov ? strtol(ov, nullptr, 10) : 0;
   if (!pair && nov >= 1 && nov <= 8) return (uint32_t)nov < spt ? (uint32_t)nov : spt;
-  if (pair || ntile >= (uint32_t)sms * kV3Warps) return 1;
+  if (pair || v3_whole(M, ntile, sms)) return 1;
   uint32_t S = ((uint32_t)sms * 27u + ntile - 1) / ntile;
   if (S > 8) S = 8;
   if (S > spt) S = spt;
@@ -564,20 +570,20 @@ uint32_t v3_slots_with(uint32_t M, uint32_t G, size_t extra) {
   return 0;
 }
 
-// v3: one split and a ring of >= 2 slots; whole tiles per warp when there are enough tiles for every warp of every SM,
-// else (not geglu, at least one tile per SM) tiles cut into k-parts
+// v3: one split and a ring of >= 2 slots; whole tiles per warp (v3_whole), else (not geglu, at least one tile per
+// SM) tiles cut into k-parts
 bool v3_fits(uint32_t M, uint32_t K, uint32_t nsplit, uint32_t ntile, int sms) {
-  return nsplit == 1 && v3_slots(M, K / 32) >= 2 && ntile >= (uint32_t)sms * kV3Warps;
+  return nsplit == 1 && v3_slots(M, K / 32) >= 2 && v3_whole(M, ntile, sms);
 }
 bool v3_split_fits(uint32_t M, uint32_t K, uint32_t nsplit, uint32_t ntile, int sms, bool pair) {
-  if (nsplit != 1 || pair || ntile < (uint32_t)sms || ntile >= (uint32_t)sms * kV3Warps) return false;
-  const uint32_t S = v3_parts(K, ntile, sms, pair);
+  if (nsplit != 1 || pair || ntile < (uint32_t)sms || v3_whole(M, ntile, sms)) return false;
+  const uint32_t S = v3_parts(K, ntile, sms, pair, M);
   return S > 1 && v3_slots_with(M, K / 32, v3_pbuf(ntile, sms, S)) >= 2;
 }
 cudaError_t launch_v3(const GemvParams &p, int sms, cudaStream_t s) {
   const bool pair = p.epi == P0_EPI_GEGLU;
   const uint32_t G = p.K / 32, ntile = p.N / 64;
-  uint32_t S = v3_parts(p.K, ntile, sms, pair);
+  uint32_t S = v3_parts(p.K, ntile, sms, pair, p.M);
   if (S > 1 && v3_slots_with(p.M, G, v3_pbuf(ntile, sms, S)) < 2) S = 1;   // the parts' totals do not fit beside a ring
   V3Kernel k = v3_kernel_for(p.M, pair, S > 1);
   const size_t pb = v3_pbuf(ntile, sms, S);

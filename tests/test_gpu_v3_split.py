@@ -1,6 +1,6 @@
 """The whole-tile streaming GEMV (v3) on calls with fewer tiles than the grid has warps: the column-split vocabulary
-head of 2 / 4 / 8 ranks (2048 / 1024 / 512 tiles per rank at K = 2048) and odd group counts. Tiles are cut into k-parts
-summed in shared memory before the epilogue; the results must match the oracle (lops_spec.js:44-157 restated) within
+head of 2 / 4 / 8 ranks (2048 / 1024 / 512 tiles per rank at K = 2048) and odd group counts. Below 13 tiles per SM (and
+at M > 4 below one tile per warp) tiles are cut into k-parts summed in shared memory before the epilogue; the results must match the oracle (lops_spec.js:44-157 restated) within
 the parity tolerance, with the per-tile argmax rows equal or tied within 1e-5 (kshipped.js:41-43). P0MM_GEMV=v3 makes
 the dispatch take v3 wherever it fits, so the parts path runs whatever the default choice for the shape is.
 """
@@ -15,9 +15,13 @@ from .test_gpu_parity import assert_close, nan_buf, wview
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 32768, 2048), (8, 32768, 2048), (4, 65536, 2048), (2, 24576, 2016), (1, 131072, 2048)])
-def test_v3_parts_head(g, monkeypatch, M, N, K):
+@pytest.mark.parametrize("M,N,K,parts", [(1, 32768, 2048, None), (8, 32768, 2048, None), (4, 65536, 2048, None),
+                                         (2, 24576, 2016, None), (1, 131072, 2048, None), (1, 131072, 2048, "2")])
+def test_v3_parts_head(g, monkeypatch, M, N, K, parts):
+    # (1, 131072): whole tiles by default (13+ tiles per SM at M <= 4: one tile per warp, some warps idle), k-parts forced
     monkeypatch.setenv("P0MM_GEMV", "v3")
+    if parts:
+        monkeypatch.setenv("P0MM_V3_PARTS", parts)
     b, _ = ref.pack_q4(ref.randn(N * K, 820 + M, 0.02), N, K)
     X = ref.round_f16(ref.randn(M * K, 821))
     nw = ref.randn(K, 822, 0.1) + 1
