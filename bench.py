@@ -130,28 +130,41 @@ def init_dist(ws, local):
 
 
 # ------------------------------------------------------------------------------------------ our arm
-def call_cost_us(M, N):
+def call_cost_us(M, N, head=False):
     """rough device time of one GEMV call (a fixed ~3 us per call plus its bytes at 4 TB/s), for placing calls on ranks"""
-    return 3.0 + gemv_bytes(M, N, K, N == HEAD_N) / 4e6
+    return 3.0 + gemv_bytes(M, N, K, head) / 4e6
+
+
+def step_bytes():
+    """the whole job's algorithmic bytes of one step: the 12 calls, whatever the split"""
+    return sum(gemv_bytes(M, N, K, N == HEAD_N) for N in NS for M in MS)
+
+
+def head_parts(ws):
+    """the parts (runs of whole 64-row tiles) each vocabulary-head call is cut into: one per rank on up to two ranks;
+    from four ranks on, ws / 4, so that the four head calls' parts spread one per rank and no rank pays a head call's
+    fixed cost (x staging, ring fill and drain, the last tiles' epilogues: ~15 us) more than once per step"""
+    return ws if ws <= 2 else max(1, ws // 4)
 
 
 def plan_calls(ws):
-    """The 12 calls of a step and where they run. The vocabulary head (N = 262144) is column-split: every rank runs
-    its N/ws rows (whole 64-row tiles) at every M. The small calls (N = 2048, 16384) are independent units and each
-    runs whole on one rank: largest first, onto the rank with the least estimated time so far (ties: lowest rank).
-    Every rank computes the same plan."""
-    calls = [{"M": M, "Nfull": N, "head": N == HEAD_N, "j": j} for N in NS for j, M in enumerate(MS)]
+    """The units of a step and where they run. Each vocabulary-head call (N = 262144) is cut into head_parts(ws) row
+    ranges (whole 64-row tiles); each small call (N = 2048, 16384) is one unit. Every unit runs whole on one rank:
+    largest first, onto the rank with the least estimated time so far (ties: lowest rank); every rank computes the same
+    plan. On two ranks each rank runs half of every head call; on four, one whole head call; on eight, one half."""
+    P = head_parts(ws)
+    units = []
+    for N in NS:
+        for j, M in enumerate(MS):
+            parts = P if N == HEAD_N else 1
+            for p in range(parts):
+                units.append({"M": M, "Nfull": N, "head": N == HEAD_N, "j": j, "part": p, "rows": N // parts})
     load = [0.0] * ws
-    for c in calls:
-        if c["head"]:
-            c["rank"] = None
-            for r in range(ws):
-                load[r] += call_cost_us(c["M"], c["Nfull"] // ws)
-    for c in sorted((c for c in calls if not c["head"]), key=lambda c: -call_cost_us(c["M"], c["Nfull"])):
+    for u in sorted(units, key=lambda u: -call_cost_us(u["M"], u["rows"], u["head"])):
         r = min(range(ws), key=lambda r: (load[r], r))
-        c["rank"] = r
-        load[r] += call_cost_us(c["M"], c["Nfull"])
-    return calls
+        u["rank"] = r
+        load[r] += call_cost_us(u["M"], u["rows"], u["head"])
+    return units
 
 
 def ring_copies(wbytes):
@@ -173,28 +186,29 @@ class Sweep:
         dev = torch.device("cuda", torch.cuda.current_device())
         gen = torch.Generator(device=dev)
         plan = plan_calls(ws)
-        self.total_bytes = sum(gemv_bytes(c["M"], c["Nfull"], K, c["head"]) for c in plan)   # the whole job's step
+        self.total_bytes = step_bytes()   # the whole job's step
+        self.parts = head_parts(ws)
         # the graph count every rank uses: the longest ring of any rank (the same number of replays everywhere)
-        self.R = max(ring_copies((c["Nfull"] // ws if c["head"] else c["Nfull"]) * K * 5 // 8) for c in plan)
+        self.R = max(ring_copies(c["rows"] * K * 5 // 8) for c in plan)
         self.calls, rings = [], {}
         out_floats = 0
         # every call's gathered output (Y, or the head's MX pairs and its rstd slot) is a slice of one per-rank buffer,
         # the all-gather's source: the step needs no copies before the collective. All ranks size it alike.
-        per_rank = max(sum((c["M"] * (c["Nfull"] // ws // 64) * 2 + 8) if c["head"] else c["M"] * c["Nfull"]
-                           for c in plan if c["head"] or c["rank"] == r) for r in range(ws))
+        per_rank = max(sum((c["M"] * (c["rows"] // 64) * 2 + 8) if c["head"] else c["M"] * c["rows"]
+                           for c in plan if c["rank"] == r) for r in range(ws))
         self.gather_src = torch.zeros(per_rank, dtype=torch.float32, device=dev)
         self.per_rank = per_rank
         slice_of = lambda off, n, label: g.wrap(self.gather_src.data_ptr() + off * 4, n * 4, label)
         for pc in plan:
-            if not (pc["head"] or pc["rank"] == rank):
+            if pc["rank"] != rank:
                 continue
             N, M, head = pc["Nfull"], pc["M"], pc["head"]
-            Nr = N // ws if head else N                      # rows this rank runs (whole 64-row tiles)
+            Nr = pc["rows"]                                  # rows this unit runs (whole 64-row tiles)
             if N not in rings:
                 wbytes = Nr * K * 5 // 8
                 ring = []
                 for c in range(ring_copies(wbytes)):
-                    gen.manual_seed(seed * 1000003 + N * 31 + c * 7 + (rank if head else 0))
+                    gen.manual_seed(seed * 1000003 + N * 31 + c * 7 + rank)
                     wf = torch.randn(Nr, K, generator=gen, device=dev, dtype=torch.float32) * 0.02
                     wb = g.wrap(wf.data_ptr(), wf.numel() * 4, "wf32")
                     q = p0.pack_q4(g, wb, Nr, K)
@@ -442,12 +456,13 @@ def run_ours(args, ws, rank, local):
             "data": "synthetic (seeded N(0,0.02) weights packed to q4g32a.t64 on device; N(0,1) fp16 x)",
             "config": sweep_config(ws),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                         "traffic": HEAD_TRAFFIC * (1.0 / ws) if ws in (1, 2, 4, 8) else None,
+                         "traffic": HEAD_TRAFFIC * heads[0]["N"] / HEAD_N,
                          "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one head launch at M=1 (N=262144) from an ncu "
-                                         "capture (335.63 + 4.38 MB; algorithmic 336.6 MB), scaled by this rank's rows at N>1",
-                         "kernel": "gemv head (rms+softcap) N=%d/rank K=%d, M=1/2/4/8" % (HEAD_N // ws, K),
+                                         "capture (335.63 + 4.38 MB; algorithmic 336.6 MB), scaled by the rows of this rank's head calls at N>1",
+                         "kernel": "gemv head (rms+softcap) N=%d rows per call K=%d, M=%s on this rank" % (
+                             heads[0]["N"], K, "/".join(str(c["M"]) for c in heads)),
                          "launch_us": round(head_launch_us, 2), "launches_timed": len(used) * len(heads),
-                         "timing": "event record nodes around this rank's 4 head calls inside every timed step graph; achieved = "
+                         "timing": "event record nodes around this rank's head calls inside every timed step graph; achieved = "
                                    "the head calls' algorithmic bytes / the group's device time", "peak_source": src},
             "e2e": e2e, "gpu_launches": len(sw.calls) * args.steps, "clocks": clocks, "rank_ms": [round(v, 4) for v in rank_ms],
             "config1": config1, "gemm": gemm, "calls_us": calls_us, "decode": decode, "decode_step": decode_step,
@@ -461,10 +476,11 @@ def run_ours(args, ws, rank, local):
 
 def sweep_config(ws):
     return {"workload": "config2_gemv_sweep", "M": list(MS), "N": list(NS), "K": K,
-            "parallelism": ("head column-split x%d, each small call whole on one rank, one all-gather per step" % ws) if ws > 1 else "one GPU",
+            "parallelism": ("each head call cut into %d row range(s); head ranges and small calls each run whole on one rank "
+                            "(largest first onto the least-loaded rank), one all-gather per step" % head_parts(ws)) if ws > 1 else "one GPU",
             "l2": "every call reads weights from HBM: each matrix has copies totalling >= 2x L2 (or one copy > 2x L2) and the "
                   "four M calls of a matrix read four different copies in a step",
-            "bytes_per_step": sum(gemv_bytes(c["M"], c["Nfull"], K, c["head"]) for c in plan_calls(ws)),
+            "bytes_per_step": step_bytes(),
             "launch": "one CUDA graph per step and weight-ring position (every rank's calls; the head group between two event "
                       "record nodes)" + (", then the NCCL all-gather graph" if ws > 1 else "")}
 
@@ -972,7 +988,7 @@ def cpu_baseline(args, budget_s=12.0):
     thr = host_cores()
     cs = CpuSweep(thr)
     cs.step()
-    total = sum(gemv_bytes(c["M"], c["Nfull"], K, c["head"]) for c in plan_calls(1))
+    total = step_bytes()
     t, n, t_start = 0.0, 0, time.perf_counter()
     while time.perf_counter() - t_start < budget_s or n < 3:
         t += cs.step()
@@ -991,7 +1007,7 @@ def run_reference(args, ws, rank):
     for _ in range(args.warmup):
         cs.step()
     t = sum(cs.step() for _ in range(args.steps))
-    total = sum(gemv_bytes(c["M"], c["Nfull"], K, c["head"]) for c in plan_calls(1))
+    total = step_bytes()
     value = round(total * args.steps / t / 1e9, 3)
     cb = {"value": value, "unit": "GB/s", "cores": thr, "kind": "port", "sample": cs.sample(args.steps)}
     return {"impl": "reference", "metric": "W4 GEMV GB/s (config 2 sweep: M 1/2/4/8 x N 2048/16384/262144, K 2048)", "value": value,
