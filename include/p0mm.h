@@ -197,7 +197,12 @@ enum { P0_ACT_SILU = 0, P0_ACT_GELU = 1 };
  * the DiT's calls, pocketflux-engine.js:4095). Both compute on the tensor cores with every product accumulated in f32:
  * the 'f16' mode's results are the f32 ones, closer to the exact sum than the reference's fp16 partials (whose extra
  * rounding error is up to about 2^-11 of each 32-term partial's magnitude).
- * The f32 x prologues run as a pass that writes the fp16 X into the context's workspace (M*K*2 bytes), then the GEMM. */
+ * The f32 x prologues run as a pass that writes the fp16 X into the context's workspace (M*K*2 bytes), then the GEMM.
+ * A call whose grid fills at most half the SMs (few tokens and few weight rows), with at least 16 k-stages and a store
+ * epilogue (f16 / bias / f32 / resadd), splits K: the splits' f32 partial products go to the same workspace (S*M*N*4 bytes,
+ * S <= 8, after the prologue's X), and a second pass sums them in split order and applies the epilogue. A call that
+ * has to grow the workspace waits for the context's stream first (as the x prologues do), so the first such call of a
+ * size should not sit inside a stream capture. */
 typedef struct {
   p0_wview w;
   p0_buf x;  uint64_t x_off; uint32_t x_ld, x_k0;
