@@ -8,6 +8,9 @@ oracle:
   gemm    engine/ops/gemm.js:131-211       (the 'f16' x path: fp16 X tile, fp16 W tile f16(q*s + mn) / f16(q*s), f32 FMA
                                             accumulation or fp16 partial sums per 32-k tile, epilogues f16 / f32 / bias /
                                             resadd / swiglu)
+          engine/ops/gemm.js:55-63         (the f32 x prologues lnmod / rms)
+          engine/ops/gemm.js:212-250       (the head-reducing epilogues heads (QK-RMSNorm + RoPE, head-major) and
+                                            onormgate)
 
 Conventions, stated once for every WGSL expression: f32 arithmetic rounds after every operation (numpy float32), with
 no contraction of a*b + c unless the WGSL writes fma(); `dot(u, v)` is u.x*v.x + u.y*v.y + u.z*v.z + u.w*v.w added
@@ -319,4 +322,83 @@ def gemm(Wbytes, X16, M, N, K, *, enc="q4g32a.t64", rows=None, cols=None, ldx=No
         c = np.asarray(bv, F)[bv_off + np.arange(N)] if bv is not None else np.zeros(N, F)
         t = gte * (A + c)
         Yr[:, ny0:ny0 + N] = t if store else Yr[:, ny0:ny0 + N] + t
+    return Y
+
+
+def gemm_xpro(mode, X, M, K, *, ldx=None, kx0=0, stats=None, stat_off=0, pv=None, pv_off=0, pv_stride=0):
+    """gemm.js:55-63, xload() for the f32 x paths: one fp16 X value per element of the k range [kx0, kx0 + K) of each
+    row, with {mean, rstd} = ST[(statOff + row) * 2 ..] and the PV vectors indexed by the x column (kx0 + k):
+      lnmod  f16(((x - mean) * rstd) * (1 + PV[pvOff + col]) + PV[pvOff + pvStride + col])
+      rms    f16((x * rstd) * PV[pvOff + col])
+    Returns fp16 bits [M][K]."""
+    ldx = ldx or K
+    Xr = np.asarray(X, F).reshape(M, ldx)[:, kx0:kx0 + K]
+    st = np.asarray(stats, F).reshape(-1)
+    srow = (stat_off + np.arange(M)) * 2
+    mean, rstd = st[srow][:, None], st[srow + 1][:, None]
+    pvv = np.asarray(pv, F)
+    col = kx0 + np.arange(K)
+    if mode == "lnmod":
+        v = ((Xr - mean) * rstd) * (F(1.0) + pvv[pv_off + col]) + pvv[pv_off + pv_stride + col]
+    elif mode == "rms":
+        v = (Xr * rstd) * pvv[pv_off + col]
+    else:
+        raise ValueError(mode)
+    return v.astype(F).astype(np.float16).view(np.uint16).ravel()
+
+
+def gemm_red128(A, M, N, *, epi, ev, ev_off=0, heads=None, gt=None, Y=None, ldy=None, ny0=0):
+    """gemm.js:212-250, the epilogues that reduce over one 128-wide head, on the call's f32 accumulators A [M][N], in
+    the workgroup-memory form (no subgroup shuffles): thread tx of the head's 16 holds 8 columns (tx*8 .. +7, or for
+    rotate_half tx*4 .. +3 and 64 + tx*4 .. +3), its share of the sum of squares is dot(a0, a0) + dot(a1, a1), and the
+    row's sum adds the 16 shares in tx order from 0.0; inv = inverseSqrt(s / 128 + eps), taken correctly rounded.
+      onormgate  Y[(m*ldy + ny0) & ~3 + n] = f16(((a * inv) * EV[evOff + c]) / (1 + exp(-GT[(m*Ltot + ny0) & ~3 + n])))
+      heads      q heads (hd < Hq) / k heads (hd < Hq + Hkv): v = (a * inv) * EV[evOff + (k ? 128 : 0) + c], then RoPE
+                 with the (cos, sin) pairs of RP row rowOff + m: rotate_half pairs (d, d + 64) with pair d, interleaved
+                 pairs (2p, 2p + 1) with pair p; v heads: a. Y head-major: Y[((hd * Ltot) + rowOff + m) * 128 + c].
+    Returns Y (fp16 bits; slots the call does not write keep theirs)."""
+    A = np.asarray(A, F).reshape(M, N)
+    h = heads or {}
+    Ltot, Hq, Hkv, rowOff = int(h.get("Ltot") or 0), int(h.get("Hq") or 0), int(h.get("Hkv") or 0), int(h.get("rowOff") or 0)
+    eps = F(h.get("eps") or 1e-6)
+    half = epi == "heads" and h.get("ropeMode") == "half"
+    ldy = ldy or N
+    evv = np.asarray(ev, F)
+    Y = np.asarray(Y, np.uint16).copy()
+    c = np.arange(128)
+    for hd in range(N // 128):
+        a = A[:, hd * 128:(hd + 1) * 128]
+        s = np.zeros(M, F)
+        for tx in range(16):
+            i0, i1 = (tx * 4, 64 + tx * 4) if half else (tx * 8, tx * 8 + 4)
+            s = s + (dot4(a[:, i0:i0 + 4], a[:, i0:i0 + 4]) + dot4(a[:, i1:i1 + 4], a[:, i1:i1 + 4]))
+        inv = (1.0 / np.sqrt((s / F(128.0) + eps).astype(np.float64))).astype(F)[:, None]
+        if epi == "onormgate":
+            g16 = _h(gt)
+            for m in range(M):
+                gb, yb = (m * Ltot + ny0) & ~3, (m * ldy + ny0) & ~3
+                n = hd * 128 + c
+                g = g16[gb + n]
+                v = ((a[m] * inv[m]) * evv[ev_off + c]) / (F(1.0) + expf(-g))
+                Y[yb + n] = v.astype(F).astype(np.float16).view(np.uint16)
+            continue
+        sec = 0 if hd < Hq else 1 if hd < Hq + Hkv else 2
+        rows = rowOff + np.arange(M)
+        out = ((hd * Ltot + rows) * 128)[:, None] + c[None, :]
+        if sec == 2:
+            Y[out] = a.astype(np.float16).view(np.uint16)
+            continue
+        v = (a * inv) * evv[ev_off + (128 if sec else 0) + c][None, :]
+        rp = np.asarray(h["rope"], F).reshape(-1, 128)[rows]           # (cos, sin) pairs of each row
+        cs, sn = rp[:, 0::2], rp[:, 1::2]                               # [M, 64]
+        r = np.empty_like(v)
+        if half:
+            lo, hi = v[:, :64], v[:, 64:]
+            r[:, :64] = (lo * cs) - (hi * sn)
+            r[:, 64:] = (hi * cs) + (lo * sn)
+        else:
+            x0, x1 = v[:, 0::2], v[:, 1::2]
+            r[:, 0::2] = (x0 * cs) - (x1 * sn)
+            r[:, 1::2] = (x0 * sn) + (x1 * cs)
+        Y[out] = r.astype(F).astype(np.float16).view(np.uint16)
     return Y

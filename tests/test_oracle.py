@@ -592,3 +592,46 @@ def test_gemm_second_transcription(enc, acc, epi):
     want = ref.gemm(b, X, M, N, K, enc=enc, epi=e, acc=acc, **{k: (v.copy() if isinstance(v, np.ndarray) and k == "Y" else v) for k, v in kw.items()})
     got = jk.gemm(b, X, M, N, K, enc=enc, epi=e, acc=acc, **kw)
     _bits_equal(got, want)
+
+
+@pytest.mark.parametrize("mode", ["lnmod", "rms"])
+def test_gemm_x_prologue_second_transcription(mode):
+    M, K, ldx, kx0, stat_off, pv_off, pv_stride = 5, 96, 120, 16, 3, 8, 136
+    X = ref.randn(M * ldx, 940, 2.0)
+    X[7] = 70000.0                     # beyond fp16's range after the prologue: both round to inf alike
+    st = ref.randn(2 * (stat_off + M), 941, 0.5)
+    st[1::2] = np.abs(st[1::2]) + 0.25
+    pv = ref.randn(pv_off + pv_stride + kx0 + K, 942, 0.3)
+    want = ref.gemm_xpro(mode, X, M, K, ldx=ldx, kx0=kx0, stats=st, stat_off=stat_off, pv=pv, pv_off=pv_off, pv_stride=pv_stride)
+    got = jk.gemm_xpro(mode, X, M, K, ldx=ldx, kx0=kx0, stats=st, stat_off=stat_off, pv=pv, pv_off=pv_off, pv_stride=pv_stride)
+    _bits_equal(got, want)
+
+
+@pytest.mark.parametrize("form", ["heads_half", "heads_inter", "onormgate"])
+def test_gemm_red128_second_transcription(form):
+    # q, k and v heads (Hq 2, Hkv 1: heads 0-1 q, 2 k, 3 v), rows written at rowOff into a head buffer of Ltot rows; the
+    # onormgate form into a column range of a wider Y with its gate rows of ld Ltot
+    M, K = 6, 128
+    N = 4 * 128 if form != "onormgate" else 128
+    b = ref.pack_q4(ref.randn(N * K, 950, 0.02), N, K)[0]
+    X = ref.f2h(ref.round_f16(ref.randn(M * K, 951)))
+    A = jk.gemm(b, X, M, N, K, epi="f32")
+    ev = ref.randn(256 + 8, 952, 0.2) + 1
+    if form == "onormgate":
+        Ltot, ldy, ny0 = 3 * 128, 2 * 128, 128
+        gt = ref.f2h(ref.round_f16(ref.randn(M * Ltot, 953)))
+        heads = {"Ltot": Ltot, "eps": 1e-5 / 64.0}
+        Y0 = ref.f2h(ref.randn(M * ldy, 954, 0.5))
+        want = ref.gemm(b, X, M, N, K, epi="onormgate", ev=ev, ev_off=8, heads=heads, gt=gt, Y=Y0.copy(), ldy=ldy, ny0=ny0)
+        got = jk.gemm_red128(A, M, N, epi="onormgate", ev=ev, ev_off=8, heads=heads, gt=gt, Y=Y0, ldy=ldy, ny0=ny0)
+    else:
+        Ltot, rowOff = M + 5, 3
+        ang = ref.randn(Ltot * 64, 955, 3.0).astype(np.float64)
+        rope = np.empty(Ltot * 128, np.float32)
+        rope[0::2], rope[1::2] = np.cos(ang), np.sin(ang)
+        heads = {"Ltot": Ltot, "Hq": 2, "Hkv": 1, "rowOff": rowOff, "eps": 1e-6, "ropeMode": "half" if form == "heads_half" else "inter",
+                 "rope": rope}
+        Y0 = ref.f2h(ref.randn(4 * Ltot * 128, 956, 0.5))
+        want = ref.gemm(b, X, M, N, K, epi="heads", ev=ev, ev_off=8, heads=heads, Y=Y0.copy())
+        got = jk.gemm_red128(A, M, N, epi="heads", ev=ev, ev_off=8, heads=heads, Y=Y0)
+    _bits_equal(got, want)
