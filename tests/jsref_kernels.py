@@ -11,6 +11,8 @@ oracle:
           engine/ops/gemm.js:55-63         (the f32 x prologues lnmod / rms)
           engine/ops/gemm.js:212-250       (the head-reducing epilogues heads (QK-RMSNorm + RoPE, head-major) and
                                             onormgate)
+  decode  engine/llm/lops.js:143-302       (normadd, qkrope, attnDec and its combine: 256-thread strided sums and
+                                            the workgroup tree, as the WGSL reduces)
 
 Conventions, stated once for every WGSL expression: f32 arithmetic rounds after every operation (numpy float32), with
 no contraction of a*b + c unless the WGSL writes fma(); `dot(u, v)` is u.x*v.x + u.y*v.y + u.z*v.z + u.w*v.w added
@@ -402,3 +404,141 @@ def gemm_red128(A, M, N, *, epi, ev, ev_off=0, heads=None, gt=None, Y=None, ldy=
             r[:, 1::2] = (x0 * sn) + (x1 * cs)
         Y[out] = r.astype(F).astype(np.float16).view(np.uint16)
     return Y
+
+
+# ---------------------------------------------------------------- decode-path operators (engine/llm/lops.js)
+def _inverse_sqrt(v):
+    """WGSL inverseSqrt, taken correctly rounded"""
+    return F(1.0 / np.sqrt(np.float64(v)))
+
+
+def _strided_sumsq(v, D):
+    """the 256 threads' shares of sum(v * v) over i = t, t + 256, ... (in that order, from 0.0), then the workgroup's
+    tree: red[t] += red[t + k] for k = 128, 64, .., 1"""
+    red = np.zeros(256, F)
+    for i0 in range(0, D, 256):
+        n = min(256, D - i0)
+        red[:n] = red[:n] + v[i0:i0 + n] * v[i0:i0 + n]
+    k = 128
+    while k > 0:
+        red[:k] = red[:k] + red[k:2 * k]
+        k >>= 1
+    return red[0]
+
+
+def _split_sum(S, nsrc, ldp, idx):
+    """src(i) = sum of the split partials S[j * ldp + i] for j = 0 .. nsrc - 1, from 0.0"""
+    v = np.zeros(len(idx), F)
+    for j in range(nsrc):
+        v = v + S[j * ldp + idx]
+    return v
+
+
+def normadd(T, nsrc, ldp, W, w_off, X, ST, st_off, D, M, *, mode=0, eps=1e-6, scale=1.0):
+    """lops.js:143-178 (NORMADD): per row m, tv = the split partials summed; rs = inverseSqrt(sumsq(tv) / D + eps);
+    mode 0: x = (x + (tv * rs) * W[wOff + i]) * scale, mode 1: x = tv; ST[statOff + m] = inverseSqrt(sumsq(x) / D + eps).
+    Returns (X, ST) as new arrays."""
+    T, X, ST = np.asarray(T, F), np.asarray(X, F).copy(), np.asarray(ST, F).copy()
+    Wv = np.asarray(W, F) if W is not None else None
+    eps, scale = F(eps), F(scale)
+    i = np.arange(D)
+    for m in range(M):
+        xb = m * D
+        tv = _split_sum(T, nsrc, ldp, xb + i)
+        rs = _inverse_sqrt(_strided_sumsq(tv, D) / F(D) + eps)
+        x = X[xb:xb + D]
+        x = (x + (tv * rs) * Wv[w_off + i]) * scale if mode == 0 else tv
+        X[xb:xb + D] = x
+        ST[st_off + m] = _inverse_sqrt(_strided_sumsq(x, D) / F(D) + eps)
+    return X, ST
+
+
+def qkrope(S, nsrc, ldp, NW, RP, D, nq, *, nkv=1, hasKV=True, pos=0, eps=1e-6, qw=0, kw=0, npairs=None, rope_off=0, kv_row=0,
+           kv_len=0, Q=None, KC=None, VC=None):
+    """lops.js:181-224 (QKROPE): workgroup h (q heads 0 .. nq - 1, then nkv k heads, then nkv v heads) sums its head's
+    split partials hv, rs = inverseSqrt(sumsq(hv) / D + eps); v heads: f16(hv * rs) into VC's row kvRow of the head;
+    q / k heads: a = (hv[d] * rs) * NW[w + d], b = (hv[d + D/2] * rs) * NW[w + d + D/2], (cos, sin) from
+    RP[ropeOff + (pos * npairs + d) * 2] for d < npairs (else (1, 0)), lo = a*c - b*sn, hi = b*c + a*sn; q heads -> Q,
+    k heads -> f16 into KC's row kvRow. Returns (Q, KC, VC) as new arrays (fp16 bits for the caches)."""
+    npairs = D // 2 if npairs is None else npairs
+    S, NW, RP = np.asarray(S, F), np.asarray(NW, F), np.asarray(RP, F)
+    Q = np.zeros(nq * D, F) if Q is None else np.asarray(Q, F).copy()
+    KC = np.zeros(max(1, nkv * kv_len * D), np.uint16) if KC is None else np.asarray(KC, np.uint16).copy()
+    VC = np.zeros(max(1, nkv * kv_len * D), np.uint16) if VC is None else np.asarray(VC, np.uint16).copy()
+    eps, half = F(eps), D // 2
+    d = np.arange(half)
+    for h in range(nq + (2 * nkv if hasKV else 0)):
+        base = h * D
+        hv = _split_sum(S, nsrc, ldp, base + np.arange(D))
+        rs = _inverse_sqrt(_strided_sumsq(hv, D) / F(D) + eps)
+        isv = h >= nq + nkv
+        kvh = h - nq - nkv if isv else h - nq
+        cb = (kvh * kv_len + kv_row) * D
+        if isv:
+            VC[cb:cb + D] = (hv * rs).astype(np.float16).view(np.uint16)
+            continue
+        wo = qw if h < nq else kw
+        a = (hv[:half] * rs) * NW[wo + d]
+        b = (hv[half:] * rs) * NW[wo + half + d]
+        c, sn = np.ones(half, F), np.zeros(half, F)
+        rb = rope_off + (pos * npairs + d[:npairs]) * 2
+        c[:npairs], sn[:npairs] = RP[rb], RP[rb + 1]
+        lo, hi = (a * c) - (b * sn), (b * c) + (a * sn)
+        if h < nq:
+            Q[base:base + half], Q[base + half:base + D] = lo, hi
+        else:
+            KC[cb:cb + half], KC[cb + half:cb + D] = lo.astype(np.float16).view(np.uint16), hi.astype(np.float16).view(np.uint16)
+    return Q, KC, VC
+
+
+def attn_dec(Q, KC, VC, D, nh, nkv, kv_len, k_start, k_end, ring=0):
+    """lops.js:236-302 (ATTDEC, one workgroup per 64-key chunk) and ATTCOMB: per chunk c and head h, the scores
+    s = sum over d of dot(f32(K[4d .. 4d+3]), Q[h][4d ..]) (from 0.0; K of the head's KV group h / (nh / nkv), row
+    j or j % ring), m = max over the chunk's keys (from -3e38), p = exp(s - m), l = sum p (from 0.0), acc[h][d] = sum
+    over keys of p * f32(V) (from 0.0); the combine: M = max_c m_c, w_c = exp(m_c - M), L = sum_c w_c * l_c, w_c /= L,
+    O[h][d] = sum_c w_c * acc_c[h][d] (from 0.0). exp is the C library's expf. Returns O f32 [nh][D]."""
+    Qv = np.asarray(Q, F).reshape(nh, D)
+    K = _h(KC).reshape(nkv, kv_len, D)
+    V = _h(VC).reshape(nkv, kv_len, D)
+    hpg = nh // nkv
+    nchunk = -(-(k_end - k_start) // 64)
+    ms, ls, accs = [], [], []
+    for ch in range(nchunk):
+        j0 = k_start + ch * 64
+        nk = min(64, k_end - j0)
+        rows = np.array([(j0 + j) % ring if ring > 0 else j0 + j for j in range(nk)])
+        sc = np.zeros((nh, nk), F)
+        for hh in range(nh):
+            kr = K[hh // hpg, rows]                                     # [nk, D]
+            s = np.zeros(nk, F)
+            for d4 in range(D // 4):
+                s = s + dot4(kr[:, 4 * d4:4 * d4 + 4], np.broadcast_to(Qv[hh, 4 * d4:4 * d4 + 4], (nk, 4)))
+            sc[hh] = s
+        m = np.full(nh, F(-3.0e38), F)
+        for k in range(nk):
+            m = np.maximum(m, sc[:, k])
+        p = expf(sc - m[:, None])
+        l = np.zeros(nh, F)
+        for k in range(nk):
+            l = l + p[:, k]
+        acc = np.zeros((nh, D), F)
+        for k in range(nk):
+            for hh in range(nh):
+                acc[hh] = acc[hh] + p[hh, k] * V[hh // hpg, rows[k]]
+        ms.append(m), ls.append(l), accs.append(acc)
+    O = np.zeros((nh, D), F)
+    for h in range(nh):
+        Mx = F(-3.0e38)
+        for ch in range(nchunk):
+            Mx = max(Mx, ms[ch][h])
+        wts, L = [], F(0.0)
+        for ch in range(nchunk):
+            e = expf(np.array([ms[ch][h] - Mx], F))[0]
+            wts.append(e)
+            L = F(L + F(e * ls[ch][h]))
+        wts = [F(w / L) for w in wts]
+        o = np.zeros(D, F)
+        for ch in range(nchunk):
+            o = o + wts[ch] * accs[ch][h]
+        O[h] = o
+    return O.ravel()

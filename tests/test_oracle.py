@@ -635,3 +635,43 @@ def test_gemm_red128_second_transcription(form):
         want = ref.gemm(b, X, M, N, K, epi="heads", ev=ev, ev_off=8, heads=heads, Y=Y0.copy())
         got = jk.gemm_red128(A, M, N, epi="heads", ev=ev, ev_off=8, heads=heads, Y=Y0)
     _bits_equal(got, want)
+
+
+@pytest.mark.parametrize("mode,nsrc,D", [(0, 1, 1000), (0, 3, 1152), (1, 2, 640), (0, 2, 200)])
+def test_normadd_second_transcription(mode, nsrc, D):
+    M = 3
+    T = ref.randn(nsrc * M * D, 960, 1.0)
+    W = ref.randn(D + 5, 961, 0.2) + 1
+    X0, ST0 = ref.randn(M * D, 962), np.zeros(M + 2, np.float32)
+    X, ST = ref.normadd(T, nsrc, M * D, W, 5, X0.copy(), ST0.copy(), 2, D, M, mode=mode, eps=1e-6, scale=0.7)
+    jX, jST = jk.normadd(T, nsrc, M * D, W, 5, X0, ST0, 2, D, M, mode=mode, eps=1e-6, scale=0.7)
+    _bits_equal(jX, X)
+    _bits_equal(jST, ST)
+
+
+@pytest.mark.parametrize("D,nq,nkv,npairs,hasKV", [(256, 4, 2, 32, True), (128, 8, 1, 64, True), (512, 2, 1, 100, False)])
+def test_qkrope_second_transcription(D, nq, nkv, npairs, hasKV):
+    kv_len, row, pos = 10, 7, 3
+    nh = nq + 2 * nkv
+    S = ref.randn(2 * nh * D, 963, 1.0)
+    NW = ref.randn(2 * D + 4, 964, 0.2) + 1
+    ang = ref.randn(8 * npairs, 965, 2.0).astype(np.float64)
+    RP = np.empty(5 + 16 * npairs, np.float32)
+    RP[5:5 + 16 * npairs:2], RP[6:5 + 16 * npairs:2] = np.cos(ang), np.sin(ang)
+    kw = dict(nkv=nkv, hasKV=hasKV, pos=pos, qw=4, kw=4 + D, npairs=npairs, rope_off=5, kv_row=row, kv_len=kv_len)
+    KC0 = ref.f2h(ref.randn(nkv * kv_len * D, 966, 0.5))
+    VC0 = ref.f2h(ref.randn(nkv * kv_len * D, 967, 0.5))
+    Q, KC, VC = ref.qkrope(S, 2, nh * D, NW, RP, D, nq, KC=KC0.copy(), VC=VC0.copy(), **kw)
+    jQ, jKC, jVC = jk.qkrope(S, 2, nh * D, NW, RP, D, nq, KC=KC0, VC=VC0, **kw)
+    _bits_equal(jQ, Q)
+    _bits_equal(jKC, KC)
+    _bits_equal(jVC, VC)
+
+
+@pytest.mark.parametrize("D,nh,nkv,k0,k1,ring", [(128, 8, 2, 5, 150, 0), (256, 4, 1, 0, 64, 0), (128, 4, 4, 30, 200, 100)])
+def test_attn_dec_second_transcription(D, nh, nkv, k0, k1, ring):
+    L = 210
+    Q = ref.randn(nh * D, 968, 0.08)
+    KC, VC = ref.f2h(ref.round_f16(ref.randn(nkv * L * D, 969))), ref.f2h(ref.round_f16(ref.randn(nkv * L * D, 970)))
+    O = ref.attn_dec(Q, KC, VC, D, nh, nkv, L, k0, k1, ring)
+    _bits_equal(jk.attn_dec(Q, KC, VC, D, nh, nkv, L, k0, k1, ring), O)
