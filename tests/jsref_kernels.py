@@ -11,8 +11,9 @@ oracle:
           engine/ops/gemm.js:55-63         (the f32 x prologues lnmod / rms)
           engine/ops/gemm.js:212-250       (the head-reducing epilogues heads (QK-RMSNorm + RoPE, head-major) and
                                             onormgate)
-  decode  engine/llm/lops.js:143-302       (normadd, qkrope, attnDec and its combine: 256-thread strided sums and
-                                            the workgroup tree, as the WGSL reduces)
+  decode  engine/llm/lops.js:143-347       (normadd, qkrope, attnDec and its combine, embed: 256-thread strided
+                                            sums and the workgroup tree, as the WGSL reduces)
+          engine/llm/lops_spec.js:428-473  (dhead: the drafter's head over selected tiles, max and lowest argmax)
 
 Conventions, stated once for every WGSL expression: f32 arithmetic rounds after every operation (numpy float32), with
 no contraction of a*b + c unless the WGSL writes fma(); `dot(u, v)` is u.x*v.x + u.y*v.y + u.z*v.z + u.w*v.w added
@@ -542,3 +543,85 @@ def attn_dec(Q, KC, VC, D, nh, nkv, kv_len, k_start, k_end, ring=0):
             o = o + wts[ch] * accs[ch][h]
         O[h] = o
     return O.ravel()
+
+
+def embed(Wbytes, ids, K, *, enc="q4g32a.t64", scale=1.0, eps=1e-6, st_off=0, row_out=0, X=None, ST=None):
+    """lops.js:324-347 (EMBED): row id of the table (tile id >> 6, row id & 63), v = ((q * s) + mn) * scale (q4) or
+    (q * s) * scale (q8, q the sign-extended byte, s the row's fp16 scale); ST[statOff + m] = inverseSqrt(sumsq(v) /
+    K + eps) with the 256-thread strided sums and the workgroup tree. Returns (X, ST) as new arrays."""
+    W = words(Wbytes)
+    ids = np.asarray(ids, np.uint32)
+    n = ids.size
+    X = np.zeros((row_out + n) * K, F) if X is None else np.asarray(X, F).copy()
+    ST = np.zeros(st_off + n, F) if ST is None else np.asarray(ST, F).copy()
+    q8 = enc == "q8g64s.t64"
+    wG = K // (64 if q8 else 32)
+    k = np.arange(K)
+    scale, eps = F(scale), F(eps)
+    for m in range(n):
+        tile, r = int(ids[m]) >> 6, int(ids[m]) & 63
+        if q8:
+            rec = (tile * wG + (k >> 6)) * 1056
+            kk = k & 63
+            qb = ((W[rec + r * 16 + (kk >> 2)] >> (8 * (kk & 3))) & 255).astype(np.uint32)
+            qs = ((qb << 24).astype(np.uint32).view(np.int32) >> 24).astype(F)
+            s2x, s2y = unpack2x16float(W[rec + 1024 + (r >> 1)])
+            v = (qs * (s2y if r & 1 else s2x)) * scale
+        else:
+            rec = (tile * wG + (k >> 5)) * 320
+            kk = k & 31
+            q = ((W[rec + r * 4 + (kk >> 3)] >> (4 * (kk & 7))) & 15).astype(F)
+            s, mn = unpack2x16float(W[rec + 256 + r])
+            v = ((q * s) + mn) * scale
+        X[(row_out + m) * K:(row_out + m + 1) * K] = v
+        ST[st_off + m] = _inverse_sqrt(_strided_sumsq(v.astype(F), K) / F(K) + eps)
+    return X, ST
+
+
+def dhead(Wbytes, X, ST, NW, SEL, K, tPer, nsel, *, enc="q4g32a.t64", stat_off=0, norm_off=0):
+    """lops_spec.js:428-473 (DHEAD): for selected tile wt (SEL[wt / tPer] * tPer + wt % tPer), xs = (X * rs) * NW[nOff + k];
+    row r's four k-quarter lanes w accumulate over the groups in order, q4: acc + s * (dot(qa, a) + dot(qb, b)) + mn *
+    (sum(a) + sum(b)) with a, b the lane's 8 x and qa, qb its 8 codes; q8: acc + s * d, d = sum over the lane's four
+    code words of dot(codes, x); the row's total ((w0 + w1) + w2) + w3; the tile's max with the lowest row on ties.
+    Returns MX f32 [nsel * tPer][max, bitcast row]."""
+    W = words(Wbytes)
+    q8 = enc == "q8g64s.t64"
+    wG = K // (64 if q8 else 32)
+    xs = (np.asarray(X, F)[:K] * F(np.asarray(ST, F)[stat_off])) * np.asarray(NW, F)[norm_off + np.arange(K)]
+    SEL = np.asarray(SEL, np.uint32)
+    MX = np.empty(2 * nsel * tPer, F)
+    one = np.ones(4, F)
+    for wt in range(nsel * tPer):
+        tile = int(SEL[wt // tPer]) * tPer + wt % tPer
+        tot = np.zeros(64, F)
+        for r in range(64):
+            lanes = []
+            for w in range(4):
+                acc = F(0.0)
+                for g in range(wG):
+                    if q8:
+                        rec = (tile * wG + g) * 1056
+                        s2x, s2y = unpack2x16float(W[rec + 1024 + (r >> 1)])
+                        sc = s2y if r & 1 else s2x
+                        d = F(0.0)
+                        for u in range(4):
+                            q = np.uint32(W[rec + r * 16 + w * 4 + u])
+                            qv = np.array([(np.uint32(q << sh) & 0xFFFFFFFF) for sh in (24, 16, 8, 0)], np.uint32).view(np.int32) >> 24
+                            xb = g * 64 + w * 16 + u * 4
+                            d = F(d + dot4(qv.astype(F), xs[xb:xb + 4]))
+                        acc = F(acc + F(sc * d))
+                    else:
+                        rec = (tile * wG + g) * 320
+                        q = np.uint32(W[rec + r * 4 + w])
+                        s, mn = unpack2x16float(W[rec + 256 + r])
+                        xb = g * 32 + w * 8
+                        a, b = xs[xb:xb + 4], xs[xb + 4:xb + 8]
+                        qa = ((q >> np.array([0, 4, 8, 12], np.uint32)) & 15).astype(F)
+                        qb = ((q >> np.array([16, 20, 24, 28], np.uint32)) & 15).astype(F)
+                        acc = F(F(acc + F(s * F(dot4(qa, a) + dot4(qb, b)))) + F(mn * F(dot4(a, one) + dot4(b, one))))
+                lanes.append(acc)
+            tot[r] = F(F(F(lanes[0] + lanes[1]) + lanes[2]) + lanes[3])
+        r = int(np.argmax(tot))   # the first of equal maxima: the lowest row
+        MX[2 * wt] = tot[r]
+        MX[2 * wt + 1] = np.uint32(tile * 64 + r).view(F)
+    return MX

@@ -675,3 +675,25 @@ def test_attn_dec_second_transcription(D, nh, nkv, k0, k1, ring):
     KC, VC = ref.f2h(ref.round_f16(ref.randn(nkv * L * D, 969))), ref.f2h(ref.round_f16(ref.randn(nkv * L * D, 970)))
     O = ref.attn_dec(Q, KC, VC, D, nh, nkv, L, k0, k1, ring)
     _bits_equal(jk.attn_dec(Q, KC, VC, D, nh, nkv, L, k0, k1, ring), O)
+
+
+@pytest.mark.parametrize("enc,K", [("q4g32a.t64", 640), ("q8g64s.t64", 320)])
+def test_embed_second_transcription(enc, K):
+    V = 64 * 5
+    b = (ref.pack_q4 if enc == "q4g32a.t64" else ref.pack_q8)(ref.randn(V * K, 975, 0.05), V, K)[0]
+    ids = np.array([7, 300, 64, 0, 129], np.uint32)
+    X, ST = ref.embed(b, ids, K, enc=enc, scale=22.6, eps=1e-6, st_off=2, row_out=1)
+    jX, jST = jk.embed(b, ids, K, enc=enc, scale=22.6, eps=1e-6, st_off=2, row_out=1)
+    _bits_equal(jX, X)
+    _bits_equal(jST, ST)
+
+
+@pytest.mark.parametrize("enc,K", [("q4g32a.t64", 256), ("q8g64s.t64", 128)])
+def test_dhead_second_transcription(enc, K):
+    V = 64 * 8
+    b = (ref.pack_q4 if enc == "q4g32a.t64" else ref.pack_q8)(ref.randn(V * K, 976, 0.05), V, K)[0]
+    X, NW = ref.randn(K, 977), ref.randn(K + 3, 978, 0.1) + 1
+    ST = np.array([0.0, 0.8], np.float32)
+    SEL = np.array([3, 0, 2], np.uint32)
+    MX = ref.dhead(b, X, ST, NW, SEL, K, 2, 3, enc=enc, stat_off=1, norm_off=3)
+    _bits_equal(jk.dhead(b, X, ST, NW, SEL, K, 2, 3, enc=enc, stat_off=1, norm_off=3), MX)
