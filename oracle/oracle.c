@@ -343,6 +343,33 @@ static inline uint16_t hfma(uint16_t a, uint16_t b, uint16_t c) {
   return h;
 }
 
+/* hfma with a and b given as doubles (their fp16 values) and c through a table: the same value a*b + c and the same
+ * rounding, by arithmetic instead of frexp / floor / fmod. For |r| < 2^(u + 52), (r + 1.5 * 2^(u + 52)) - 1.5 * 2^(u + 52)
+ * is r rounded to a multiple of 2^u, ties to even (the sum's last bit is the parity of the multiple: 1.5 * 2^52 is
+ * even), where u is the fp16 ulp exponent of r, as in hfma. h2d_init() fills the table; or_gemm calls it. */
+static double h2d_tab[65536];
+static int h2d_ready;
+static void h2d_init(void) {
+  if (h2d_ready) return;
+  for (uint32_t i = 0; i < 65536u; i++) h2d_tab[i] = or_h2f((uint16_t)i);
+  h2d_ready = 1;
+}
+static inline uint16_t hfma_d(double a, double b, uint16_t c) {
+  double r = a * b + h2d_tab[c];
+  if (!(r == r)) return 0x7e00;
+  if (r == 0) return signbit(r) ? 0x8000 : 0;
+  if (isinf(r)) return r < 0 ? 0xfc00 : 0x7c00;
+  double ar = fabs(r);
+  uint64_t bits; memcpy(&bits, &ar, 8);
+  int ulpe = (int)((bits >> 52) & 0x7ffu) - 1033;        /* frexp's e - 11: ar = f * 2^e, f in [0.5, 1) */
+  if (ulpe < -24) ulpe = -24;
+  uint64_t sb = ((uint64_t)(ulpe + 52 + 1023) << 52) | 0x8000000000000ull;   /* 1.5 * 2^(ulpe + 52) */
+  double sm; memcpy(&sm, &sb, 8);
+  volatile double t = ar + sm;                             /* rounded once, to nearest even */
+  double v = t - sm;
+  return or_f2h(r < 0 ? -v : v);
+}
+
 /* the fp16 weight tile element (row, k) the WGSL dequantises into ws[] */
 static inline uint16_t wtile(int wenc, const uint32_t *W, uint32_t row, uint32_t kabs, uint32_t wG) {
   if (wenc == WQ4) {
@@ -369,39 +396,59 @@ void or_gemm(int wenc, int epi, int acc16, int act_gelu, int res, int store, int
              uint32_t ldy, uint32_t ny0, uint32_t Nw, uint32_t evOff, uint32_t bvOff, uint32_t bvUp, int nthreads) {
   uint16_t *Yh = (uint16_t *)Yv; float *Yf = (float *)Yv;
   uint32_t BN = 128, ntiles = (N + BN - 1) / BN;
+  const uint32_t ncol = ntiles * BN;
   (void)nthreads;
 #ifdef _OPENMP
   if (nthreads > 0) omp_set_num_threads(nthreads);
+#endif
+  /* The W tile of every column (gemm.js:96-160: the column's weight row, f16(q*s + mn) / f16(q*s)) and the X values,
+   * dequantised and converted once per call instead of once per multiply: the same values, so every output's
+   * arithmetic and summation order below are unchanged. */
+  uint16_t *Wh = (uint16_t *)malloc(sizeof(uint16_t) * (size_t)ncol * K);
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static) if (nthreads != 1)
+#endif
+  for (int64_t nn = 0; nn < (int64_t)ncol; nn++) {
+    const uint32_t n = (uint32_t)nn, cc = n % BN;
+    const uint32_t row = epi == GE_SWIGLU ? (((cc & 1u) == 0u ? wR0 : wR1) + (n >> 1)) : (wR0 + n < Nw - 1 ? wR0 + n : Nw - 1);
+    for (uint32_t k = 0; k < K; k++) Wh[(size_t)n * K + k] = wtile(wenc, W, row, wk0 + k, wG);
+  }
+  float *Wf = NULL, *Xf = NULL;
+  double *Wd = NULL, *Xd = NULL;
+  if (acc16) {
+    h2d_init();
+    Wd = (double *)malloc(sizeof(double) * (size_t)ncol * K);
+    Xd = (double *)malloc(sizeof(double) * (size_t)M * K);
+    for (size_t i = 0; i < (size_t)ncol * K; i++) Wd[i] = h2d_tab[Wh[i]];
+    for (uint32_t m = 0; m < M; m++)
+      for (uint32_t k = 0; k < K; k++) Xd[(size_t)m * K + k] = h2d_tab[X[(size_t)m * ldx + kx0 + k]];
+  } else {
+    Wf = (float *)malloc(sizeof(float) * (size_t)ncol * K);
+    Xf = (float *)malloc(sizeof(float) * (size_t)M * K);
+    for (size_t i = 0; i < (size_t)ncol * K; i++) Wf[i] = h2f32(Wh[i]);
+    for (uint32_t m = 0; m < M; m++)
+      for (uint32_t k = 0; k < K; k++) Xf[(size_t)m * K + k] = h2f32(X[(size_t)m * ldx + kx0 + k]);
+  }
+#ifdef _OPENMP
 #pragma omp parallel for schedule(dynamic, 1) if (nthreads != 1)
 #endif
   for (int64_t mm = 0; mm < (int64_t)M; mm++) {
     uint32_t m = (uint32_t)mm;
     float *a = (float *)malloc(sizeof(float) * ntiles * BN);
-    uint16_t *wrow_cache = NULL; (void)wrow_cache;
-    for (uint32_t nt = 0; nt < ntiles; nt++) {
-      uint32_t nB = nt * BN;
-      for (uint32_t cc = 0; cc < BN; cc++) {
-        uint32_t row = epi == GE_SWIGLU ? (((cc & 1u) == 0u ? wR0 : wR1) + ((nB + cc) >> 1)) : (wR0 + nB + cc < Nw - 1 ? wR0 + nB + cc : Nw - 1);
-        float acc = 0.0f;
-        for (uint32_t k0 = 0; k0 < K; k0 += 32) {
-          if (acc16) {
-            uint16_t h = 0;
-            for (uint32_t k = 0; k < 32; k++) {
-              uint16_t xh = X[(size_t)m * ldx + kx0 + k0 + k];
-              uint16_t wh = wtile(wenc, W, row, wk0 + k0 + k, wG);
-              h = hfma(xh, wh, h);
-            }
-            acc = acc + h2f32(h);
-          } else {
-            for (uint32_t k = 0; k < 32; k++) {
-              float xv = h2f32(X[(size_t)m * ldx + kx0 + k0 + k]);
-              float wv = h2f32(wtile(wenc, W, row, wk0 + k0 + k, wG));
-              acc = fmaf(xv, wv, acc);
-            }
-          }
+    for (uint32_t n = 0; n < ncol; n++) {
+      float acc = 0.0f;
+      for (uint32_t k0 = 0; k0 < K; k0 += 32) {
+        if (acc16) {
+          uint16_t h = 0;
+          const double *wv = Wd + (size_t)n * K + k0, *xv = Xd + (size_t)m * K + k0;
+          for (uint32_t k = 0; k < 32; k++) h = hfma_d(xv[k], wv[k], h);
+          acc = acc + h2f32(h);
+        } else {
+          const float *wv = Wf + (size_t)n * K + k0, *xv = Xf + (size_t)m * K + k0;
+          for (uint32_t k = 0; k < 32; k++) acc = fmaf(xv[k], wv[k], acc);
         }
-        a[nB + cc] = acc;
       }
+      a[n] = acc;
     }
     /* epilogues (gemm.js:190-211): columns in vec4 units, col < N checks per vec4 */
     if (epi == GE_SWIGLU) {
@@ -435,6 +482,11 @@ void or_gemm(int wenc, int epi, int acc16, int act_gelu, int res, int store, int
     }
     free(a);
   }
+  free(Wh);
+  free(Wf);
+  free(Xf);
+  free(Wd);
+  free(Xd);
 }
 
 /* ------------------------------------------------------------------ f64 references and the timed CPU baseline */
@@ -483,6 +535,11 @@ int or_max_threads(void) {
 void or_f2h_arr(const double *x, int64_t n, uint16_t *o) { for (int64_t i = 0; i < n; i++) o[i] = or_f2h(x[i]); }
 void or_h2f_arr(const uint16_t *h, int64_t n, double *o) { for (int64_t i = 0; i < n; i++) o[i] = or_h2f(h[i]); }
 void or_hfma_arr(const uint16_t *a, const uint16_t *b, const uint16_t *c, int64_t n, uint16_t *o) { for (int64_t i = 0; i < n; i++) o[i] = hfma(a[i], b[i], c[i]); }
+/* the table / add-and-subtract form the GEMM uses, for the check that it equals hfma */
+void or_hfma_d_arr(const uint16_t *a, const uint16_t *b, const uint16_t *c, int64_t n, uint16_t *o) {
+  h2d_init();
+  for (int64_t i = 0; i < n; i++) o[i] = hfma_d(h2d_tab[a[i]], h2d_tab[b[i]], c[i]);
+}
 
 /* ------------------------------------------------------------------ GEMM x prologues (ops/gemm.js:55-63)
  * The fp16 X the reference's xload() yields for the f32 x modes: row m, k = 0..K-1 of X f32 [row * ldx + kx0 + k],

@@ -51,6 +51,7 @@ def lib():
         L.or_f2h_arr.argtypes = [_f64p, _i64, _u16p]
         L.or_h2f_arr.argtypes = [_u16p, _i64, _f64p]
         L.or_hfma_arr.argtypes = [_u16p, _u16p, _u16p, _i64, _u16p]
+        L.or_hfma_d_arr.argtypes = [_u16p, _u16p, _u16p, _i64, _u16p]
         L.or_pack_q4.argtypes = [_f32p, _i64, _i64, _u8p, _vp]
         L.or_pack_q8.argtypes = [_f32p, _i64, _i64, _u8p, _vp]
         L.or_deq16_q4.argtypes = [_u8p, _i64, _i64, _u16p]

@@ -697,3 +697,22 @@ def test_dhead_second_transcription(enc, K):
     SEL = np.array([3, 0, 2], np.uint32)
     MX = ref.dhead(b, X, ST, NW, SEL, K, 2, 3, enc=enc, stat_off=1, norm_off=3)
     _bits_equal(jk.dhead(b, X, ST, NW, SEL, K, 2, 3, enc=enc, stat_off=1, norm_off=3), MX)
+
+
+def test_fast_fp16_fma_equals_definitional():
+    # the GEMM's fp16-partial accumulation uses a table / add-and-subtract form of the oracle's fp16 FMA (one rounding of
+    # the f64 value a*b + c to fp16, ties to even); it must give the definitional form's bits on every input
+    rng = np.random.default_rng(990)
+    n = 2_000_000
+    a, b, c = (rng.integers(0, 65536, n, dtype=np.uint32).astype(np.uint16) for _ in range(3))
+    a[: n // 2] &= 0xBFFF                      # half the products in a moderate range, where rounding ties occur
+    b[: n // 2] &= 0xBFFF
+    special = np.array([0, 0x8000, 0x0001, 0x8001, 0x03FF, 0x0400, 0x7BFF, 0xFBFF, 0x7C00, 0xFC00, 0x7E00, 0x3C00, 0xBC00], np.uint16)
+    sa, sb, sc = (g.ravel() for g in np.meshgrid(special, special, special, indexing="ij"))
+    a, b, c = np.concatenate([a, sa]), np.concatenate([b, sb]), np.concatenate([c, sc])
+    want, got = np.empty_like(a), np.empty_like(a)
+    L = ref.lib()
+    L.or_hfma_arr(a, b, c, a.size, want)
+    L.or_hfma_d_arr(a, b, c, a.size, got)
+    nan = lambda h: ((h & 0x7C00) == 0x7C00) & ((h & 0x3FF) != 0)
+    assert np.all((got == want) | (nan(got) & nan(want)))
