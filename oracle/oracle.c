@@ -223,6 +223,11 @@ void or_gemv(int q8, int pro, int epi, const float *X, const uint32_t *W, float 
       xs[k - k0] = v;
     }
     uint32_t g0 = k0 / G, g1 = (k1 + G - 1) / G;
+    /* tiles are independent (each writes its own Y rows and MX slot): spread over the host's threads, every tile's
+     * arithmetic unchanged */
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static) if (NT >= 16)
+#endif
     for (uint32_t tile = 0; tile < NT; tile++) {
       float tot[2][64];
       int npair = epi == EPI_GEGLU ? 2 : 1;
@@ -283,6 +288,9 @@ void or_gemvM(int q8, int pro, int epi, uint32_t M, const float *X, const uint32
       xs[(size_t)m * (K + 64) + (k - k0)] = v;
     }
     uint32_t g0 = k0 / G, g1 = (k1 + G - 1) / G;
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static) if (NT >= 16)
+#endif
     for (uint32_t tile = 0; tile < NT; tile++) {
       float tot[2][8][64];
       for (int ti = 0; ti < npair; ti++) {
