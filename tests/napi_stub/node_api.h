@@ -1,0 +1,42 @@
+/* The few Node-API declarations the INTEGRATION.md addon uses (types and signatures as Node-API documents them), so
+ * that tests/test_integration_addon.py can compile the addon's source against include/p0mm.h without Node. Test
+ * infrastructure only: nothing here is linked or run. */
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+typedef struct napi_env__ *napi_env;
+typedef struct napi_value__ *napi_value;
+typedef struct napi_callback_info__ *napi_callback_info;
+typedef enum { napi_ok } napi_status;
+typedef enum { napi_undefined, napi_null, napi_boolean, napi_number, napi_string, napi_symbol, napi_object, napi_function,
+               napi_external, napi_bigint } napi_valuetype;
+typedef enum { napi_default = 0 } napi_property_attributes;
+typedef napi_value (*napi_callback)(napi_env env, napi_callback_info info);
+typedef struct {
+  const char *utf8name;
+  napi_value name;
+  napi_callback method;
+  napi_callback getter;
+  napi_callback setter;
+  napi_value value;
+  napi_property_attributes attributes;
+  void *data;
+} napi_property_descriptor;
+
+extern "C" {
+napi_status napi_has_named_property(napi_env env, napi_value object, const char *utf8name, bool *result);
+napi_status napi_get_named_property(napi_env env, napi_value object, const char *utf8name, napi_value *result);
+napi_status napi_typeof(napi_env env, napi_value value, napi_valuetype *result);
+napi_status napi_get_value_uint32(napi_env env, napi_value value, uint32_t *result);
+napi_status napi_get_value_double(napi_env env, napi_value value, double *result);
+napi_status napi_get_value_bigint_uint64(napi_env env, napi_value value, uint64_t *result, bool *lossless);
+napi_status napi_get_value_string_utf8(napi_env env, napi_value value, char *buf, size_t bufsize, size_t *result);
+napi_status napi_throw_error(napi_env env, const char *code, const char *msg);
+napi_status napi_get_cb_info(napi_env env, napi_callback_info cbinfo, size_t *argc, napi_value *argv, napi_value *this_arg,
+                             void **data);
+napi_status napi_create_uint32(napi_env env, uint32_t value, napi_value *result);
+napi_status napi_define_properties(napi_env env, napi_value object, size_t property_count, const napi_property_descriptor *properties);
+}
+
+#define NAPI_MODULE_INIT() extern "C" napi_value p0mm_module_init(napi_env env, napi_value exports)
