@@ -30,12 +30,14 @@ napi_status napi_get_named_property(napi_env env, napi_value object, const char 
 napi_status napi_typeof(napi_env env, napi_value value, napi_valuetype *result);
 napi_status napi_get_value_uint32(napi_env env, napi_value value, uint32_t *result);
 napi_status napi_get_value_double(napi_env env, napi_value value, double *result);
+napi_status napi_get_value_bool(napi_env env, napi_value value, bool *result);
 napi_status napi_get_value_bigint_uint64(napi_env env, napi_value value, uint64_t *result, bool *lossless);
 napi_status napi_get_value_string_utf8(napi_env env, napi_value value, char *buf, size_t bufsize, size_t *result);
 napi_status napi_throw_error(napi_env env, const char *code, const char *msg);
 napi_status napi_get_cb_info(napi_env env, napi_callback_info cbinfo, size_t *argc, napi_value *argv, napi_value *this_arg,
                              void **data);
 napi_status napi_create_uint32(napi_env env, uint32_t value, napi_value *result);
+napi_status napi_create_double(napi_env env, double value, napi_value *result);
 napi_status napi_define_properties(napi_env env, napi_value object, size_t property_count, const napi_property_descriptor *properties);
 }
 
