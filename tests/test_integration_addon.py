@@ -29,3 +29,17 @@ def test_addon_compiles_against_header(tmp_path):
                         "-I", os.path.join(ROOT, "include"), "-I", os.path.join(ROOT, "tests", "napi_stub"), str(src)],
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stderr[-3000:]
+
+
+def test_tuning_variables_documented():
+    """Every environment variable the library reads (a tuning override or switch) has a row in INTEGRATION.md's table,
+    and the table names none that the library no longer reads."""
+    csrc = os.path.join(ROOT, "p0pc0rn_b200", "csrc")
+    read = set()
+    for f in os.listdir(csrc):
+        if f.endswith((".cu", ".cuh", ".h", ".cc")):
+            read |= set(re.findall(r'getenv\("(P0MM_\w+)"\)', open(os.path.join(csrc, f)).read()))
+    with open(os.path.join(ROOT, "INTEGRATION.md")) as f:
+        documented = set(re.findall(r"^\| `(P0MM_\w+)", f.read(), re.M))
+    assert read, "the library reads tuning variables"
+    assert read == documented, (sorted(read - documented), sorted(documented - read))
