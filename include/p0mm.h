@@ -42,10 +42,11 @@ enum { P0_ENC_Q4G32A_T64 = 1, P0_ENC_Q8G64S_T64 = 2, P0_ENC_F16 = 3 };
 /* ---------------------------------------------------------------------------------------------- device context */
 /* createGpu (engine/core/gpu.js:18-23): one context per device; owns a CUDA stream and every buffer */
 p0_status p0_init(int device, p0_ctx **out);
-/* Gpu.freeAll + device.destroy (gpu.js) */
+/* Gpu.freeAll (engine/core/gpu.js:95) + device.destroy: frees every buffer, the stream and the context */
 p0_status p0_destroy(p0_ctx *ctx);
 /* run subsequent work on an external cudaStream_t (NULL = the context's own stream; pass cudaStreamLegacy for CUDA's
- * legacy default stream, whose handle 0 would otherwise mean "own stream") */
+ * legacy default stream, whose handle 0 would otherwise mean "own stream"). No counterpart in the reference, whose
+ * device has one queue. */
 p0_status p0_set_stream(p0_ctx *ctx, void *cuda_stream);
 /* Consecutive GEMV calls on the context's stream always overlap their launch with the call ahead (programmatic
  * dependent launch: a call waits for the work ahead before it reads x or writes anything). With P0_OVERLAP_WEIGHTS set
@@ -55,7 +56,8 @@ p0_status p0_set_stream(p0_ctx *ctx, void *cuda_stream);
  * order. Default: 0. */
 enum { P0_OVERLAP_WEIGHTS = 1 };
 p0_status p0_set_overlap(p0_ctx *ctx, uint32_t flags);
-/* the message of the last failed call, in the reference's wording (e.g. "gemv: N % 64") */
+/* the message of the last failed call, in the reference's wording (e.g. "gemv: N % 64", the Error that
+ * engine/llm/lops.js:122 throws); the reference hands its messages over as thrown errors instead */
 p0_status p0_last_error(p0_ctx *ctx, char *msg, size_t cap);
 /* byte accounting (gpu.js:28, 81-96) and dispatch counter (Runner, gpu.js:177-179) */
 p0_status p0_stats(p0_ctx *ctx, uint64_t *alive_bytes, uint64_t *peak_bytes, uint64_t *dispatches);
@@ -63,7 +65,8 @@ p0_status p0_stats(p0_ctx *ctx, uint64_t *alive_bytes, uint64_t *peak_bytes, uin
 /* ---------------------------------------------------------------------------------------------- buffers */
 /* Gpu.buffer(bytes, label) (gpu.js:81-96): device allocation rounded up to 16 B, zero-filled, accounted */
 p0_status p0_buffer(p0_ctx *ctx, size_t bytes, const char *label, p0_buf *out);
-/* register caller-owned device memory (e.g. a torch tensor) as a buffer; p0_free() only unregisters it */
+/* register caller-owned device memory (e.g. a torch tensor) as a buffer; p0_free() only unregisters it. No
+ * counterpart in the reference (WebGPU buffers are always created by the device). */
 p0_status p0_wrap(p0_ctx *ctx, void *device_ptr, size_t bytes, const char *label, p0_buf *out);
 /* Gpu.upload / queue.writeBuffer (gpu.js:98-117): host -> device, ordered on the stream */
 p0_status p0_upload(p0_ctx *ctx, p0_buf buf, size_t dst_off, const void *src, size_t n);
@@ -79,7 +82,8 @@ p0_status p0_read(p0_ctx *ctx, p0_buf buf, size_t off, size_t n, void *dst);
 p0_status p0_free(p0_ctx *ctx, p0_buf buf);
 /* Gpu.done (gpu.js:141-147): wait for the stream with a bound; reports in-kernel wait timeouts */
 p0_status p0_done(p0_ctx *ctx, uint32_t timeout_ms);
-/* the device address of a buffer (for NCCL / interop); the address is valid until p0_free */
+/* the device address of a buffer (for NCCL / interop); the address is valid until p0_free. No counterpart in the
+ * reference (WebGPU hides buffer addresses). */
 p0_status p0_device_ptr(p0_ctx *ctx, p0_buf buf, uint64_t *out);
 
 /* a weight tensor view: WeightStore h.t(name) -> {buf, off (bytes), bytes, enc, rows, cols} (core/store.js:249-253) */
@@ -319,14 +323,15 @@ p0_status p0_pack_q8(p0_ctx *ctx, p0_buf w, uint64_t w_off, uint32_t ldw, uint32
 
 /* ---------------------------------------------------------------------------------------------- testing aids */
 /* writes the fp16 weight the GEMM tile holds for rows [0, rows) x k [0, cols) of a q4/q8 view, row-major,
- * into out_f16 (a buffer of rows*cols*2 bytes): the in-kernel dequantisation, dumped for bit-exact checks */
+ * into out_f16 (a buffer of rows*cols*2 bytes): the in-kernel dequantisation (gemm.js:139-160), dumped for bit-exact
+ * checks; no entry point of its own in the reference */
 p0_status p0_dequant_f16(p0_ctx *ctx, const p0_wview *w, p0_buf out_f16);
 /* failure-path check, no counterpart in the reference: enqueues one small kernel whose warp waits on an mbarrier
  * phase that nothing completes, through the same bounded in-kernel wait as the matmul kernels, giving up after `polls`
  * tries (1 .. 2^20). It records its code (0x7e1) in the context's error word and returns, so the next p0_done reports
  * P0_ETIMEOUT (the reference's GpuError at done(), core/gpu.js:141-147) and the context stays usable. */
 p0_status p0_wait_selftest(p0_ctx *ctx, uint32_t polls);
-/* the library build tag (kernel versions), e.g. "p0mm sm_100a gemv-v1 gemm-tc-v1" */
+/* the library build tag (kernel versions), e.g. "p0mm sm_100a gemv-v1 gemm-tc-v1"; no counterpart in the reference */
 const char *p0_version(void);
 
 #ifdef __cplusplus
