@@ -317,7 +317,7 @@ p0_status p0_attn_dec(p0_ctx *ctx, const p0_attn_dec_args *a);
  * (N*K*5/8 bytes) at out_off. N % 64 == 0, K % 32 == 0. The dequantised value of code q is q*s + mn. */
 p0_status p0_pack_q4(p0_ctx *ctx, p0_buf w, uint64_t w_off, uint32_t ldw, uint32_t N, uint32_t K, p0_buf out, uint64_t out_off);
 
-/* packQ8 (engine/kcheck.js:40-53) on the device, bit for bit: W f32 [N][ldw] -> q8g64s.t64 records (N*K*66/64 bytes:
+/* packQ8 (engine/kcheck.js:39-52) on the device, bit for bit: W f32 [N][ldw] -> q8g64s.t64 records (N*K*66/64 bytes:
  * 64 rows x 64 int8 codes + 64 fp16 scales per record). N % 64 == 0, K % 64 == 0. The dequantised value is q*s. */
 p0_status p0_pack_q8(p0_ctx *ctx, p0_buf w, uint64_t w_off, uint32_t ldw, uint32_t N, uint32_t K, p0_buf out, uint64_t out_off);
 

@@ -1,5 +1,5 @@
 // pack.cu -- the quantisers on the device, bit for bit: packQ4 (q4g32a.t64, engine/kcheck.js:22-38) and packQ8
-// (q8g64s.t64, engine/kcheck.js:40-53).
+// (q8g64s.t64, engine/kcheck.js:39-52).
 // One thread per (row, 32-k group): mn = f16(min), s = f16((max - mn) / 15) (s == 0 -> 1), q = clamp(rhe((w - mn) / s),
 // 0, 15), bytes r*16 + j = q[2j] | q[2j+1] << 4, word 1024 + 4r = f16(s) | f16(mn) << 16. The reference computes in
 // f64 and converts f64 -> f32 -> f16 with round-to-nearest-even (core/gpu.js:274-289); so does this kernel.
@@ -41,7 +41,7 @@ __global__ void pack_q4_kernel(const float *__restrict__ W, uint64_t ldw, uint32
   *reinterpret_cast<uint32_t *>(rec + 1024 + r * 4) = f2h(s) | (f2h(mn) << 16);
 }
 
-// packQ8 (kcheck.js:40-53), one thread per (row, 64-k group): s = f16(max|w| / 127) (s == 0 -> 1), q = clamp(rhe(w / s),
+// packQ8 (kcheck.js:39-52), one thread per (row, 64-k group): s = f16(max|w| / 127) (s == 0 -> 1), q = clamp(rhe(w / s),
 // -128, 127); bytes r*64 + i = q & 255 of record (t, g) (4224 B), u16 at 4096 + 2r = f16(s).
 __global__ void pack_q8_kernel(const float *__restrict__ W, uint64_t ldw, uint32_t N, uint32_t K, uint8_t *__restrict__ out) {
   const uint32_t G = K / 64;

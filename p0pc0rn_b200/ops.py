@@ -130,7 +130,7 @@ def pack_q4(g, w_f32, N, K, out=None, w_off=0, ldw=0, out_off=0):
 
 
 def pack_q8(g, w_f32, N, K, out=None, w_off=0, ldw=0, out_off=0):
-    """packQ8 (engine/kcheck.js:40-53) on the device: a W f32 [N][K] buffer -> q8g64s.t64 records; returns the out buffer"""
+    """packQ8 (engine/kcheck.js:39-52) on the device: a W f32 [N][K] buffer -> q8g64s.t64 records; returns the out buffer"""
     if out is None:
         out = g.buffer(N * K // 64 * 66, "q8")
     g._check(g._lib.p0_pack_q8(g.ctx, handle(w_f32), int(w_off), int(ldw), int(N), int(K), handle(out), int(out_off)))

@@ -1,6 +1,6 @@
 """A second, independent transcription of the reference's JS helpers in plain Python (no C), used to pin the C oracle:
 rng / randn (engine/kcheck.js:10-11), f2h / h2f (engine/core/gpu.js:274-295), rhe (kcheck.js:14), packQ4
-(kcheck.js:22-38), packQ8 (kcheck.js:40-53). JS numbers are f64; Float32Array stores round to f32 (struct pack 'f'); `>>` is JS's signed shift
+(kcheck.js:22-38), packQ8 (kcheck.js:39-52). JS numbers are f64; Float32Array stores round to f32 (struct pack 'f'); `>>` is JS's signed shift
 of the int32 view. Slow: small sizes only.
 """
 import math

@@ -1,4 +1,4 @@
-"""q8g64s.t64 on the GPU: the device packQ8 bit for bit against the oracle (engine/kcheck.js:40-53 restated); the
+"""q8g64s.t64 on the GPU: the device packQ8 bit for bit against the oracle (engine/kcheck.js:39-52 restated); the
 GEMV / gemvM over q8 weights (the lgemv / lgemvM q8 arithmetic of lops.js:72-81, lops_spec.js restated) within the
 parity tolerance, for the forms the reference's 8-bit layers use (raw and rms prologues, store / softcap / geglu
 epilogues, k-splits, M up to 8); and the GEMM over q8 weights (gemm.js:150-160): its dequantised weights bit for bit,

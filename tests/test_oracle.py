@@ -414,7 +414,7 @@ def test_attn_dec_oracle(D, nh, nkv, k0, k1, ring):
         assert np.max(np.abs(O[h * D:(h + 1) * D] - (p / p.sum()) @ V[g, rows])) <= 1e-5
 
 
-# ---------------------------------------------------------------- q8g64s.t64 (kcheck.js:40-53) in the oracle
+# ---------------------------------------------------------------- q8g64s.t64 (kcheck.js:39-52) in the oracle
 def test_pack_q8_matches_transcription():
     N, K = 64, 128
     W = ref.randn(N * K, 80, 0.05)
