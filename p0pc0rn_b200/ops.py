@@ -109,7 +109,7 @@ def gemm(gpu, a):
     args.h_Ltot, args.h_Hq, args.h_Hkv, args.h_rowOff = (int(h.get(k) or 0) for k in ("Ltot", "Hq", "Hkv", "rowOff"))
     args.h_eps = float(h.get("eps") or 0.0)
     args.h_rope_mode = L.P0_ROPE_HALF if h.get("ropeMode") == "half" else L.P0_ROPE_INTER
-    args.rope, args.gt = _b(h.get("rope")), _b(a.get("gt"))   # bound from the buffer start, as gemm.js:302-303 binds them
+    args.rope, args.gt = _b(h.get("rope")), _b(a.get("gt"))   # bound from the buffer start, as gemm.js:304 binds them
     fl = ctypes.c_double()
     gpu._check(gpu._lib.p0_gemm(gpu.ctx, ctypes.byref(args), ctypes.byref(fl)))
     return fl.value
