@@ -63,15 +63,20 @@ p0_status p0_init(int device, p0_ctx **out) {
   p0_ctx *c = new p0_ctx();
   c->device = device;
   p0_status st;
-  if ((st = p0_cuda(c, cudaSetDevice(device), "p0_init")) != P0_OK) { delete c; return st; }
-  cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
-  if ((st = p0_cuda(c, cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking), "p0_init stream")) != P0_OK) { delete c; return st; }
+  // a failed step releases what the earlier steps made (p0_destroy takes a partly built context)
+  if ((st = p0_cuda(c, cudaSetDevice(device), "p0_init")) != P0_OK) { p0_destroy(c); return st; }
+  if ((st = p0_cuda(c, cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device), "p0_init SM count")) != P0_OK ||
+      c->sm_count <= 0) {
+    p0_destroy(c);
+    return st != P0_OK ? st : P0_EDEVICE;
+  }
+  if ((st = p0_cuda(c, cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking), "p0_init stream")) != P0_OK) { p0_destroy(c); return st; }
   c->stream = c->own_stream;
-  if ((st = p0_cuda(c, cudaMalloc(&c->d_err, 16), "p0_init error word")) != P0_OK) { delete c; return st; }
-  cudaMemset(c->d_err, 0, 16);
-  if ((st = p0_cuda(c, cudaMallocHost(&c->h_err, 16), "p0_init pinned word")) != P0_OK) { delete c; return st; }
+  if ((st = p0_cuda(c, cudaMalloc(&c->d_err, 16), "p0_init error word")) != P0_OK) { p0_destroy(c); return st; }
+  if ((st = p0_cuda(c, cudaMemset(c->d_err, 0, 16), "p0_init error word")) != P0_OK) { p0_destroy(c); return st; }
+  if ((st = p0_cuda(c, cudaMallocHost(&c->h_err, 16), "p0_init pinned word")) != P0_OK) { p0_destroy(c); return st; }
   memset(c->h_err, 0, 16);
-  cudaDeviceSynchronize();
+  if ((st = p0_cuda(c, cudaDeviceSynchronize(), "p0_init")) != P0_OK) { p0_destroy(c); return st; }
   *out = c;
   return P0_OK;
 }
