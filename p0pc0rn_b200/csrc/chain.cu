@@ -579,6 +579,9 @@ p0_status p0_chain_end(p0_ctx *c, p0_chain **out) {
     }
     // state zeroed once here and before every launch
     e = cudaMemset(base + desc_bytes, 0, state_bytes);
+    // those copies and the memset run on the legacy stream and may still be in flight when the calls return; the
+    // context's stream (non-blocking) does not wait for it, so finish them before a run can be enqueued
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamLegacy);
     if (e != cudaSuccess) { p0_status st = p0_cuda(c, e, "chain"); cudaFree(ch->d_mem); delete ch; return st; }
     for (auto &pc : ch->pieces) pc.state_off += desc_bytes;
   }

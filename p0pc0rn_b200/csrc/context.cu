@@ -159,6 +159,9 @@ p0_status p0_wrap(p0_ctx *c, void *ptr, size_t bytes, const char *label, p0_buf 
     cudaGetLastError();
     return p0_fail(c, P0_EINVAL, "wrap: %s is not device memory", label ? label : "");
   }
+  // the kernels read and write a context's buffers as this device's own memory
+  if (at.device != c->device)
+    return p0_fail(c, P0_EINVAL, "wrap: %s is memory of device %d, the context's device is %d", label ? label : "", at.device, c->device);
   P0Buffer b;
   b.ptr = ptr; b.bytes = bytes; b.owned = false; b.label = label ? label : "";
   out->id = c->next_id++;
@@ -224,9 +227,11 @@ p0_status p0_done(p0_ctx *c, uint32_t timeout_ms) {
   if (st) return st;
   if (c->h_err[0]) {
     uint32_t code = c->h_err[0];
-    cudaMemset(c->d_err, 0, 4);
+    // the resets go on the context's stream, so the next call's kernels run after them (a plain cudaMemset would run
+    // on the legacy stream, which the context's non-blocking stream does not wait for)
+    if ((st = p0_cuda(c, cudaMemsetAsync(c->d_err, 0, 4, c->stream), "done error word"))) return st;
     // a kernel that gave up may have left workspace counters mid-count: start the next call from zero
-    if (c->ws) cudaMemset(c->ws, 0, c->ws_bytes);
+    if (c->ws && (st = p0_cuda(c, cudaMemsetAsync(c->ws, 0, c->ws_bytes, c->stream), "done workspace"))) return st;
     return p0_fail(c, P0_ETIMEOUT, "done: a kernel gave up a bounded wait (code 0x%x)", code);
   }
   return P0_OK;
