@@ -10,6 +10,9 @@
  * Units follow the reference: weight / x / y byte offsets where the reference uses bytes (ops/gemm.js:300-302),
  * f32-element offsets where it uses elements (llm/lops.js:127-128: x.rowB, norm.off, stat.off, ev.off).
  * All work is enqueued on the context's stream and is asynchronous; p0_read() and p0_done() synchronise.
+ * A context is used by one thread at a time (as the reference's Gpu object lives on JavaScript's one thread): calls
+ * on the same context from several threads at once must be serialised by the caller. Separate contexts, one per
+ * thread, may be used concurrently.
  */
 #ifndef P0MM_H
 #define P0MM_H
